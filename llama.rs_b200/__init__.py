@@ -1,0 +1,599 @@
+"""B200 (sm_100a) CUDA backend for llama.rs's Qwen2 token loop -- Python host module.
+
+This module binds ``libllamars.so`` (the C ABI declared in ``include/llamars.h``
+and ``include/llamars_synth.h``) with ctypes and mirrors the reference
+engine's interfaces for the hot path:
+
+* ``QuantType`` / ``QuantTensor``      -- src/quant.rs:10-324
+* ``CudaBackend`` (``KernelBackend``)  -- src/backend.rs:67-73 (name, threads, matvec)
+* ``CudaQwen2Model`` (``CausalModel``) -- src/architecture.rs:42-78 (forward_token, prefill)
+  plus the greedy loop of ``InferenceEngine::benchmark_tokens`` (src/engine.rs:189-241)
+* ``synth_model``                      -- the load path (src/loader.rs:83-227 + maybe_quantize
+  :406-447) for seeded synthetic checkpoints.
+
+Errors surface as ``LrsError`` carrying the library's message, the way the
+reference surfaces ``anyhow`` errors.  There is no CPU fallback: if the CUDA
+library is missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libllamars.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build the CUDA backend first (make -C llama.rs_b200, "
+        "or __graft_entry__.build())")
+_lib = C.CDLL(LIB_PATH)
+
+
+class LrsError(RuntimeError):
+    """A failed call into the CUDA backend (the reference's anyhow::Error)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+# ------------------------------------------------------------------ types --
+class QuantType(enum.IntEnum):
+    """QuantType with its GGML ids (src/quant.rs:10-44)."""
+
+    F32 = 0
+    F16 = 1
+    Q4_0 = 2
+    Q4_1 = 3
+    Q5_0 = 6
+    Q5_1 = 7
+    Q8_0 = 8
+    Q4_K = 12
+    Q5_K = 13
+    Q6_K = 14
+    BF16 = 30
+
+    @classmethod
+    def from_ggml_type(cls, value: int) -> "QuantType":
+        try:
+            return cls(value)
+        except ValueError:
+            raise LrsError(2, f"unsupported GGML tensor type {value}; supported: F32, F16, BF16, "
+                              "Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K") from None
+
+    def block_size(self) -> int:
+        return _GEOM[self][0]
+
+    def type_size(self) -> int:
+        return _GEOM[self][1]
+
+    def display_name(self) -> str:
+        return "Q4_K" if self is QuantType.Q4_K else (
+            "Q5_K" if self is QuantType.Q5_K else ("Q6_K" if self is QuantType.Q6_K else self.name))
+
+
+_GEOM = {
+    QuantType.F32: (1, 4), QuantType.F16: (1, 2), QuantType.BF16: (1, 2),
+    QuantType.Q4_0: (32, 18), QuantType.Q4_1: (32, 20), QuantType.Q5_0: (32, 22),
+    QuantType.Q5_1: (32, 24), QuantType.Q8_0: (32, 34), QuantType.Q4_K: (256, 144),
+    QuantType.Q5_K: (256, 176), QuantType.Q6_K: (256, 210),
+}
+
+
+class LoadQuantization(enum.IntEnum):
+    """LoadQuantization (src/loader.rs:16-25)."""
+
+    NONE = 0
+    Q4K = 1
+    Q4KM = 2
+
+
+class LogitsMode(enum.IntEnum):
+    """LogitsMode (src/architecture.rs:34-38)."""
+
+    SKIP = 0
+    COMPUTE = 1
+
+
+# ------------------------------------------------------------ C structs --
+class _Config(C.Structure):
+    _fields_ = [("hidden_size", C.c_uint32), ("intermediate_size", C.c_uint32),
+                ("num_attention_heads", C.c_uint32), ("num_key_value_heads", C.c_uint32),
+                ("num_hidden_layers", C.c_uint32), ("vocab_size", C.c_uint32),
+                ("head_dim", C.c_uint32), ("max_position_embeddings", C.c_uint32),
+                ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float)]
+
+
+class _TensorDesc(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("nbytes", C.c_uint64), ("rows", C.c_uint64),
+                ("cols", C.c_uint64), ("ggml_type", C.c_uint32), ("reserved", C.c_uint32)]
+
+
+class _LayerDesc(C.Structure):
+    _fields_ = [("input_layernorm", C.c_void_p), ("post_attention_layernorm", C.c_void_p),
+                ("q_proj", _TensorDesc), ("k_proj", _TensorDesc), ("v_proj", _TensorDesc),
+                ("o_proj", _TensorDesc), ("gate_proj", _TensorDesc), ("up_proj", _TensorDesc),
+                ("down_proj", _TensorDesc), ("q_bias", C.c_void_p), ("k_bias", C.c_void_p),
+                ("v_bias", C.c_void_p)]
+
+
+class _ModelDesc(C.Structure):
+    _fields_ = [("config", _Config), ("embed_tokens", _TensorDesc), ("lm_head", _TensorDesc),
+                ("final_norm", C.c_void_p), ("layers", C.POINTER(_LayerDesc))]
+
+
+class _ModelOptions(C.Structure):
+    _fields_ = [("max_seq_len", C.c_uint32), ("max_sequences", C.c_uint32),
+                ("kv_dtype", C.c_uint32), ("use_graph", C.c_uint32)]
+
+
+class _SynthSpec(C.Structure):
+    _fields_ = [("config", _Config), ("seed", C.c_uint64), ("recipe", C.c_uint32),
+                ("tie_word_embeddings", C.c_uint32), ("init_std", C.c_float),
+                ("threads", C.c_uint32)]
+
+
+_P = C.c_void_p
+_F = C.POINTER(C.c_float)
+_U32 = C.POINTER(C.c_uint32)
+
+
+def _sig(name, res, *args):
+    fn = getattr(_lib, name)
+    fn.restype = res
+    fn.argtypes = list(args)
+    return fn
+
+
+_lib_last_error = _sig("lrs_last_error", C.c_char_p)
+_sig("lrs_type_geometry", C.c_int32, C.c_uint32, _U32, _U32)
+_sig("lrs_backend_create", C.c_int32, C.c_int, C.POINTER(_P))
+_sig("lrs_backend_destroy", None, _P)
+_sig("lrs_backend_name", C.c_char_p, _P)
+_sig("lrs_backend_threads", C.c_size_t, _P)
+_sig("lrs_backend_synchronize", C.c_int32, _P)
+_sig("lrs_backend_stream", _P, _P)
+_sig("lrs_tensor_upload", C.c_int32, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_uint32,
+     C.POINTER(_P))
+_sig("lrs_tensor_free", None, _P)
+_sig("lrs_tensor_device_ptr", _P, _P)
+_sig("lrs_dequantize_rows", C.c_int32, _P, _P, C.c_size_t, C.c_size_t, _F)
+_sig("lrs_matvec", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
+_sig("lrs_matvec_batched", C.c_int32, _P, _P, _F, C.c_size_t, C.c_size_t, _F, C.c_size_t)
+_sig("lrs_matvec_device", C.c_int32, _P, _P, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+_sig("lrs_model_create", C.c_int32, _P, C.POINTER(_ModelDesc), C.POINTER(_ModelOptions),
+     C.POINTER(_P))
+_sig("lrs_model_destroy", None, _P)
+_sig("lrs_model_reset", C.c_int32, _P, C.c_uint32)
+_sig("lrs_model_forward_token", C.c_int32, _P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, _F,
+     _U32)
+_sig("lrs_model_prefill", C.c_int32, _P, C.c_uint32, _U32, C.c_size_t, C.c_uint32, _F, _U32)
+_sig("lrs_model_decode_greedy", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c_size_t, _U32)
+_sig("lrs_model_decode_enqueue", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c_size_t)
+_sig("lrs_model_read_tokens", C.c_int32, _P, C.c_size_t, C.c_size_t, _U32)
+_sig("lrs_model_weight_bytes", C.c_uint64, _P)
+_sig("lrs_recipe_type", C.c_uint32, C.c_uint32, C.c_char_p, C.c_size_t, C.c_size_t)
+_sig("lrs_quantize_matrix", C.c_int32, C.c_uint32, _F, C.c_size_t, C.c_size_t, _P, C.c_size_t,
+     _U32, C.POINTER(C.c_size_t))
+_sig("lrs_quantized_size", C.c_size_t, C.c_uint32, C.c_size_t, C.c_size_t)
+_sig("lrs_synth_fill", None, C.c_uint64, C.c_char_p, C.c_float, C.c_uint64, C.c_size_t, _F)
+_sig("lrs_synth_model_create", C.c_int32, C.POINTER(_SynthSpec), C.POINTER(_P))
+_sig("lrs_synth_model_desc", C.POINTER(_ModelDesc), _P)
+_sig("lrs_synth_model_destroy", None, _P)
+
+#: every symbol include/*.h declares (checked by the CPU tests)
+EXPORTED_SYMBOLS = (
+    "lrs_last_error", "lrs_type_geometry", "lrs_backend_create", "lrs_backend_destroy",
+    "lrs_backend_name", "lrs_backend_threads", "lrs_backend_synchronize", "lrs_backend_stream",
+    "lrs_tensor_upload", "lrs_tensor_free", "lrs_tensor_device_ptr", "lrs_dequantize_rows",
+    "lrs_matvec", "lrs_matvec_batched", "lrs_matvec_device", "lrs_model_create",
+    "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
+    "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
+    "lrs_model_weight_bytes", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
+    "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
+)
+
+
+def _check(code: int) -> None:
+    if code != 0:
+        raise LrsError(code, (_lib.lrs_last_error() or b"").decode())
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(_F)
+
+
+def _uptr(a: np.ndarray):
+    return a.ctypes.data_as(_U32)
+
+
+def library():
+    """The loaded ctypes handle of libllamars.so."""
+    return _lib
+
+
+# ----------------------------------------------------------- QuantTensor --
+class QuantTensor:
+    """Row-major [rows, cols] GGML tensor (QuantTensor, src/quant.rs:105-324).
+
+    ``data`` is a contiguous uint8 numpy array of exactly
+    rows * cols / block_size * type_size bytes.
+    """
+
+    def __init__(self, data, shape: Sequence[int], quant_type: QuantType):
+        quant_type = QuantType(quant_type)
+        shape = tuple(int(s) for s in shape)
+        if not (1 <= len(shape) <= 2):
+            raise LrsError(1, "only 1D and 2D tensors are supported")
+        cols = shape[-1]
+        if cols % quant_type.block_size():
+            raise LrsError(1, f"last dimension {cols} is not divisible by "
+                              f"{quant_type.block_size()} for {quant_type.display_name()}")
+        elems = int(np.prod(shape))
+        expected = elems // quant_type.block_size() * quant_type.type_size()
+        buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8) if isinstance(
+            data, (bytes, bytearray, memoryview)) else data, dtype=np.uint8).reshape(-1)
+        if buf.size != expected:
+            raise LrsError(1, f"bad {quant_type.display_name()} tensor byte length: got "
+                              f"{buf.size}, expected {expected}")
+        self.data = buf
+        self.shape = shape
+        self.quant_type = quant_type
+
+    def rows(self) -> int:
+        return 1 if len(self.shape) == 1 else self.shape[0]
+
+    def cols(self) -> int:
+        return self.shape[-1]
+
+    def row_bytes(self) -> int:
+        return self.cols() // self.quant_type.block_size() * self.quant_type.type_size()
+
+    def row_data(self, row: int) -> np.ndarray:
+        rb = self.row_bytes()
+        return self.data[row * rb:(row + 1) * rb]
+
+    @classmethod
+    def from_f32(cls, values: np.ndarray, shape: Sequence[int]) -> "QuantTensor":
+        v = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+        return cls(v.view(np.uint8), shape, QuantType.F32)
+
+    @classmethod
+    def quantize(cls, values: np.ndarray, rows: int, cols: int, quant_type: QuantType) -> "QuantTensor":
+        """Encodes F32 values as ``quant_type`` (QuantTensor::quantize_*, src/quant.rs:187-259,
+        with the reference fallbacks; see lrs_quantize_matrix)."""
+        v = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+        if v.size != rows * cols:
+            raise LrsError(1, "quantization shape/data mismatch")
+        size = _lib.lrs_quantized_size(int(quant_type), rows, cols)
+        out = np.zeros(size, dtype=np.uint8)
+        t = C.c_uint32()
+        n = C.c_size_t()
+        _check(_lib.lrs_quantize_matrix(int(quant_type), _fptr(v), rows, cols,
+                                        out.ctypes.data_as(_P), size, C.byref(t), C.byref(n)))
+        return cls(out, (rows, cols), QuantType(t.value))
+
+    @classmethod
+    def quantize_q4k(cls, values, rows, cols):
+        return cls.quantize(values, rows, cols, QuantType.Q4_K)
+
+    @classmethod
+    def quantize_q5_0(cls, values, rows, cols):
+        return cls.quantize(values, rows, cols, QuantType.Q5_0)
+
+    @classmethod
+    def quantize_q8_0(cls, values, rows, cols):
+        return cls.quantize(values, rows, cols, QuantType.Q8_0)
+
+    @classmethod
+    def quantize_q6k(cls, values, rows, cols):
+        return cls.quantize(values, rows, cols, QuantType.Q6_K)
+
+    def desc(self) -> _TensorDesc:
+        return _TensorDesc(self.data.ctypes.data, self.data.size, self.rows(), self.cols(),
+                           int(self.quant_type), 0)
+
+
+def recipe_type(recipe: LoadQuantization, name: str, rows: int, cols: int) -> QuantType:
+    """Type maybe_quantize (src/loader.rs:406-447) assigns to an F32 tensor."""
+    return QuantType(_lib.lrs_recipe_type(int(recipe), name.encode(), rows, cols))
+
+
+def synth_values(seed: int, name: str, n: int, offset: int = 0, std: float = 0.02) -> np.ndarray:
+    """The N(0, std) values of tensor ``name`` in the seeded synthetic models."""
+    out = np.empty(n, dtype=np.float32)
+    _lib.lrs_synth_fill(seed, name.encode(), std, offset, n, _fptr(out))
+    return out
+
+
+# ------------------------------------------------------------ backend ----
+class CudaBackend:
+    """KernelBackend over one CUDA device (src/backend.rs:67-73).
+
+    Tensors are uploaded to HBM once, in their native block layout, and cached
+    by the address of their host bytes -- the lookup a Rust ``CudaBackend``
+    shim does for ``matvec(&QuantTensor, ..)``.
+    """
+
+    def __init__(self, device: int = 0):
+        h = _P()
+        _check(_lib.lrs_backend_create(device, C.byref(h)))
+        self._h = h
+        self.device = device
+        self._cache = {}
+
+    def close(self):
+        for _, (t, _keep) in list(self._cache.items()):
+            _lib.lrs_tensor_free(t)
+        self._cache.clear()
+        if self._h:
+            _lib.lrs_backend_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def name(self) -> str:
+        return _lib.lrs_backend_name(self._h).decode()
+
+    def threads(self) -> int:
+        return int(_lib.lrs_backend_threads(self._h))
+
+    def stream(self) -> int:
+        return _lib.lrs_backend_stream(self._h)
+
+    def synchronize(self) -> None:
+        _check(_lib.lrs_backend_synchronize(self._h))
+
+    def upload(self, weight: QuantTensor):
+        key = (weight.data.ctypes.data, weight.data.size, int(weight.quant_type))
+        hit = self._cache.get(key)
+        if hit is not None:
+            return hit[0]
+        t = _P()
+        _check(_lib.lrs_tensor_upload(self._h, weight.data.ctypes.data_as(_P), weight.data.size,
+                                      weight.rows(), weight.cols(), int(weight.quant_type),
+                                      C.byref(t)))
+        self._cache[key] = (t, weight.data)
+        return t
+
+    def release(self, weight: QuantTensor) -> None:
+        key = (weight.data.ctypes.data, weight.data.size, int(weight.quant_type))
+        hit = self._cache.pop(key, None)
+        if hit is not None:
+            _lib.lrs_tensor_free(hit[0])
+
+    def matvec(self, weight: QuantTensor, input: np.ndarray, output: np.ndarray) -> None:
+        """output[r] = dot(row r, input)  (KernelBackend::matvec)."""
+        t = self.upload(weight)
+        _check(_lib.lrs_matvec(self._h, t, _fptr(input), input.size, _fptr(output), output.size))
+
+    def matvec_batched(self, weight: QuantTensor, inputs: np.ndarray) -> np.ndarray:
+        """[B, cols] -> [B, rows]; equals B independent matvec calls."""
+        x = np.ascontiguousarray(inputs, dtype=np.float32)
+        b = x.shape[0]
+        out = np.empty((b, weight.rows()), dtype=np.float32)
+        t = self.upload(weight)
+        _check(_lib.lrs_matvec_batched(self._h, t, _fptr(x), b, x.shape[1], _fptr(out),
+                                       weight.rows()))
+        return out
+
+    def matvec_device(self, weight: QuantTensor, d_in: int, batch: int, d_out: int,
+                      stream: Optional[int] = None) -> None:
+        """Queues a batched matvec on device pointers (no synchronization)."""
+        t = self.upload(weight)
+        _check(_lib.lrs_matvec_device(self._h, t, d_in, batch, d_out, stream))
+
+    def dequantize_rows(self, weight: QuantTensor, row0: int, nrows: int) -> np.ndarray:
+        """value_at for rows [row0, row0 + nrows) (QuantTensor::row_into)."""
+        out = np.empty((nrows, weight.cols()), dtype=np.float32)
+        t = self.upload(weight)
+        _check(_lib.lrs_dequantize_rows(self._h, t, row0, nrows, _fptr(out)))
+        return out
+
+
+# --------------------------------------------------------------- model ---
+@dataclass
+class LlamaConfig:
+    """LlamaConfig (src/config.rs:18-39) with head_dim resolved."""
+
+    hidden_size: int
+    intermediate_size: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    num_hidden_layers: int
+    vocab_size: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    max_position_embeddings: int = 32768
+    head_dim: Optional[int] = None
+    tie_word_embeddings: bool = False
+
+    def resolved_head_dim(self) -> int:
+        return self.head_dim or self.hidden_size // self.num_attention_heads
+
+    def kv_width(self) -> int:
+        return self.num_key_value_heads * self.resolved_head_dim()
+
+    def to_c(self) -> _Config:
+        return _Config(self.hidden_size, self.intermediate_size, self.num_attention_heads,
+                       self.num_key_value_heads, self.num_hidden_layers, self.vocab_size,
+                       self.resolved_head_dim(), self.max_position_embeddings,
+                       self.rms_norm_eps, self.rope_theta)
+
+
+class SynthModel:
+    """A seeded synthetic Qwen2 checkpoint, quantized at load time like the reference."""
+
+    def __init__(self, config: LlamaConfig, seed: int, recipe: LoadQuantization,
+                 init_std: float = 0.02, threads: int = 0):
+        spec = _SynthSpec(config.to_c(), seed, int(recipe), 1 if config.tie_word_embeddings else 0,
+                          init_std, threads)
+        h = _P()
+        _check(_lib.lrs_synth_model_create(C.byref(spec), C.byref(h)))
+        self._h = h
+        self.config = config
+        self.seed = seed
+        self.recipe = recipe
+
+    def close(self):
+        if self._h:
+            _lib.lrs_synth_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def desc(self):
+        """Pointer to the lrs_model_desc (host views stay valid while this object lives)."""
+        return _lib.lrs_synth_model_desc(self._h)
+
+    def tensor(self, which: str, layer: Optional[int] = None) -> QuantTensor:
+        """A weight as a QuantTensor view: 'embed', 'lm_head' or a layer projection name."""
+        d = self.desc().contents
+        if layer is None:
+            td = getattr(d, "embed_tokens" if which == "embed" else which)
+        else:
+            td = getattr(d.layers[layer], which)
+        buf = (C.c_uint8 * td.nbytes).from_address(td.data)
+        return QuantTensor(np.frombuffer(buf, dtype=np.uint8), (td.rows, td.cols),
+                           QuantType(td.ggml_type))
+
+
+class CudaQwen2Model:
+    """CausalModel on the CUDA backend (src/architecture.rs:42-78).
+
+    Owns the device weights, a paged KV cache with ``max_sequences`` slots and
+    the activation buffers.  ``forward_token`` / ``prefill`` follow the trait;
+    ``decode_greedy`` is the decode half of benchmark_tokens with the argmax on
+    the device and each step replayed as one CUDA graph.
+    """
+
+    def __init__(self, backend: CudaBackend, desc, max_seq_len: int = 4096,
+                 max_sequences: int = 1, kv_bf16: bool = False, use_graph: bool = True,
+                 keepalive=None):
+        opts = _ModelOptions(max_seq_len, max_sequences, 1 if kv_bf16 else 0,
+                             1 if use_graph else 0)
+        h = _P()
+        _check(_lib.lrs_model_create(backend.handle, desc, C.byref(opts), C.byref(h)))
+        self._h = h
+        self.backend = backend
+        self.keepalive = keepalive
+        cfg = desc.contents.config
+        self.vocab_size = cfg.vocab_size
+        self.max_seq_len = max_seq_len
+        self.max_sequences = max_sequences
+
+    def close(self):
+        if self._h:
+            _lib.lrs_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight_bytes(self) -> int:
+        return int(_lib.lrs_model_weight_bytes(self._h))
+
+    def reset(self, seq: int = 0) -> None:
+        _check(_lib.lrs_model_reset(self._h, seq))
+
+    def forward_token(self, token_id: int, pos: int, logits: LogitsMode = LogitsMode.COMPUTE,
+                      seq: int = 0):
+        """Returns (logits, argmax) for LogitsMode.COMPUTE, else None."""
+        if logits == LogitsMode.COMPUTE:
+            out = np.empty(self.vocab_size, dtype=np.float32)
+            am = np.zeros(1, dtype=np.uint32)
+            _check(_lib.lrs_model_forward_token(self._h, seq, token_id, pos, 1, _fptr(out),
+                                                _uptr(am)))
+            return out, int(am[0])
+        _check(_lib.lrs_model_forward_token(self._h, seq, token_id, pos, 0, None, None))
+        return None
+
+    def prefill(self, tokens: Sequence[int], start_pos: int = 0, seq: int = 0,
+                want_logits: bool = True):
+        """Prompt pass; returns (last logits, argmax) like the reference's prefill."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.vocab_size, dtype=np.float32) if want_logits else None
+        am = np.zeros(1, dtype=np.uint32)
+        _check(_lib.lrs_model_prefill(self._h, seq, _uptr(t), t.size, start_pos,
+                                      _fptr(out) if out is not None else None, _uptr(am)))
+        return out, int(am[0])
+
+    def decode_greedy(self, first_tokens: Sequence[int], start_pos: Sequence[int], n_steps: int,
+                      seqs: Optional[Sequence[int]] = None) -> np.ndarray:
+        """[n_steps, n_seqs] tokens fed to each greedy step (row 0 = first_tokens)."""
+        ft = np.ascontiguousarray(first_tokens, dtype=np.uint32)
+        n = ft.size
+        sp = np.ascontiguousarray(start_pos, dtype=np.uint32)
+        sq = np.ascontiguousarray(seqs if seqs is not None else range(n), dtype=np.uint32)
+        out = np.zeros((n_steps, n), dtype=np.uint32)
+        _check(_lib.lrs_model_decode_greedy(self._h, n, _uptr(sq), _uptr(ft), _uptr(sp), n_steps,
+                                            _uptr(out)))
+        return out
+
+    def decode_enqueue(self, first_tokens, start_pos, n_steps: int, seqs=None) -> None:
+        ft = np.ascontiguousarray(first_tokens, dtype=np.uint32)
+        sp = np.ascontiguousarray(start_pos, dtype=np.uint32)
+        sq = np.ascontiguousarray(seqs if seqs is not None else range(ft.size), dtype=np.uint32)
+        self._enq_keep = (ft, sp, sq)
+        _check(_lib.lrs_model_decode_enqueue(self._h, ft.size, _uptr(sq), _uptr(ft), _uptr(sp),
+                                             n_steps))
+
+    def read_tokens(self, n_seqs: int, n_steps: int) -> np.ndarray:
+        out = np.zeros((n_steps, n_seqs), dtype=np.uint32)
+        _check(_lib.lrs_model_read_tokens(self._h, n_seqs, n_steps, _uptr(out)))
+        return out
+
+    def benchmark_tokens(self, prompt: Sequence[int], decode_tokens: int, seq: int = 0):
+        """InferenceEngine::benchmark_tokens (src/engine.rs:189-223) on the device:
+        returns the decode_tokens tokens fed to the decode steps."""
+        _, first = self.prefill(prompt, 0, seq, want_logits=False)
+        if decode_tokens == 0:
+            return np.zeros(0, dtype=np.uint32)
+        return self.decode_greedy([first], [len(prompt)], decode_tokens, [seq])[:, 0]
+
+
+# ------------------------------------------------------ benchmark configs --
+def config_c0() -> LlamaConfig:
+    """Qwen2.5-0.5B shape."""
+    return LlamaConfig(896, 4864, 14, 2, 24, 151936, 1e-6, 1e6, 32768, 64, True)
+
+
+def config_c2() -> LlamaConfig:
+    """Qwen2.5-1.5B shape."""
+    return LlamaConfig(1536, 8960, 12, 2, 28, 151936, 1e-6, 1e6, 32768, 128, True)
+
+
+def config_c3() -> LlamaConfig:
+    """Qwen2.5-7B shape."""
+    return LlamaConfig(3584, 18944, 28, 4, 28, 152064, 1e-6, 1e6, 32768, 128, False)
+
+
+def config_c4() -> LlamaConfig:
+    """Qwen2.5-32B shape."""
+    return LlamaConfig(5120, 27648, 40, 8, 64, 152064, 1e-6, 1e6, 32768, 128, False)
+
+
+def prompt_tokens(seed: int, n: int, vocab: int) -> np.ndarray:
+    """Uniform prompt token ids of the benchmark workloads (numpy PCG64, seed + 1000)."""
+    return np.random.default_rng(seed + 1000).integers(0, vocab, n, dtype=np.int64).astype(np.uint32)

@@ -1,0 +1,816 @@
+// capi.cu -- the extern "C" surface of include/llamars.h.
+//
+// Host side of the CUDA backend: the KernelBackend::matvec equivalent
+// (src/backend.rs:69-73), tensor upload, and a CausalModel equivalent
+// (src/architecture.rs:42-78, src/model.rs:135-270) that owns the device
+// weights, the paged KV cache and the activation buffers, and replays the
+// per-token decode step as one CUDA graph.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/llamars.h"
+#include "common.h"
+#include "decode.cuh"
+#include "gemv.cuh"
+
+namespace lrs {
+thread_local std::string g_last_error;
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+void clear_error() { g_last_error.clear(); }
+}  // namespace lrs
+
+using namespace lrs;
+
+#define LRS_CUDA(call)                                                                      \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(LRS_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));        \
+  } while (0)
+
+struct lrs_backend {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  float* d_x = nullptr;
+  float* d_y = nullptr;
+  size_t x_cap = 0, y_cap = 0;
+};
+
+struct DevTensor {
+  uint8_t* d = nullptr;
+  size_t nbytes = 0;
+  int rows = 0, cols = 0;
+  uint32_t type = 0;
+};
+
+struct lrs_tensor {
+  lrs_backend* be = nullptr;
+  DevTensor t;
+};
+
+namespace {
+
+int32_t check_device_error(lrs_backend* be) {
+  int h = 0;
+  LRS_CUDA(cudaMemcpy(&h, be->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) {
+    cudaMemset(be->d_err, 0, sizeof(int));
+    return fail(LRS_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up (TMA copy not completed)");
+  }
+  return LRS_OK;
+}
+
+int32_t validate_tensor(size_t nbytes, size_t rows, size_t cols, uint32_t type) {
+  // QuantTensor::from_data, src/quant.rs:132-157
+  uint32_t bv, bb;
+  if (!type_geometry(type, &bv, &bb))
+    return fail(LRS_ERR_UNSUPPORTED,
+                "unsupported GGML tensor type " + std::to_string(type) +
+                    "; supported: F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K");
+  if (rows == 0 || cols == 0) return fail(LRS_ERR_INVALID, "empty tensor");
+  if (cols % bv)
+    return fail(LRS_ERR_INVALID, "last dimension " + std::to_string(cols) + " is not divisible by " +
+                                     std::to_string(bv) + " for " + type_name(type));
+  size_t expected = rows * (cols / bv) * bb;
+  if (nbytes != expected)
+    return fail(LRS_ERR_INVALID, std::string("bad ") + type_name(type) + " tensor byte length: got " +
+                                     std::to_string(nbytes) + ", expected " + std::to_string(expected));
+  if (cols % 32)
+    return fail(LRS_ERR_UNSUPPORTED, "the CUDA backend requires cols % 32 == 0");
+  return LRS_OK;
+}
+
+int32_t upload(const void* data, size_t nbytes, size_t rows, size_t cols, uint32_t type,
+               DevTensor* out) {
+  int32_t rc = validate_tensor(nbytes, rows, cols, type);
+  if (rc) return rc;
+  uint8_t* d = nullptr;
+  // +256: tiles are copied in 16-byte granules that may run past the last row.
+  if (cudaMalloc(&d, nbytes + 256) != cudaSuccess)
+    return fail(LRS_ERR_OOM, "cudaMalloc of " + std::to_string(nbytes) + " bytes failed");
+  cudaMemset(d + nbytes, 0, 256);
+  if (cudaMemcpy(d, data, nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(d);
+    return fail(LRS_ERR_CUDA, "upload copy failed");
+  }
+  out->d = d;
+  out->nbytes = nbytes;
+  out->rows = (int)rows;
+  out->cols = (int)cols;
+  out->type = type;
+  return LRS_OK;
+}
+
+template <typename T>
+int32_t dalloc(T** p, size_t count) {
+  if (cudaMalloc((void**)p, std::max<size_t>(count, 1) * sizeof(T)) != cudaSuccess)
+    return fail(LRS_ERR_OOM, "cudaMalloc failed (" + std::to_string(count * sizeof(T)) + " bytes)");
+  return LRS_OK;
+}
+
+int32_t ensure_cap(float** p, size_t* cap, size_t n) {
+  if (*cap >= n) return LRS_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  int32_t rc = dalloc(p, n);
+  if (rc) return rc;
+  *cap = n;
+  return LRS_OK;
+}
+
+GemvMat mat_of(const DevTensor& t, float* out, int out_ld, const float* bias = nullptr,
+               const DevTensor* t2 = nullptr) {
+  GemvMat m{};
+  m.w = t.d;
+  m.w2 = t2 ? t2->d : nullptr;
+  m.bias = bias;
+  m.out = out;
+  m.type = t.type;
+  m.rows = t.rows;
+  m.cols = t.cols;
+  m.out_ld = out_ld;
+  return m;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* lrs_last_error(void) { return g_last_error.c_str(); }
+
+lrs_status lrs_type_geometry(uint32_t t, uint32_t* bv, uint32_t* bb) {
+  uint32_t a, b;
+  if (!type_geometry(t, &a, &b)) return fail(LRS_ERR_UNSUPPORTED, "unsupported GGML type");
+  if (bv) *bv = a;
+  if (bb) *bb = b;
+  return LRS_OK;
+}
+
+lrs_status lrs_backend_create(int device, lrs_backend** out) {
+  if (!out) return fail(LRS_ERR_INVALID, "null out");
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+    return fail(LRS_ERR_CUDA, "no CUDA device is available");
+  if (device < 0 || device >= n) return fail(LRS_ERR_INVALID, "device ordinal out of range");
+  LRS_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  LRS_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(LRS_ERR_UNSUPPORTED, std::string("this build targets sm_100a (B200); device is ") +
+                                         prop.name);
+  auto* be = new lrs_backend();
+  be->device = device;
+  be->sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&be->d_err, sizeof(int)) != cudaSuccess) {
+    delete be;
+    return fail(LRS_ERR_CUDA, "stream / flag allocation failed");
+  }
+  cudaMemset(be->d_err, 0, sizeof(int));
+  *out = be;
+  return LRS_OK;
+}
+
+void lrs_backend_destroy(lrs_backend* be) {
+  if (!be) return;
+  cudaSetDevice(be->device);
+  cudaStreamSynchronize(be->stream);
+  cudaFree(be->d_err);
+  cudaFree(be->d_x);
+  cudaFree(be->d_y);
+  cudaStreamDestroy(be->stream);
+  delete be;
+}
+
+const char* lrs_backend_name(const lrs_backend*) { return "cuda-sm100a"; }
+size_t lrs_backend_threads(const lrs_backend* be) { return be ? (size_t)be->sms : 0; }
+void* lrs_backend_stream(lrs_backend* be) { return be ? (void*)be->stream : nullptr; }
+
+lrs_status lrs_backend_synchronize(lrs_backend* be) {
+  if (!be) return fail(LRS_ERR_INVALID, "null backend");
+  LRS_CUDA(cudaSetDevice(be->device));
+  LRS_CUDA(cudaStreamSynchronize(be->stream));
+  return check_device_error(be);
+}
+
+lrs_status lrs_tensor_upload(lrs_backend* be, const void* data, size_t nbytes, size_t rows,
+                             size_t cols, uint32_t type, lrs_tensor** out) {
+  if (!be || !data || !out) return fail(LRS_ERR_INVALID, "null argument");
+  LRS_CUDA(cudaSetDevice(be->device));
+  auto* t = new lrs_tensor();
+  t->be = be;
+  int32_t rc = upload(data, nbytes, rows, cols, type, &t->t);
+  if (rc) {
+    delete t;
+    return rc;
+  }
+  *out = t;
+  return LRS_OK;
+}
+
+void lrs_tensor_free(lrs_tensor* t) {
+  if (!t) return;
+  cudaSetDevice(t->be->device);
+  cudaFree(t->t.d);
+  delete t;
+}
+
+const void* lrs_tensor_device_ptr(const lrs_tensor* t) { return t ? t->t.d : nullptr; }
+
+lrs_status lrs_dequantize_rows(lrs_backend* be, const lrs_tensor* t, size_t row0, size_t nrows,
+                               float* out) {
+  if (!be || !t || !out) return fail(LRS_ERR_INVALID, "null argument");
+  if (row0 + nrows > (size_t)t->t.rows) return fail(LRS_ERR_INVALID, "row range out of bounds");
+  if (nrows == 0) return LRS_OK;
+  LRS_CUDA(cudaSetDevice(be->device));
+  size_t n = nrows * (size_t)t->t.cols;
+  int32_t rc = ensure_cap(&be->d_y, &be->y_cap, n);
+  if (rc) return rc;
+  LRS_CUDA(launch_dequant_rows(t->t.d, t->t.type, t->t.cols, (int)row0, (int)nrows, be->d_y,
+                               be->stream));
+  LRS_CUDA(cudaMemcpyAsync(out, be->d_y, n * 4, cudaMemcpyDeviceToHost, be->stream));
+  LRS_CUDA(cudaStreamSynchronize(be->stream));
+  return LRS_OK;
+}
+
+lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* d_in,
+                             size_t batch, float* d_out, void* stream) {
+  if (!be || !w || !d_in || !d_out) return fail(LRS_ERR_INVALID, "null argument");
+  if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
+  GemvMat m = mat_of(w->t, d_out, w->t.rows);
+  GemvParams p;
+  int32_t rc = gemv_plan(&p, &m, 1, EPI_STORE, (int)batch);
+  if (rc) return rc;
+  p.x = d_in;
+  p.x_ld = w->t.cols;
+  p.error_flag = be->d_err;
+  cudaStream_t st = stream ? (cudaStream_t)stream : be->stream;
+  LRS_CUDA(gemv_launch(p, st, be->sms, false));
+  return LRS_OK;
+}
+
+lrs_status lrs_matvec_batched(lrs_backend* be, const lrs_tensor* w, const float* in, size_t batch,
+                              size_t n_in, float* out, size_t n_out) {
+  if (!be || !w || !in || !out) return fail(LRS_ERR_INVALID, "null argument");
+  // QuantTensor::validate_matvec, src/quant.rs:303-318
+  if (n_in != (size_t)w->t.cols)
+    return fail(LRS_ERR_INVALID, "matvec input mismatch: got " + std::to_string(n_in) +
+                                     ", expected " + std::to_string(w->t.cols));
+  if (n_out != (size_t)w->t.rows)
+    return fail(LRS_ERR_INVALID, "matvec output mismatch: got " + std::to_string(n_out) +
+                                     ", expected " + std::to_string(w->t.rows));
+  if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
+  LRS_CUDA(cudaSetDevice(be->device));
+  int32_t rc = ensure_cap(&be->d_x, &be->x_cap, batch * n_in);
+  if (rc) return rc;
+  rc = ensure_cap(&be->d_y, &be->y_cap, batch * n_out);
+  if (rc) return rc;
+  LRS_CUDA(cudaMemcpyAsync(be->d_x, in, batch * n_in * 4, cudaMemcpyHostToDevice, be->stream));
+  rc = lrs_matvec_device(be, w, be->d_x, batch, be->d_y, be->stream);
+  if (rc) return rc;
+  LRS_CUDA(cudaMemcpyAsync(out, be->d_y, batch * n_out * 4, cudaMemcpyDeviceToHost, be->stream));
+  LRS_CUDA(cudaStreamSynchronize(be->stream));
+  return check_device_error(be);
+}
+
+lrs_status lrs_matvec(lrs_backend* be, const lrs_tensor* w, const float* in, size_t n_in,
+                      float* out, size_t n_out) {
+  return lrs_matvec_batched(be, w, in, 1, n_in, out, n_out);
+}
+
+}  // extern "C"
+
+// =============================================================== model ====
+
+namespace {
+
+struct Layer {
+  DevTensor q, k, v, o, gate, up, down;
+  float *in_norm = nullptr, *post_norm = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr;
+  void *kpool = nullptr, *vpool = nullptr;
+};
+
+struct GraphKey {
+  int batch;
+  const void* tokens_out;
+  bool operator<(const GraphKey& o) const {
+    return batch != o.batch ? batch < o.batch : tokens_out < o.tokens_out;
+  }
+};
+
+}  // namespace
+
+struct lrs_model {
+  lrs_backend* be = nullptr;
+  lrs_config c{};
+  lrs_model_options opt{};
+  std::vector<Layer> layers;
+  DevTensor embed, lm;
+  bool tied = false;
+  float* final_norm = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  std::vector<void*> allocs;  // everything cudaMalloc'd except the tensors above
+  // paged KV
+  int pages_per_seq = 0, total_pages = 0;
+  std::vector<int> free_pages;
+  std::vector<std::vector<int>> seq_pages;
+  int* d_pages = nullptr;
+  size_t kv_elem = 4;
+  // activations, for up to max_items items per step
+  int max_items = 0, max_split = 64;
+  float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+        *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+  unsigned long long* keys = nullptr;
+  int *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_step = nullptr;
+  uint32_t* d_last = nullptr;
+  uint32_t* d_tokens_out = nullptr;
+  size_t tokens_out_cap = 0;  // in elements
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  uint64_t weight_bytes = 0;
+};
+
+namespace {
+
+int32_t model_alloc(lrs_model* m, void** p, size_t bytes) {
+  if (cudaMalloc(p, std::max<size_t>(bytes, 4)) != cudaSuccess)
+    return fail(LRS_ERR_OOM, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+  m->allocs.push_back(*p);
+  return LRS_OK;
+}
+
+int32_t upload_vec(lrs_model* m, const float* h, size_t n, float** out) {
+  if (!h) {
+    *out = nullptr;
+    return LRS_OK;
+  }
+  int32_t rc = model_alloc(m, (void**)out, n * 4);
+  if (rc) return rc;
+  LRS_CUDA(cudaMemcpy(*out, h, n * 4, cudaMemcpyHostToDevice));
+  return LRS_OK;
+}
+
+int32_t upload_mat(const lrs_tensor_desc& d, size_t rows, size_t cols, const char* what,
+                   DevTensor* out) {
+  if (d.rows != rows || d.cols != cols)
+    return fail(LRS_ERR_INVALID, std::string("tensor ") + what + " has shape [" +
+                                     std::to_string(d.rows) + ", " + std::to_string(d.cols) +
+                                     "], expected [" + std::to_string(rows) + ", " +
+                                     std::to_string(cols) + "]");
+  return upload(d.data, d.nbytes, rows, cols, d.ggml_type, out);
+}
+
+int nsplit_for(const lrs_model* m, int batch) {
+  int want = (4 * m->be->sms + batch * (int)m->c.num_key_value_heads - 1) /
+             (batch * (int)m->c.num_key_value_heads);
+  int maxs = std::max(1, (int)((m->opt.max_seq_len + 31) / 32));
+  return std::max(1, std::min({want, m->max_split, maxs}));
+}
+
+int32_t ensure_pages(lrs_model* m, int seq, uint32_t last_pos) {
+  size_t need = last_pos / kPageSize + 1;
+  auto& pg = m->seq_pages[seq];
+  if (pg.size() >= need) return LRS_OK;
+  size_t old = pg.size();
+  while (pg.size() < need) {
+    if (m->free_pages.empty()) return fail(LRS_ERR_OOM, "KV page pool exhausted");
+    pg.push_back(m->free_pages.back());
+    m->free_pages.pop_back();
+  }
+  LRS_CUDA(cudaMemcpyAsync(m->d_pages + (size_t)seq * m->pages_per_seq + old, pg.data() + old,
+                           (pg.size() - old) * sizeof(int), cudaMemcpyHostToDevice, m->be->stream));
+  return LRS_OK;
+}
+
+// Queues one forward step for items 0..B-1 (d_tok / d_pos / d_seq already set):
+// Qwen2Model::forward_impl, src/model.rs:135-270, for B tokens at once.  When
+// `lm_item` >= 0 only that item runs the final norm + LM head (prefill);
+// lm_item == -1 runs it for every item; -2 skips it.
+int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool greedy_advance,
+                     int n_steps_cap) {
+  const lrs_config& c = m->c;
+  cudaStream_t st = m->be->stream;
+  const int h = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
+            nkv = c.num_key_value_heads, hd = c.head_dim, kvw = nkv * hd;
+  const int sms = m->be->sms;
+  StepIO io{m->d_tok, m->d_pos, m->d_seq, m->d_pages, m->pages_per_seq};
+  const int kv_bf16 = m->opt.kv_dtype == LRS_KV_BF16;
+  const int nsplit = nsplit_for(m, B);
+  int32_t rc;
+  LRS_CUDA(launch_embed(m->embed.d, m->embed.type, h, m->d_tok, B, m->residual, m->keys, st));
+  for (size_t li = 0; li < m->layers.size(); li++) {
+    Layer& L = m->layers[li];
+    GemvParams p;
+    // input_layernorm + q/k/v projections with bias (src/model.rs:175-186)
+    GemvMat qkv[3] = {mat_of(L.q, m->q, h, L.qb), mat_of(L.k, m->k, kvw, L.kb),
+                      mat_of(L.v, m->v, kvw, L.vb)};
+    if ((rc = gemv_plan(&p, qkv, 3, EPI_STORE, B))) return rc;
+    p.error_flag = m->be->d_err;
+    if (B == 1) {
+      p.x = m->residual;
+      p.norm_w = L.in_norm;
+      p.norm_eps = c.rms_norm_eps;
+    } else {
+      LRS_CUDA(launch_rmsnorm(m->residual, L.in_norm, c.rms_norm_eps, h, B, m->xn, st));
+      p.x = m->xn;
+    }
+    p.x_ld = h;
+    LRS_CUDA(gemv_launch(p, st, sms, true));
+    // RoPE + KV store (src/model.rs:188-205), attention (:206-231)
+    LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
+                               L.kpool, L.vpool, kv_bf16, st));
+    LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
+                              m->att, st));
+    // o_proj + residual (src/model.rs:233-238)
+    GemvMat om = mat_of(L.o, m->residual, h);
+    if ((rc = gemv_plan(&p, &om, 1, EPI_ADD, B))) return rc;
+    p.error_flag = m->be->d_err;
+    p.x = m->att;
+    p.x_ld = h;
+    LRS_CUDA(gemv_launch(p, st, sms, true));
+    // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
+    GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
+    if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B))) return rc;
+    p.error_flag = m->be->d_err;
+    if (B == 1) {
+      p.x = m->residual;
+      p.norm_w = L.post_norm;
+      p.norm_eps = c.rms_norm_eps;
+    } else {
+      LRS_CUDA(launch_rmsnorm(m->residual, L.post_norm, c.rms_norm_eps, h, B, m->xn, st));
+      p.x = m->xn;
+    }
+    p.x_ld = h;
+    LRS_CUDA(gemv_launch(p, st, sms, true));
+    // down_proj + residual (src/model.rs:255-260)
+    GemvMat dm = mat_of(L.down, m->residual, h);
+    if ((rc = gemv_plan(&p, &dm, 1, EPI_ADD, B))) return rc;
+    p.error_flag = m->be->d_err;
+    p.x = m->act;
+    p.x_ld = I;
+    LRS_CUDA(gemv_launch(p, st, sms, true));
+  }
+  if (lm_item == -2) return LRS_OK;
+  // final norm + lm_head (src/model.rs:263-268) fused with the greedy argmax
+  const int nb = lm_item >= 0 ? 1 : B;
+  const float* xin = m->residual + (lm_item >= 0 ? (size_t)lm_item * h : 0);
+  GemvMat lmm = mat_of(m->lm, want_logits ? m->logits : nullptr, c.vocab_size);
+  GemvParams p;
+  if ((rc = gemv_plan(&p, &lmm, 1, EPI_ARGMAX, nb))) return rc;
+  p.error_flag = m->be->d_err;
+  p.argmax_keys = m->keys + (lm_item >= 0 ? lm_item : 0);
+  if (nb == 1) {
+    p.x = xin;
+    p.norm_w = m->final_norm;
+    p.norm_eps = c.rms_norm_eps;
+  } else {
+    LRS_CUDA(launch_rmsnorm(xin, m->final_norm, c.rms_norm_eps, h, nb, m->xn, st));
+    p.x = m->xn;
+  }
+  p.x_ld = h;
+  LRS_CUDA(gemv_launch(p, st, sms, true));
+  if (greedy_advance)
+    LRS_CUDA(launch_advance(m->keys, m->d_tok, m->d_pos, B, m->d_step, n_steps_cap,
+                            m->d_tokens_out, m->d_last, st));
+  return LRS_OK;
+}
+
+int32_t set_items(lrs_model* m, int n, const int* tok, const int* pos, const int* seq) {
+  cudaStream_t st = m->be->stream;
+  LRS_CUDA(cudaMemcpyAsync(m->d_tok, tok, n * sizeof(int), cudaMemcpyHostToDevice, st));
+  LRS_CUDA(cudaMemcpyAsync(m->d_pos, pos, n * sizeof(int), cudaMemcpyHostToDevice, st));
+  LRS_CUDA(cudaMemcpyAsync(m->d_seq, seq, n * sizeof(int), cudaMemcpyHostToDevice, st));
+  // the host arrays may go out of scope: make the copies complete
+  LRS_CUDA(cudaStreamSynchronize(st));
+  return LRS_OK;
+}
+
+int32_t read_argmax(lrs_model* m, int item, uint32_t* out) {
+  unsigned long long key = 0;
+  LRS_CUDA(cudaMemcpy(&key, m->keys + item, sizeof(key), cudaMemcpyDeviceToHost));
+  *out = (uint32_t)(key & 0xffffffffull);
+  return LRS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
+                            const lrs_model_options* options, lrs_model** out) {
+  if (!be || !d || !out) return fail(LRS_ERR_INVALID, "null argument");
+  const lrs_config& c = d->config;
+  // LlamaConfig::validate, src/config.rs:57-89
+  if (!c.hidden_size || !c.intermediate_size || !c.num_attention_heads ||
+      !c.num_key_value_heads || !c.num_hidden_layers || !c.vocab_size || !c.head_dim)
+    return fail(LRS_ERR_INVALID, "invalid Qwen2 config: dimensions must be non-zero");
+  if (c.num_attention_heads % c.num_key_value_heads)
+    return fail(LRS_ERR_INVALID, "num_attention_heads must be divisible by num_key_value_heads");
+  if (c.num_attention_heads * c.head_dim != c.hidden_size)
+    return fail(LRS_ERR_INVALID, "num_attention_heads * head_dim must equal hidden_size");
+  if (c.head_dim % 2) return fail(LRS_ERR_INVALID, "Qwen2 RoPE requires an even head_dim");
+  if (!(c.rms_norm_eps > 0.0f) || !std::isfinite(c.rms_norm_eps))
+    return fail(LRS_ERR_INVALID, "rms_norm_eps must be finite and positive");
+  if (!(c.rope_theta > 0.0f) || !std::isfinite(c.rope_theta))
+    return fail(LRS_ERR_INVALID, "rope_theta must be finite and positive");
+  if (c.head_dim != 64 && c.head_dim != 128)
+    return fail(LRS_ERR_UNSUPPORTED, "the CUDA attention kernel supports head_dim 64 or 128");
+  if (c.num_attention_heads / c.num_key_value_heads > 8)
+    return fail(LRS_ERR_UNSUPPORTED, "the CUDA attention kernel supports up to 8 query heads per KV head");
+  lrs_model_options opt{};
+  opt.max_seq_len = 4096;
+  opt.max_sequences = 1;
+  opt.kv_dtype = LRS_KV_F32;
+  opt.use_graph = 1;
+  if (options) opt = *options;
+  if (opt.max_seq_len == 0 || opt.max_seq_len > c.max_position_embeddings)
+    return fail(LRS_ERR_INVALID, "requested context " + std::to_string(opt.max_seq_len) +
+                                     " exceeds model limit " +
+                                     std::to_string(c.max_position_embeddings));
+  if (opt.max_sequences == 0) opt.max_sequences = 1;
+  LRS_CUDA(cudaSetDevice(be->device));
+
+  auto m = std::make_unique<lrs_model>();
+  m->be = be;
+  m->c = c;
+  m->opt = opt;
+  const size_t h = c.hidden_size, I = c.intermediate_size, kvw = (size_t)c.num_key_value_heads * c.head_dim;
+  int32_t rc;
+  auto cleanup = [&](int32_t code) {
+    lrs_model_destroy(m.release());
+    return code;
+  };
+  if ((rc = upload_mat(d->embed_tokens, c.vocab_size, h, "model.embed_tokens.weight", &m->embed)))
+    return cleanup(rc);
+  if (d->lm_head.data == d->embed_tokens.data) {
+    m->tied = true;
+    m->lm = m->embed;
+  } else if ((rc = upload_mat(d->lm_head, c.vocab_size, h, "lm_head.weight", &m->lm))) {
+    return cleanup(rc);
+  }
+  if ((rc = upload_vec(m.get(), d->final_norm, h, &m->final_norm))) return cleanup(rc);
+  if (!m->final_norm) return cleanup(fail(LRS_ERR_INVALID, "missing model.norm.weight"));
+  m->weight_bytes = m->lm.nbytes + m->embed.nbytes / c.vocab_size;
+  m->layers.resize(c.num_hidden_layers);
+  for (uint32_t i = 0; i < c.num_hidden_layers; i++) {
+    const lrs_layer_desc& s = d->layers[i];
+    Layer& L = m->layers[i];
+    if ((rc = upload_mat(s.q_proj, h, h, "q_proj", &L.q)) ||
+        (rc = upload_mat(s.k_proj, kvw, h, "k_proj", &L.k)) ||
+        (rc = upload_mat(s.v_proj, kvw, h, "v_proj", &L.v)) ||
+        (rc = upload_mat(s.o_proj, h, h, "o_proj", &L.o)) ||
+        (rc = upload_mat(s.gate_proj, I, h, "gate_proj", &L.gate)) ||
+        (rc = upload_mat(s.up_proj, I, h, "up_proj", &L.up)) ||
+        (rc = upload_mat(s.down_proj, h, I, "down_proj", &L.down)))
+      return cleanup(rc);
+    if (L.gate.type != L.up.type)
+      return cleanup(fail(LRS_ERR_UNSUPPORTED, "gate_proj and up_proj must share a GGML type"));
+    if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
+        (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
+        (rc = upload_vec(m.get(), s.q_bias, h, &L.qb)) ||
+        (rc = upload_vec(m.get(), s.k_bias, kvw, &L.kb)) ||
+        (rc = upload_vec(m.get(), s.v_bias, kvw, &L.vb)))
+      return cleanup(rc);
+    if (!L.in_norm || !L.post_norm) return cleanup(fail(LRS_ERR_INVALID, "missing layer norm weight"));
+    m->weight_bytes += L.q.nbytes + L.k.nbytes + L.v.nbytes + L.o.nbytes + L.gate.nbytes +
+                       L.up.nbytes + L.down.nbytes;
+  }
+  // RoPE table: prepare_rope (src/model.rs:76-84) for every position, on the
+  // host with the same libm calls, so device and reference agree bit for bit.
+  {
+    const size_t half = c.head_dim / 2;
+    std::vector<float> cs(opt.max_seq_len * half), sn(opt.max_seq_len * half);
+    for (size_t pos = 0; pos < opt.max_seq_len; pos++)
+      for (size_t i = 0; i < half; i++) {
+        float inv_freq = 1.0f / powf(c.rope_theta, 2.0f * (float)i / (float)c.head_dim);
+        float angle = (float)pos * inv_freq;
+        sn[pos * half + i] = sinf(angle);
+        cs[pos * half + i] = cosf(angle);
+      }
+    if ((rc = upload_vec(m.get(), cs.data(), cs.size(), &m->rope_cos)) ||
+        (rc = upload_vec(m.get(), sn.data(), sn.size(), &m->rope_sin)))
+      return cleanup(rc);
+  }
+  // Paged KV pools.
+  m->kv_elem = opt.kv_dtype == LRS_KV_BF16 ? 2 : 4;
+  m->pages_per_seq = (int)((opt.max_seq_len + kPageSize - 1) / kPageSize);
+  m->total_pages = m->pages_per_seq * (int)opt.max_sequences;
+  const size_t page_elems = (size_t)c.num_key_value_heads * kPageSize * c.head_dim;
+  for (auto& L : m->layers) {
+    if ((rc = model_alloc(m.get(), &L.kpool, (size_t)m->total_pages * page_elems * m->kv_elem)) ||
+        (rc = model_alloc(m.get(), &L.vpool, (size_t)m->total_pages * page_elems * m->kv_elem)))
+      return cleanup(rc);
+  }
+  for (int pg = m->total_pages - 1; pg >= 0; pg--) m->free_pages.push_back(pg);
+  m->seq_pages.resize(opt.max_sequences);
+  if ((rc = model_alloc(m.get(), (void**)&m->d_pages,
+                        (size_t)m->total_pages * sizeof(int))))
+    return cleanup(rc);
+  LRS_CUDA(cudaMemset(m->d_pages, 0, (size_t)m->total_pages * sizeof(int)));
+  // Activations (InferenceBuffers, src/cache.rs:79-101) for up to max_items items.
+  m->max_items = std::max<int>(64, (int)opt.max_sequences);
+  const size_t B = m->max_items;
+  if ((rc = model_alloc(m.get(), (void**)&m->residual, B * h * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->xn, B * h * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->q, B * h * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->k, B * kvw * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->v, B * kvw * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->att, B * h * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->act, B * I * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->logits, (size_t)c.vocab_size * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->part,
+                        B * c.num_attention_heads * m->max_split * (c.head_dim + 2) * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->keys, B * 8)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_tok, B * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_pos, B * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_seq, B * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_step, 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
+    return cleanup(rc);
+  LRS_CUDA(cudaDeviceSynchronize());
+  *out = m.release();
+  return LRS_OK;
+}
+
+void lrs_model_destroy(lrs_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->be->device);
+  cudaStreamSynchronize(m->be->stream);
+  for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+  for (auto& L : m->layers) {
+    cudaFree(L.q.d);
+    cudaFree(L.k.d);
+    cudaFree(L.v.d);
+    cudaFree(L.o.d);
+    cudaFree(L.gate.d);
+    cudaFree(L.up.d);
+    cudaFree(L.down.d);
+  }
+  cudaFree(m->embed.d);
+  if (!m->tied) cudaFree(m->lm.d);
+  for (void* p : m->allocs) cudaFree(p);
+  cudaFree(m->d_tokens_out);
+  delete m;
+}
+
+uint64_t lrs_model_weight_bytes(const lrs_model* m) { return m ? m->weight_bytes : 0; }
+
+lrs_status lrs_model_reset(lrs_model* m, uint32_t seq) {
+  if (!m) return fail(LRS_ERR_INVALID, "null model");
+  if (seq >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
+  // KVCache::reset is a no-op in the reference (positions are overwritten
+  // before they are read); here the slot's pages go back to the pool.
+  for (int pg : m->seq_pages[seq]) m->free_pages.push_back(pg);
+  m->seq_pages[seq].clear();
+  return LRS_OK;
+}
+
+lrs_status lrs_model_forward_token(lrs_model* m, uint32_t seq, uint32_t token, uint32_t pos,
+                                   int logits_mode, float* logits_out, uint32_t* argmax_out) {
+  if (!m) return fail(LRS_ERR_INVALID, "null model");
+  return lrs_model_prefill(m, seq, &token, 1, pos, logits_mode == LRS_LOGITS_COMPUTE ? logits_out : nullptr,
+                           logits_mode == LRS_LOGITS_COMPUTE ? argmax_out : nullptr) ;
+}
+
+lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens, size_t n,
+                             uint32_t start_pos, float* logits_out, uint32_t* argmax_out) {
+  if (!m || !tokens) return fail(LRS_ERR_INVALID, "null argument");
+  if (n == 0) return fail(LRS_ERR_INVALID, "prefill requires at least one token");
+  if (seq >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
+  if ((size_t)start_pos + n > m->opt.max_seq_len)
+    return fail(LRS_ERR_INVALID, "position " + std::to_string(start_pos + n - 1) +
+                                     " exceeds configured context " + std::to_string(m->opt.max_seq_len));
+  for (size_t i = 0; i < n; i++)
+    if (tokens[i] >= m->c.vocab_size)
+      return fail(LRS_ERR_INVALID, "token id " + std::to_string(tokens[i]) + " is outside vocabulary");
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  int32_t rc = ensure_pages(m, (int)seq, start_pos + (uint32_t)n - 1);
+  if (rc) return rc;
+  const bool want = logits_out != nullptr || argmax_out != nullptr;
+  const size_t chunk = 64;
+  std::vector<int> tok(chunk), pos(chunk), sq(chunk, (int)seq);
+  for (size_t c0 = 0; c0 < n; c0 += chunk) {
+    const int nb = (int)std::min(chunk, n - c0);
+    for (int i = 0; i < nb; i++) {
+      tok[i] = (int)tokens[c0 + i];
+      pos[i] = (int)(start_pos + c0 + i);
+    }
+    if ((rc = set_items(m, nb, tok.data(), pos.data(), sq.data()))) return rc;
+    const bool last = c0 + nb == n;
+    rc = enqueue_step(m, nb, last && want ? nb - 1 : -2, logits_out != nullptr, false, 0);
+    if (rc) return rc;
+  }
+  if (logits_out)
+    LRS_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->c.vocab_size * 4,
+                             cudaMemcpyDeviceToHost, m->be->stream));
+  LRS_CUDA(cudaStreamSynchronize(m->be->stream));
+  if ((rc = check_device_error(m->be))) return rc;
+  if (argmax_out) {
+    int item = (int)((n - 1) % chunk);
+    if ((rc = read_argmax(m, item, argmax_out))) return rc;
+  }
+  return LRS_OK;
+}
+
+lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
+                                    const uint32_t* first_tokens, const uint32_t* start_pos,
+                                    size_t n_steps) {
+  if (!m || !seqs || !first_tokens || !start_pos) return fail(LRS_ERR_INVALID, "null argument");
+  if (n_seqs == 0 || n_seqs > (size_t)m->max_items)
+    return fail(LRS_ERR_INVALID, "n_seqs out of range");
+  if (n_steps == 0) return LRS_OK;
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  const int B = (int)n_seqs;
+  std::vector<int> tok(B), pos(B), sq(B);
+  for (int i = 0; i < B; i++) {
+    if (seqs[i] >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
+    if (first_tokens[i] >= m->c.vocab_size) return fail(LRS_ERR_INVALID, "token id is outside vocabulary");
+    if ((size_t)start_pos[i] + n_steps > m->opt.max_seq_len)
+      return fail(LRS_ERR_INVALID, "decode steps exceed configured context");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == seqs[i]) return fail(LRS_ERR_INVALID, "duplicate sequence slot in batch");
+    tok[i] = (int)first_tokens[i];
+    pos[i] = (int)start_pos[i];
+    sq[i] = (int)seqs[i];
+    int32_t rc = ensure_pages(m, sq[i], start_pos[i] + (uint32_t)n_steps - 1);
+    if (rc) return rc;
+  }
+  // tokens_out: [n_steps][B]; row 0 holds the first tokens.
+  size_t need = n_steps * (size_t)B;
+  if (need > m->tokens_out_cap) {
+    for (auto it = m->graphs.begin(); it != m->graphs.end();) {
+      cudaGraphExecDestroy(it->second);
+      it = m->graphs.erase(it);
+    }
+    cudaFree(m->d_tokens_out);
+    m->d_tokens_out = nullptr;
+    size_t cap = std::max(need, (size_t)4096);
+    if (cudaMalloc(&m->d_tokens_out, cap * 4) != cudaSuccess)
+      return fail(LRS_ERR_OOM, "token buffer allocation failed");
+    m->tokens_out_cap = cap;
+  }
+  int32_t rc = set_items(m, B, tok.data(), pos.data(), sq.data());
+  if (rc) return rc;
+  cudaStream_t st = m->be->stream;
+  LRS_CUDA(cudaMemcpyAsync(m->d_tokens_out, first_tokens, B * 4, cudaMemcpyHostToDevice, st));
+  LRS_CUDA(cudaMemsetAsync(m->d_step, 0, 4, st));
+  const int cap_steps = (int)(m->tokens_out_cap / B);
+  if (m->opt.use_graph) {
+    GraphKey key{B, m->d_tokens_out};
+    auto it = m->graphs.find(key);
+    cudaGraphExec_t exec = nullptr;
+    if (it == m->graphs.end()) {
+      cudaGraph_t graph;
+      LRS_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_step(m, B, -1, false, true, cap_steps);
+      cudaError_t e = cudaStreamEndCapture(st, &graph);
+      if (rc) return rc;
+      if (e != cudaSuccess) return fail(LRS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess)
+        return fail(LRS_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+      m->graphs[key] = exec;
+    } else {
+      exec = it->second;
+    }
+    for (size_t s = 0; s < n_steps; s++) LRS_CUDA(cudaGraphLaunch(exec, st));
+  } else {
+    for (size_t s = 0; s < n_steps; s++)
+      if ((rc = enqueue_step(m, B, -1, false, true, cap_steps))) return rc;
+  }
+  return LRS_OK;
+}
+
+lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, uint32_t* out) {
+  if (!m || !out) return fail(LRS_ERR_INVALID, "null argument");
+  if (n_seqs * n_steps > m->tokens_out_cap) return fail(LRS_ERR_INVALID, "token range out of bounds");
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  LRS_CUDA(cudaMemcpyAsync(out, m->d_tokens_out, n_seqs * n_steps * 4, cudaMemcpyDeviceToHost,
+                           m->be->stream));
+  LRS_CUDA(cudaStreamSynchronize(m->be->stream));
+  return check_device_error(m->be);
+}
+
+lrs_status lrs_model_decode_greedy(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
+                                   const uint32_t* first_tokens, const uint32_t* start_pos,
+                                   size_t n_steps, uint32_t* tokens_out) {
+  int32_t rc = lrs_model_decode_enqueue(m, n_seqs, seqs, first_tokens, start_pos, n_steps);
+  if (rc) return rc;
+  if (!tokens_out || n_steps == 0) return lrs_backend_synchronize(m->be);
+  return lrs_model_read_tokens(m, n_seqs, n_steps, tokens_out);
+}
+
+}  // extern "C"

@@ -1,0 +1,363 @@
+// decode.cu -- embedding, RMSNorm, RoPE + paged KV store, split-K GQA decode
+// attention and greedy bookkeeping for the Qwen2 token step (sm_100a).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <math.h>
+
+#include "common.h"
+#include "decode.cuh"
+#include "device_common.cuh"
+
+namespace lrs {
+namespace {
+
+// ---- embedding / dequantization (value_at, bit-exact) ---------------------
+template <int T>
+__global__ void __launch_bounds__(128)
+    embed_kernel(const uint8_t* w, int cols, const int* rows, int row0, float* out,
+                 unsigned long long* keys) {
+  using BT = BlockTraits<T>;
+  const int b = blockIdx.x;
+  const size_t rb = (size_t)(cols / BT::kValues) * BT::kBytes;
+  const int row = rows ? rows[b] : row0 + b;
+  const uint8_t* rp = w + (size_t)row * rb;
+  float* o = out + (size_t)b * cols;
+  if (keys && threadIdx.x == 0) keys[b] = 0ull;
+  for (int pc = threadIdx.x; pc < cols / 32; pc += blockDim.x) {
+    const int unit = pc / BT::kPieces, sub = pc % BT::kPieces;
+    float v[32];
+    decode_piece<T>(rp + (size_t)unit * BT::kBytes, sub, v);
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int col = unit * BT::kValues + run_col<T>(sub, r);
+#pragma unroll
+      for (int i = 0; i < 8; i++) o[col + i] = v[r * 8 + i];
+    }
+  }
+}
+
+cudaError_t embed_dispatch(const uint8_t* w, uint32_t type, int cols, const int* rows, int row0,
+                           int n, float* out, unsigned long long* keys, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  dim3 g(n), b(128);
+#define LRS_EMBED(T) \
+  case T: embed_kernel<T><<<g, b, 0, st>>>(w, cols, rows, row0, out, keys); break;
+  switch (type) {
+    LRS_EMBED(LRS_GGML_F32)
+    LRS_EMBED(LRS_GGML_F16)
+    LRS_EMBED(LRS_GGML_BF16)
+    LRS_EMBED(LRS_GGML_Q4_0)
+    LRS_EMBED(LRS_GGML_Q4_1)
+    LRS_EMBED(LRS_GGML_Q5_0)
+    LRS_EMBED(LRS_GGML_Q5_1)
+    LRS_EMBED(LRS_GGML_Q8_0)
+    LRS_EMBED(LRS_GGML_Q4_K)
+    LRS_EMBED(LRS_GGML_Q5_K)
+    LRS_EMBED(LRS_GGML_Q6_K)
+    default: return cudaErrorInvalidValue;
+  }
+#undef LRS_EMBED
+  return cudaGetLastError();
+}
+
+// ---- RMSNorm ---------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    rmsnorm_kernel(const float* x, const float* w, float eps, int n, float* out) {
+  __shared__ float red[8];
+  const float* xb = x + (size_t)blockIdx.x * n;
+  float* ob = out + (size_t)blockIdx.x * n;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(xb[i], xb[i], ss);
+  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int k = 0; k < 8; k++) tot += red[k];
+  const float inv = 1.0f / sqrtf(tot / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += 256) ob[i] = xb[i] * (inv * w[i]);
+}
+
+// ---- RoPE + KV store --------------------------------------------------------
+__device__ __forceinline__ size_t kv_offset(const StepIO& io, int b, int p, int nkv, int kvh,
+                                            int hd) {
+  const int page = io.pages[io.seq[b] * io.max_pages + p / kPageSize];
+  return (((size_t)page * nkv + kvh) * kPageSize + (p % kPageSize)) * hd;
+}
+
+__global__ void __launch_bounds__(256)
+    rope_store_kernel(float* q, const float* k, const float* v, const float* cos_t,
+                      const float* sin_t, StepIO io, int nh, int nkv, int hd, void* kpool,
+                      void* vpool, int kv_bf16) {
+  const int b = blockIdx.x;
+  const int half = hd / 2;
+  const int pos = io.pos[b];
+  const float* c = cos_t + (size_t)pos * half;
+  const float* s = sin_t + (size_t)pos * half;
+  float* qb = q + (size_t)b * nh * hd;
+  // apply_rope_inplace, src/model.rs:86-95 (unfused, as the reference)
+  for (int idx = threadIdx.x; idx < nh * half; idx += 256) {
+    const int h = idx / half, i = idx % half;
+    float re = qb[h * hd + i], im = qb[h * hd + i + half];
+    qb[h * hd + i] = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
+    qb[h * hd + i + half] = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
+  }
+  const float* kb = k + (size_t)b * nkv * hd;
+  const float* vb = v + (size_t)b * nkv * hd;
+  for (int idx = threadIdx.x; idx < nkv * half; idx += 256) {
+    const int h = idx / half, i = idx % half;
+    float re = kb[h * hd + i], im = kb[h * hd + i + half];
+    float k0 = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
+    float k1 = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
+    size_t o = kv_offset(io, b, pos, nkv, h, hd);
+    if (kv_bf16) {
+      reinterpret_cast<__nv_bfloat16*>(kpool)[o + i] = __float2bfloat16_rn(k0);
+      reinterpret_cast<__nv_bfloat16*>(kpool)[o + i + half] = __float2bfloat16_rn(k1);
+    } else {
+      reinterpret_cast<float*>(kpool)[o + i] = k0;
+      reinterpret_cast<float*>(kpool)[o + i + half] = k1;
+    }
+  }
+  for (int idx = threadIdx.x; idx < nkv * hd; idx += 256) {
+    const int h = idx / hd, d = idx % hd;
+    size_t o = kv_offset(io, b, pos, nkv, h, hd);
+    if (kv_bf16)
+      reinterpret_cast<__nv_bfloat16*>(vpool)[o + d] = __float2bfloat16_rn(vb[idx]);
+    else
+      reinterpret_cast<float*>(vpool)[o + d] = vb[idx];
+  }
+}
+
+// ---- split-K GQA decode attention ------------------------------------------
+constexpr int kMaxGroup = 8;  // query heads per KV head handled by one CTA
+constexpr int kAttnWarps = 4;
+
+template <int HD, bool BF16>
+__device__ __forceinline__ void load_row(const void* pool, size_t off, int d0, float* out) {
+  constexpr int DPL = HD / 32;
+  if constexpr (BF16) {
+    const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(pool) + off + d0;
+#pragma unroll
+    for (int k = 0; k < DPL; k++) out[k] = __bfloat162float(p[k]);
+  } else {
+    const float* p = reinterpret_cast<const float*>(pool) + off + d0;
+    if constexpr (DPL == 4) {
+      float4 t = *reinterpret_cast<const float4*>(p);
+      out[0] = t.x, out[1] = t.y, out[2] = t.z, out[3] = t.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < DPL; k++) out[k] = p[k];
+    }
+  }
+}
+
+template <int HD, bool BF16>
+__global__ void __launch_bounds__(kAttnWarps * 32)
+    attn_split_kernel(const float* q, StepIO io, int nh, int nkv, const void* kpool,
+                      const void* vpool, int nsplit, float scale, float* part) {
+  constexpr int DPL = HD / 32;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = nh / nkv;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int L = io.pos[b] + 1;
+  const int chunk = (L + nsplit - 1) / nsplit;
+  const int s0 = split * chunk, s1 = min(L, s0 + chunk);
+  __shared__ float qs[kMaxGroup][HD];
+  __shared__ float wm[kAttnWarps][kMaxGroup], wl[kAttnWarps][kMaxGroup];
+  __shared__ float wo[kAttnWarps][kMaxGroup][HD];
+  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x)
+    qs[idx / HD][idx % HD] = q[(size_t)b * nh * HD + (size_t)(kvh * G) * HD + idx];
+  __syncthreads();
+
+  float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][DPL];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
+#pragma unroll
+    for (int k = 0; k < DPL; k++) o[g][k] = 0.0f;
+  }
+  for (int base = s0 + warp * 32; base < s1; base += kAttnWarps * 32) {
+    const int p = base + lane;
+    const bool valid = p < s1;
+    float sc[kMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.0f;
+    if (valid) {
+      const size_t off = kv_offset(io, b, p, nkv, kvh, HD);
+      for (int d = 0; d < HD; d += 4) {
+        float kk[4];
+        if constexpr (BF16) {
+          const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(kpool) + off + d;
+#pragma unroll
+          for (int t = 0; t < 4; t++) kk[t] = __bfloat162float(kp[t]);
+        } else {
+          float4 t4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kpool) + off + d);
+          kk[0] = t4.x, kk[1] = t4.y, kk[2] = t4.z, kk[3] = t4.w;
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; g++)
+          if (g < G)
+#pragma unroll
+            for (int t = 0; t < 4; t++) sc[g] = fmaf(qs[g][d + t], kk[t], sc[g]);
+      }
+    }
+    float pe[kMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) {
+      if (g >= G) {
+        pe[g] = 0.0f;
+        continue;
+      }
+      float s = valid ? sc[g] * scale : -INFINITY;
+      float cm = s;
+      for (int w = 16; w >= 1; w >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, w));
+      const float mn = fmaxf(m[g], cm);
+      const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
+      float e = valid ? expf(s - mn) : 0.0f;
+      float es = e;
+      for (int w = 16; w >= 1; w >>= 1) es += __shfl_xor_sync(0xffffffffu, es, w);
+      l[g] = l[g] * corr + es;
+#pragma unroll
+      for (int k = 0; k < DPL; k++) o[g][k] *= corr;
+      m[g] = mn;
+      pe[g] = e;
+    }
+    const int nvalid = min(32, s1 - base);
+    for (int j = 0; j < nvalid; j++) {
+      float vv[DPL];
+      load_row<HD, BF16>(vpool, kv_offset(io, b, base + j, nkv, kvh, HD), lane * DPL, vv);
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; g++) {
+        const float pj = __shfl_sync(0xffffffffu, pe[g], j);
+#pragma unroll
+        for (int k = 0; k < DPL; k++) o[g][k] = fmaf(pj, vv[k], o[g][k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; g++) {
+    if (g >= G) break;
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+#pragma unroll
+    for (int k = 0; k < DPL; k++) wo[warp][g][lane * DPL + k] = o[g][k];
+  }
+  __syncthreads();
+  // Merge the warps; part layout [b][head][split][2 + HD] = (m, l, o[HD]).
+  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+    const int g = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w][g]);
+    float Ls = 0.0f, O = 0.0f;
+    for (int w = 0; w < kAttnWarps; w++) {
+      const float f = wm[w][g] == -INFINITY ? 0.0f : expf(wm[w][g] - M);
+      Ls += wl[w][g] * f;
+      O += wo[w][g][d] * f;
+    }
+    float* pp = part + (((size_t)b * nh + kvh * G + g) * nsplit + split) * (HD + 2);
+    if (d == 0) {
+      pp[0] = s0 < s1 ? M : -INFINITY;
+      pp[1] = s0 < s1 ? Ls : 0.0f;
+    }
+    pp[2 + d] = s0 < s1 ? O : 0.0f;
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(HD) attn_combine_kernel(const float* part, int nh, int nsplit,
+                                                          float* att) {
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const float* pp = part + ((size_t)b * nh + h) * nsplit * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[s * (HD + 2)]);
+  float Ls = 0.0f, O = 0.0f;
+  for (int s = 0; s < nsplit; s++) {
+    const float ms = pp[s * (HD + 2)];
+    if (ms == -INFINITY) continue;
+    const float f = expf(ms - M);
+    Ls += pp[s * (HD + 2) + 1] * f;
+    O += pp[s * (HD + 2) + 2 + d] * f;
+  }
+  att[((size_t)b * nh + h) * HD + d] = O / Ls;
+}
+
+__global__ void advance_kernel(const unsigned long long* keys, int* tok, int* pos, int batch,
+                               int* step, int n_steps, uint32_t* tokens_out, uint32_t* last) {
+  const int s = *step;
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+    const uint32_t t = (uint32_t)(keys[b] & 0xffffffffull);
+    tok[b] = (int)t;
+    pos[b] += 1;
+    if (last) last[b] = t;
+    if (tokens_out && s + 1 < n_steps) tokens_out[(size_t)(s + 1) * batch + b] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *step = s + 1;
+}
+
+}  // namespace
+
+cudaError_t launch_embed(const uint8_t* w, uint32_t type, int cols, const int* rows, int n,
+                         float* out, unsigned long long* keys, cudaStream_t st) {
+  return embed_dispatch(w, type, cols, rows, 0, n, out, keys, st);
+}
+
+cudaError_t launch_dequant_rows(const uint8_t* w, uint32_t type, int cols, int row0, int n,
+                                float* out, cudaStream_t st) {
+  return embed_dispatch(w, type, cols, nullptr, row0, n, out, nullptr, st);
+}
+
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int batch, float* out,
+                           cudaStream_t st) {
+  rmsnorm_kernel<<<batch, 256, 0, st>>>(x, w, eps, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_store(float* q, const float* k, const float* v, const float* cos_t,
+                              const float* sin_t, StepIO io, int batch, int nh, int nkv, int hd,
+                              void* kpool, void* vpool, int kv_bf16, cudaStream_t st) {
+  rope_store_kernel<<<batch, 256, 0, st>>>(q, k, v, cos_t, sin_t, io, nh, nkv, hd, kpool, vpool,
+                                           kv_bf16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
+                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
+                             float* part, float* att, cudaStream_t st) {
+  if (nh / nkv > kMaxGroup) return cudaErrorInvalidValue;
+  const float scale = 1.0f / sqrtf((float)hd);
+  dim3 g(nsplit, nkv, batch);
+#define LRS_ATTN(HD, BF)                                                                         \
+  attn_split_kernel<HD, BF><<<g, kAttnWarps * 32, 0, st>>>(q, io, nh, nkv, kpool, vpool, nsplit, \
+                                                            scale, part);                        \
+  attn_combine_kernel<HD><<<dim3(nh, batch), HD, 0, st>>>(part, nh, nsplit, att);
+  if (hd == 128) {
+    if (kv_bf16) {
+      LRS_ATTN(128, true)
+    } else {
+      LRS_ATTN(128, false)
+    }
+  } else if (hd == 64) {
+    if (kv_bf16) {
+      LRS_ATTN(64, true)
+    } else {
+      LRS_ATTN(64, false)
+    }
+  } else {
+    return cudaErrorInvalidValue;
+  }
+#undef LRS_ATTN
+  return cudaGetLastError();
+}
+
+cudaError_t launch_advance(const unsigned long long* keys, int* tok, int* pos, int batch,
+                           int* step, int n_steps, uint32_t* tokens_out, uint32_t* last,
+                           cudaStream_t st) {
+  advance_kernel<<<1, 64, 0, st>>>(keys, tok, pos, batch, step, n_steps, tokens_out, last);
+  return cudaGetLastError();
+}
+
+}  // namespace lrs

@@ -1,0 +1,54 @@
+// gemv.cuh -- quantized matrix-vector products (decode GEMV) for sm_100a.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lrs {
+
+enum GemvEpilogue : int {
+  EPI_STORE = 0,   // out[b][r] = y (+ bias[r])           LinearLayer::forward, src/model.rs:33-46
+  EPI_ADD = 1,     // out[b][r] += y                      residual adds, src/model.rs:236-238, 258-260
+  EPI_SWIGLU = 2,  // out[b][r] = silu(y_gate) * y_up     src/model.rs:251-254
+  EPI_ARGMAX = 3   // logits (optional) + greedy argmax    src/engine.rs:233-241
+};
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvMaxSeg = 3;
+constexpr int kGemvMaxStages = 4;
+
+// One output segment: rows of one matrix (or of a gate/up pair for EPI_SWIGLU).
+struct GemvSeg {
+  const uint8_t* w;   // device block bytes, [rows][rb]
+  const uint8_t* w2;  // second matrix of a pair (EPI_SWIGLU), same type and shape
+  const float* bias;  // [rows] or null
+  float* out;         // out[b * out_ld + r]
+  int type, rows, rb, rt, tiles, tile0, out_ld;
+};
+
+struct GemvParams {
+  GemvSeg seg[kGemvMaxSeg];
+  int nseg, total_tiles, cols, epi;
+  const float* x;    // x[b * x_ld + c]
+  int x_ld, batch;
+  const float* norm_w;  // fused RMSNorm of x (batch 1 only) or null
+  float norm_eps;
+  unsigned long long* argmax_keys;  // [batch], EPI_ARGMAX
+  int stage_bytes, stages, x_in_smem;
+  int* error_flag;
+};
+
+// Host helpers (gemv.cu).
+struct GemvMat {
+  const uint8_t* w;
+  const uint8_t* w2;
+  const float* bias;
+  float* out;
+  uint32_t type;
+  int rows, cols, out_ld;
+};
+// Fills the tiling of `params` for the given segments; returns 0 or an lrs status.
+int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch);
+// Launches on `stream` (with programmatic dependent launch when pdl != 0).
+cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl);
+
+}  // namespace lrs
