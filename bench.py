@@ -1,0 +1,377 @@
+#!/usr/bin/env python
+"""Decode throughput of llama.rs's Qwen2 token loop on B200.
+
+Workload (default --config c3): the Qwen2.5-7B-shape model (seed 2, q4km),
+64 independent sequences, each a 1024-token uniform prompt followed by greedy
+decoding, context 4096; the sequences are split data-parallel over the ranks
+(one process per GPU, no collective on the data path).  A "step" is one greedy
+decode step of every local sequence; `value` is decode tokens/s over all ranks
+(device time, CUDA events, max over ranks), `e2e` the same through the public
+C-ABI call with host buffers (token ids in, token ids out, every step).
+
+Also reported: batch-1 decode on the same model (the north-star target), the
+prefill rate, the GEMV roofline (per-launch CUDA events inside the run), the
+SM clocks seen during the timed region, and the reference CPU path (the C++
+restatement of the reference AVX2 backend, oracle/) timed on the host cores.
+
+`--impl reference` times only that CPU path, on the same workload and metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def load_pkg():
+    import importlib.util
+    if "llamars_b200" in sys.modules:
+        return sys.modules["llamars_b200"]
+    pkg = os.path.join(ROOT, "llama.rs_b200")
+    spec = importlib.util.spec_from_file_location(
+        "llamars_b200", os.path.join(pkg, "__init__.py"), submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["llamars_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # CPU baseline leg only
+    return oracle
+
+
+WORKLOADS = {
+    "c3": dict(cfg="config_c3", seed=2, recipe="Q4KM", seqs=64, prompt=1024, decode=256, ctx=4096,
+               model="Qwen2.5-7B-shape", quant="q4km"),
+    "c2": dict(cfg="config_c2", seed=1, recipe="Q4K", seqs=1, prompt=512, decode=128, ctx=4096,
+               model="Qwen2.5-1.5B-shape", quant="q4k"),
+    "c0": dict(cfg="config_c0", seed=0, recipe="Q4KM", seqs=1, prompt=128, decode=32, ctx=4096,
+               model="Qwen2.5-0.5B-shape", quant="q4km"),
+}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index):
+        self.idx = phys_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)], stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def launches_per_step(layers, batch):
+    # embed, per layer [rmsnorm] qkv rope_store attn combine o [rmsnorm] gate_up down,
+    # then [rmsnorm] lm_head advance
+    per_layer = 7 + (2 if batch > 1 else 0)
+    return 1 + layers * per_layer + (2 if batch == 1 else 3)
+
+
+def build_model(lrs, wl, threads=0):
+    cfg = getattr(lrs, wl["cfg"])()
+    return cfg, lrs.SynthModel(cfg, wl["seed"], lrs.LoadQuantization[wl["recipe"]], threads=threads)
+
+
+def cpu_decode_rate(orc, lrs, sm, cfg, wl, threads, budget_s=15.0):
+    """Reference AVX2 path (oracle port) on the host: tokens/s of greedy decode for one
+    sequence after a 16-token prompt, on a bounded number of steps."""
+    om = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
+    prompt = lrs.prompt_tokens(wl["seed"], 16, cfg.vocab_size)
+    probe = om.benchmark_tokens(prompt, 2)
+    per_tok = max(probe["decode_s"] / 2, 1e-4)
+    n = int(max(2, min(128, budget_s / per_tok)))
+    om2 = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
+    r = om2.benchmark_tokens(prompt, n)
+    return n / r["decode_s"], n
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lrs = load_pkg()  # host-side model construction only (no CUDA call)
+    orc = load_oracle()
+    threads = os.cpu_count() or 1
+    cfg, sm = build_model(lrs, wl, threads)
+    prompt = lrs.prompt_tokens(wl["seed"], 16, cfg.vocab_size)
+    om2 = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
+    om2.prefill(prompt)
+    tok = orc.argmax(om2.forward_token(int(prompt[-1]), len(prompt) - 1))
+    pos = len(prompt)
+    for _ in range(args.warmup):
+        tok = orc.argmax(om2.forward_token(tok, pos))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = orc.argmax(om2.forward_token(tok, pos))
+        pos += 1
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    sample = (f"1 sequence (the reference has no batching), 16-token prompt, {args.warmup} warm-up "
+              f"+ {args.steps} timed greedy decode steps")
+    line = {
+        "impl": "reference", "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and ids)",
+        "config": {"workload": f"{wl['model']} {wl['quant']} greedy decode", "kernel": "avx2",
+                   "threads": threads},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample + "; C++ restatement of the reference AVX2 backend "
+                                            "(src/simd.rs) -- the Rust reference cannot be built "
+                                            "here (no cargo)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, wl):
+    import torch
+    lrs = load_pkg()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    total_seqs = args.seqs or wl["seqs"]
+    if total_seqs % world:
+        raise SystemExit("sequences must divide evenly over the GPUs")
+    B = total_seqs // world
+    P = args.prompt or wl["prompt"]
+    ncpu = os.cpu_count() or 1
+
+    t_build = time.perf_counter()
+    cfg, sm = build_model(lrs, wl, max(1, ncpu // world))
+    build_s = time.perf_counter() - t_build
+    be = lrs.CudaBackend(local)
+    model = lrs.CudaQwen2Model(be, sm.desc(), max_seq_len=wl["ctx"], max_sequences=B,
+                               kv_bf16=args.kv_bf16)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local))
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    # ---- prefill every local sequence (prompt of P uniform ids) ----
+    prompts = [lrs.prompt_tokens(wl["seed"], P, cfg.vocab_size, rank * B + s) for s in range(B)]
+    firsts = []
+    p0, p1 = ev(), ev()
+    p0.record(ext)
+    for s in range(B):
+        _, f = model.prefill(prompts[s], 0, seq=s, want_logits=False)
+        firsts.append(f)
+    p1.record(ext)
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
+    seqs = list(range(B))
+    pos = [P] * B
+
+    # ---- warm-up (W greedy steps, graph captured on the first) ----
+    out = model.decode_greedy(firsts, pos, args.warmup, seqs)
+    firsts = out[-1].tolist()
+    pos = [p + args.warmup for p in pos]
+
+    # ---- timed region: K device-resident greedy steps ----
+    phys = local
+    if os.environ.get("CUDA_VISIBLE_DEVICES"):
+        phys = os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]
+    clocks = ClockSampler(phys)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0, t1 = ev(), ev()
+    t0.record(ext)
+    model.decode_enqueue(firsts, pos, args.steps, seqs)
+    t1.record(ext)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    barrier()
+    step_ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    toks = model.read_tokens(B, args.steps)
+    firsts = toks[-1].tolist()
+    pos = [p + args.steps for p in pos]
+    value = total_seqs / (step_ms / 1e3)
+
+    # ---- e2e: the public C-ABI call per step, host token ids in and out ----
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record(ext)
+    for _ in range(args.steps):
+        out = model.decode_greedy(firsts, pos, 1, seqs)
+        firsts = out[0].tolist()
+        pos = [p + 1 for p in pos]
+    e1.record(ext)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    e2e_value = total_seqs / (e2e_ms / 1e3)
+
+    # ---- GEMV roofline: one step with per-launch CUDA events ----
+    gemv_ms, gemv_n, prof_step_ms = model.profile_step(firsts, pos, seqs)
+    gemv_ms = max_over_ranks(gemv_ms)
+    wbytes = model.weight_bytes()
+    hbm, peak_kind = peaks()
+    achieved = wbytes / (gemv_ms / 1e3) / 1e9
+    pos = [p + 1 for p in pos]
+
+    # ---- batch-1 decode on the same model (sequence 0) ----
+    b1 = None
+    if not args.no_b1:
+        model.decode_greedy([firsts[0]], [pos[0]], 3, [0])
+        q0, q1 = ev(), ev()
+        q0.record(ext)
+        model.decode_enqueue([firsts[0]], [pos[0] + 3], args.steps, [0])
+        q1.record(ext)
+        torch.cuda.synchronize()
+        b1_ms = max_over_ranks(q0.elapsed_time(q1)) / args.steps
+        g1, n1, _ = model.profile_step([int(model.read_tokens(1, args.steps)[-1, 0])],
+                                       [pos[0] + 3 + args.steps], [0])
+        g1 = max_over_ranks(g1)
+        b1 = {"decode_tok_s_per_gpu": 1e3 / b1_ms, "ms_per_step": b1_ms,
+              "weight_stream_gbs": wbytes / (b1_ms / 1e3) / 1e9,
+              "weight_stream_frac": wbytes / (b1_ms / 1e3) / 1e9 / hbm,
+              "gemv_gbs": wbytes / (g1 / 1e3) / 1e9, "gemv_frac": wbytes / (g1 / 1e3) / 1e9 / hbm,
+              "gemv_launches": n1}
+
+    # ---- CPU baseline: reference AVX2 path (port) on rank 0 at N=1 ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        orc = load_oracle()
+        rate, n = cpu_decode_rate(orc, lrs, sm, cfg, wl, ncpu)
+        cpu = {"value": rate, "unit": "tok/s", "cores": ncpu, "kind": "port",
+               "sample": f"1 sequence, 16-token prompt then {n} greedy decode steps of the same "
+                         "model; C++ restatement of the reference AVX2 backend (src/simd.rs, "
+                         "row-parallel pool as src/backend.rs:143-162)"}
+
+    if rank == 0:
+        nl = launches_per_step(cfg.num_hidden_layers, B)
+        line = {
+            "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random weights N(0,0.02), uniform prompt ids)",
+            "config": {"workload": f"{wl['model']} {wl['quant']}: {total_seqs} sequences x "
+                                   f"({P} prompt + greedy decode), ctx {wl['ctx']}, "
+                                   f"data-parallel over {world} GPU(s)",
+                       "sequences_per_gpu": B, "prompt": P,
+                       "kv_cache": "bf16" if args.kv_bf16 else "f32",
+                       "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights streamed per step"},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+                    "d2h_bytes_per_step": 4 * B + 4},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "kernel": "gemv_kernel (all GEMV launches of one decode step)",
+                         "bytes_per_launch": wbytes / gemv_n, "ms_per_launch": gemv_ms / gemv_n,
+                         "launches": gemv_n, "peak_kind": peak_kind},
+            "weight_stream_gbs": wbytes / (step_ms / 1e3) / 1e9,
+            "prefill_tok_s": total_seqs * P / (prefill_ms / 1e3),
+            "b1": b1,
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+            "gpu_launches": nl * args.steps,
+            "model_build_s": build_s,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    be.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=48)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--seqs", type=int, default=0, help="total sequences (default: the config's)")
+    ap.add_argument("--prompt", type=int, default=0, help="prompt tokens (default: the config's)")
+    ap.add_argument("--kv-bf16", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--no-b1", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    wl = WORKLOADS[args.config]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

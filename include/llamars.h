@@ -198,8 +198,9 @@ lrs_status lrs_model_prefill(lrs_model* model, uint32_t seq, const uint32_t* tok
 /* The decode half of InferenceEngine::benchmark_tokens (src/engine.rs:189-223)
  * with the argmax on the device: for each of `n_seqs` sequences (slots
  * seqs[i], next input token first_tokens[i] at position start_pos[i]) runs
- * n_steps greedy steps; tokens_out is [n_steps][n_seqs] (the token fed to each
- * step's forward, i.e. the argmax of the previous logits). */
+ * n_steps greedy steps; tokens_out is [n_steps][n_seqs]: row s is the token
+ * step s produced (the argmax of its logits), which the reference loop feeds
+ * to step s + 1. */
 lrs_status lrs_model_decode_greedy(lrs_model* model, size_t n_seqs, const uint32_t* seqs,
                                    const uint32_t* first_tokens, const uint32_t* start_pos,
                                    size_t n_steps, uint32_t* tokens_out);
@@ -212,6 +213,15 @@ lrs_status lrs_model_decode_enqueue(lrs_model* model, size_t n_seqs, const uint3
                                     size_t n_steps);
 lrs_status lrs_model_read_tokens(lrs_model* model, size_t n_seqs, size_t n_steps,
                                  uint32_t* tokens_out);
+
+/* Measurement hook (no counterpart in the reference): runs ONE greedy step for
+ * the given items outside any CUDA graph, with every GEMV launch bracketed by
+ * CUDA events on the model's stream.  Reports the summed GEMV time, the number
+ * of GEMV launches and the whole step's time (milliseconds).  The step writes
+ * the KV cache at `pos` like a normal decode step. */
+lrs_status lrs_model_profile_step(lrs_model* model, size_t n_seqs, const uint32_t* seqs,
+                                  const uint32_t* tokens, const uint32_t* pos, float* gemv_ms,
+                                  uint32_t* gemv_launches, float* step_ms);
 
 /* Device stream (cudaStream_t) the model and backend queue work on. */
 void* lrs_backend_stream(lrs_backend* backend);

@@ -178,6 +178,7 @@ _sig("lrs_model_decode_greedy", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c
 _sig("lrs_model_decode_enqueue", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c_size_t)
 _sig("lrs_model_read_tokens", C.c_int32, _P, C.c_size_t, C.c_size_t, _U32)
 _sig("lrs_model_weight_bytes", C.c_uint64, _P)
+_sig("lrs_model_profile_step", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, _F, _U32, _F)
 _sig("lrs_recipe_type", C.c_uint32, C.c_uint32, C.c_char_p, C.c_size_t, C.c_size_t)
 _sig("lrs_quantize_matrix", C.c_int32, C.c_uint32, _F, C.c_size_t, C.c_size_t, _P, C.c_size_t,
      _U32, C.POINTER(C.c_size_t))
@@ -195,7 +196,7 @@ EXPORTED_SYMBOLS = (
     "lrs_matvec", "lrs_matvec_batched", "lrs_matvec_device", "lrs_model_create",
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
-    "lrs_model_weight_bytes", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
+    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
 )
 
@@ -541,7 +542,7 @@ class CudaQwen2Model:
 
     def decode_greedy(self, first_tokens: Sequence[int], start_pos: Sequence[int], n_steps: int,
                       seqs: Optional[Sequence[int]] = None) -> np.ndarray:
-        """[n_steps, n_seqs] tokens fed to each greedy step (row 0 = first_tokens)."""
+        """[n_steps, n_seqs]: row s = token produced by greedy step s (fed to step s + 1)."""
         ft = np.ascontiguousarray(first_tokens, dtype=np.uint32)
         n = ft.size
         sp = np.ascontiguousarray(start_pos, dtype=np.uint32)
@@ -564,13 +565,27 @@ class CudaQwen2Model:
         _check(_lib.lrs_model_read_tokens(self._h, n_seqs, n_steps, _uptr(out)))
         return out
 
+    def profile_step(self, tokens, pos, seqs=None):
+        """One greedy step outside the graph with per-GEMV CUDA events:
+        returns (gemv_ms, gemv_launches, step_ms)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(pos, dtype=np.uint32)
+        sq = np.ascontiguousarray(seqs if seqs is not None else range(t.size), dtype=np.uint32)
+        g = np.zeros(1, np.float32)
+        n = np.zeros(1, np.uint32)
+        s = np.zeros(1, np.float32)
+        _check(_lib.lrs_model_profile_step(self._h, t.size, _uptr(sq), _uptr(t), _uptr(p),
+                                           _fptr(g), _uptr(n), _fptr(s)))
+        return float(g[0]), int(n[0]), float(s[0])
+
     def benchmark_tokens(self, prompt: Sequence[int], decode_tokens: int, seq: int = 0):
         """InferenceEngine::benchmark_tokens (src/engine.rs:189-223) on the device:
         returns the decode_tokens tokens fed to the decode steps."""
         _, first = self.prefill(prompt, 0, seq, want_logits=False)
         if decode_tokens == 0:
             return np.zeros(0, dtype=np.uint32)
-        return self.decode_greedy([first], [len(prompt)], decode_tokens, [seq])[:, 0]
+        produced = self.decode_greedy([first], [len(prompt)], decode_tokens, [seq])[:, 0]
+        return np.concatenate([[first], produced[:-1]]).astype(np.uint32)
 
 
 # ------------------------------------------------------ benchmark configs --
@@ -594,6 +609,10 @@ def config_c4() -> LlamaConfig:
     return LlamaConfig(5120, 27648, 40, 8, 64, 152064, 1e-6, 1e6, 32768, 128, False)
 
 
-def prompt_tokens(seed: int, n: int, vocab: int) -> np.ndarray:
-    """Uniform prompt token ids of the benchmark workloads (numpy PCG64, seed + 1000)."""
-    return np.random.default_rng(seed + 1000).integers(0, vocab, n, dtype=np.int64).astype(np.uint32)
+def prompt_tokens(seed: int, n: int, vocab: int, sequence: int = 0) -> np.ndarray:
+    """Uniform prompt token ids of the benchmark workloads (numpy PCG64).
+
+    Sequence 0 uses seed + 1000; sequence g > 0 of a multi-sequence workload
+    uses the seed sequence [seed, g]."""
+    rng = np.random.default_rng(seed + 1000 if sequence == 0 else [seed, sequence])
+    return rng.integers(0, vocab, n, dtype=np.int64).astype(np.uint32)

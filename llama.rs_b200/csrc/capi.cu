@@ -340,6 +340,8 @@ struct lrs_model {
   size_t tokens_out_cap = 0;  // in elements
   std::map<GraphKey, cudaGraphExec_t> graphs;
   uint64_t weight_bytes = 0;
+  // When set, every GEMV launch of enqueue_step is bracketed by two events.
+  std::vector<cudaEvent_t>* prof = nullptr;
 };
 
 namespace {
@@ -349,6 +351,19 @@ int32_t model_alloc(lrs_model* m, void** p, size_t bytes) {
     return fail(LRS_ERR_OOM, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
   m->allocs.push_back(*p);
   return LRS_OK;
+}
+
+cudaError_t model_gemv(lrs_model* m, const GemvParams& p, cudaStream_t st, int sms) {
+  if (!m->prof) return gemv_launch(p, st, sms, true);
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  m->prof->push_back(a);
+  m->prof->push_back(b);
+  cudaEventRecord(a, st);
+  cudaError_t e = gemv_launch(p, st, sms, false);
+  cudaEventRecord(b, st);
+  return e;
 }
 
 int32_t upload_vec(lrs_model* m, const float* h, size_t n, float** out) {
@@ -427,7 +442,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->xn;
     }
     p.x_ld = h;
-    LRS_CUDA(gemv_launch(p, st, sms, true));
+    LRS_CUDA(model_gemv(m, p, st, sms));
     // RoPE + KV store (src/model.rs:188-205), attention (:206-231)
     LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
                                L.kpool, L.vpool, kv_bf16, st));
@@ -439,7 +454,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     p.error_flag = m->be->d_err;
     p.x = m->att;
     p.x_ld = h;
-    LRS_CUDA(gemv_launch(p, st, sms, true));
+    LRS_CUDA(model_gemv(m, p, st, sms));
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
     GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
     if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B))) return rc;
@@ -453,14 +468,14 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->xn;
     }
     p.x_ld = h;
-    LRS_CUDA(gemv_launch(p, st, sms, true));
+    LRS_CUDA(model_gemv(m, p, st, sms));
     // down_proj + residual (src/model.rs:255-260)
     GemvMat dm = mat_of(L.down, m->residual, h);
     if ((rc = gemv_plan(&p, &dm, 1, EPI_ADD, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->act;
     p.x_ld = I;
-    LRS_CUDA(gemv_launch(p, st, sms, true));
+    LRS_CUDA(model_gemv(m, p, st, sms));
   }
   if (lm_item == -2) return LRS_OK;
   // final norm + lm_head (src/model.rs:263-268) fused with the greedy argmax
@@ -480,7 +495,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     p.x = m->xn;
   }
   p.x_ld = h;
-  LRS_CUDA(gemv_launch(p, st, sms, true));
+  LRS_CUDA(model_gemv(m, p, st, sms));
   if (greedy_advance)
     LRS_CUDA(launch_advance(m->keys, m->d_tok, m->d_pos, B, m->d_step, n_steps_cap,
                             m->d_tokens_out, m->d_last, st));
@@ -747,7 +762,7 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
     int32_t rc = ensure_pages(m, sq[i], start_pos[i] + (uint32_t)n_steps - 1);
     if (rc) return rc;
   }
-  // tokens_out: [n_steps][B]; row 0 holds the first tokens.
+  // tokens_out: [n_steps][B]; row s holds the token step s produced.
   size_t need = n_steps * (size_t)B;
   if (need > m->tokens_out_cap) {
     for (auto it = m->graphs.begin(); it != m->graphs.end();) {
@@ -764,7 +779,6 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
   int32_t rc = set_items(m, B, tok.data(), pos.data(), sq.data());
   if (rc) return rc;
   cudaStream_t st = m->be->stream;
-  LRS_CUDA(cudaMemcpyAsync(m->d_tokens_out, first_tokens, B * 4, cudaMemcpyHostToDevice, st));
   LRS_CUDA(cudaMemsetAsync(m->d_step, 0, 4, st));
   const int cap_steps = (int)(m->tokens_out_cap / B);
   if (m->opt.use_graph) {
@@ -801,6 +815,55 @@ lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, ui
   LRS_CUDA(cudaMemcpyAsync(out, m->d_tokens_out, n_seqs * n_steps * 4, cudaMemcpyDeviceToHost,
                            m->be->stream));
   LRS_CUDA(cudaStreamSynchronize(m->be->stream));
+  return check_device_error(m->be);
+}
+
+lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
+                                  const uint32_t* tokens, const uint32_t* pos, float* gemv_ms,
+                                  uint32_t* gemv_launches, float* step_ms) {
+  if (!m || !seqs || !tokens || !pos) return fail(LRS_ERR_INVALID, "null argument");
+  if (n_seqs == 0 || n_seqs > (size_t)m->max_items) return fail(LRS_ERR_INVALID, "n_seqs out of range");
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  const int B = (int)n_seqs;
+  std::vector<int> tok(B), ps(B), sq(B);
+  for (int i = 0; i < B; i++) {
+    if (seqs[i] >= m->opt.max_sequences || tokens[i] >= m->c.vocab_size ||
+        pos[i] >= m->opt.max_seq_len)
+      return fail(LRS_ERR_INVALID, "profile_step: item out of range");
+    tok[i] = (int)tokens[i];
+    ps[i] = (int)pos[i];
+    sq[i] = (int)seqs[i];
+    int32_t rc = ensure_pages(m, sq[i], pos[i]);
+    if (rc) return rc;
+  }
+  int32_t rc = set_items(m, B, tok.data(), ps.data(), sq.data());
+  if (rc) return rc;
+  cudaStream_t st = m->be->stream;
+  std::vector<cudaEvent_t> ev;
+  cudaEvent_t s0, s1;
+  cudaEventCreate(&s0);
+  cudaEventCreate(&s1);
+  cudaEventRecord(s0, st);
+  m->prof = &ev;
+  rc = enqueue_step(m, B, -1, false, true, 0);
+  m->prof = nullptr;
+  cudaEventRecord(s1, st);
+  cudaError_t e = cudaStreamSynchronize(st);
+  float total = 0.0f, step = 0.0f;
+  for (size_t i = 0; i + 1 < ev.size(); i += 2) {
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+    total += t;
+  }
+  cudaEventElapsedTime(&step, s0, s1);
+  for (auto x : ev) cudaEventDestroy(x);
+  cudaEventDestroy(s0);
+  cudaEventDestroy(s1);
+  if (rc) return rc;
+  if (e != cudaSuccess) return fail(LRS_ERR_CUDA, cudaGetErrorString(e));
+  if (gemv_ms) *gemv_ms = total;
+  if (gemv_launches) *gemv_launches = (uint32_t)(ev.size() / 2);
+  if (step_ms) *step_ms = step;
   return check_device_error(m->be);
 }
 

@@ -292,7 +292,7 @@ __global__ void advance_kernel(const unsigned long long* keys, int* tok, int* po
     tok[b] = (int)t;
     pos[b] += 1;
     if (last) last[b] = t;
-    if (tokens_out && s + 1 < n_steps) tokens_out[(size_t)(s + 1) * batch + b] = t;
+    if (tokens_out && s < n_steps) tokens_out[(size_t)s * batch + b] = t;
   }
   __syncthreads();
   if (threadIdx.x == 0) *step = s + 1;

@@ -39,7 +39,7 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
                              const void* kpool, const void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
-// tokens_out[(step + 1) * B + b] = argmax while step + 1 < n_steps; step += 1.
+// tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
 cudaError_t launch_advance(const unsigned long long* keys, int* tok, int* pos, int batch,
                            int* step, int n_steps, uint32_t* tokens_out, uint32_t* last,
                            cudaStream_t st);

@@ -23,7 +23,10 @@ def _run_pair(lrs, orc, backend, cfg, recipe, seed, n_prompt, n_decode, max_seq=
         prompt, n_decode, keep_logits=True)
     model = lrs.CudaQwen2Model(backend, sm.desc(), max_seq_len=max_seq, kv_bf16=kv_bf16)
     logits, first = model.prefill(prompt, 0)
-    toks = model.decode_greedy([first], [n_prompt], n_decode)[:, 0] if n_decode else []
+    toks = []
+    if n_decode:  # tokens fed to each decode step: the prefill argmax, then each step's argmax
+        produced = model.decode_greedy([first], [n_prompt], n_decode)[:, 0]
+        toks = np.concatenate([[first], produced[:-1]])
     return sm, model, prompt, ref, logits, first, np.asarray(toks)
 
 
@@ -70,9 +73,10 @@ def test_batched_sequences_match_single(lrs, orc, backend):
         _, f = m.prefill(prompt, 0, seq=s)
         firsts.append(f)
         refs.append(orc.OracleModel(sm.desc(), 512).benchmark_tokens(prompt, n_dec))
-    toks = m.decode_greedy(firsts, [n_prompt + s for s in range(B)], n_dec, list(range(B)))
+    produced = m.decode_greedy(firsts, [n_prompt + s for s in range(B)], n_dec, list(range(B)))
+    fed = np.concatenate([np.array(firsts, np.uint32)[None, :], produced[:-1]], axis=0)
     for s in range(B):
-        _assert_tokens(refs[s], toks[:, s])
+        _assert_tokens(refs[s], fed[:, s])
 
 
 def test_kv_bf16_option_runs(lrs, orc, backend):
