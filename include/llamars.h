@@ -107,6 +107,21 @@ lrs_status lrs_matvec(lrs_backend* backend, const lrs_tensor* weight, const floa
 lrs_status lrs_matvec_batched(lrs_backend* backend, const lrs_tensor* weight, const float* in,
                               size_t batch, size_t n_in, float* out, size_t n_out);
 
+/* lrs_matvec for callers that cannot allocate device memory.  This entry point
+ * has no counterpart in the reference.  lrs_matvec stages the host vectors
+ * through device buffers it cudaMalloc's on first use; callers that run on a
+ * device-memory budget fixed at start-up, or that must not let a call trigger
+ * cudaMalloc's device-wide synchronization, call this instead: it stages
+ * through one fixed-size __device__ array built into the library (1.25 MiB,
+ * held by every GPU that loads the library until exit) and allocates nothing.
+ * Limits: cols <= 65536, rows <= 262144 (larger matrices: LRS_ERR_INVALID).
+ * The first call on a device looks up the array's address there; make it
+ * before any stream capture.  All calls on a device share the array: calls
+ * whose GPU work overlaps race, so callers on several threads must serialize
+ * them.  Synchronous; same validation and results as lrs_matvec. */
+lrs_status lrs_matvec_noalloc(lrs_backend* backend, const lrs_tensor* weight, const float* in,
+                              size_t n_in, float* out, size_t n_out);
+
 /* Device-pointer form of lrs_matvec_batched: `d_in` / `d_out` are device
  * addresses, the work is queued on `stream` (a cudaStream_t, NULL = the
  * backend's stream) and the call returns without synchronizing. */

@@ -166,6 +166,7 @@ _sig("lrs_tensor_device_ptr", _P, _P)
 _sig("lrs_dequantize_rows", C.c_int32, _P, _P, C.c_size_t, C.c_size_t, _F)
 _sig("lrs_matvec", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_batched", C.c_int32, _P, _P, _F, C.c_size_t, C.c_size_t, _F, C.c_size_t)
+_sig("lrs_matvec_noalloc", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_device", C.c_int32, _P, _P, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
 _sig("lrs_model_create", C.c_int32, _P, C.POINTER(_ModelDesc), C.POINTER(_ModelOptions),
      C.POINTER(_P))
@@ -193,7 +194,8 @@ EXPORTED_SYMBOLS = (
     "lrs_last_error", "lrs_type_geometry", "lrs_backend_create", "lrs_backend_destroy",
     "lrs_backend_name", "lrs_backend_threads", "lrs_backend_synchronize", "lrs_backend_stream",
     "lrs_tensor_upload", "lrs_tensor_free", "lrs_tensor_device_ptr", "lrs_dequantize_rows",
-    "lrs_matvec", "lrs_matvec_batched", "lrs_matvec_device", "lrs_model_create",
+    "lrs_matvec", "lrs_matvec_noalloc", "lrs_matvec_batched", "lrs_matvec_device",
+    "lrs_model_create",
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
     "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",

@@ -19,6 +19,7 @@
 #include "common.h"
 #include "decode.cuh"
 #include "gemv.cuh"
+#include "internal.h"
 
 namespace lrs {
 thread_local std::string g_last_error;
@@ -37,28 +38,6 @@ using namespace lrs;
     if (e_ != cudaSuccess)                                                                  \
       return fail(LRS_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));        \
   } while (0)
-
-struct lrs_backend {
-  int device = 0;
-  int sms = 148;
-  cudaStream_t stream = nullptr;
-  int* d_err = nullptr;
-  float* d_x = nullptr;
-  float* d_y = nullptr;
-  size_t x_cap = 0, y_cap = 0;
-};
-
-struct DevTensor {
-  uint8_t* d = nullptr;
-  size_t nbytes = 0;
-  int rows = 0, cols = 0;
-  uint32_t type = 0;
-};
-
-struct lrs_tensor {
-  lrs_backend* be = nullptr;
-  DevTensor t;
-};
 
 namespace {
 

@@ -1,0 +1,28 @@
+// internal.h -- handle types shared by the C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+struct lrs_backend {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  float* d_x = nullptr;
+  float* d_y = nullptr;
+  size_t x_cap = 0, y_cap = 0;
+};
+
+struct DevTensor {
+  uint8_t* d = nullptr;
+  size_t nbytes = 0;
+  int rows = 0, cols = 0;
+  uint32_t type = 0;
+};
+
+struct lrs_tensor {
+  lrs_backend* be = nullptr;
+  DevTensor t;
+};
