@@ -351,6 +351,62 @@ def run_ours(args, wl):
         torch.distributed.destroy_process_group()
 
 
+SWEEP_SHAPES = ["4864x896", "896x4864", "18944x3584", "3584x18944", "152064x3584"]
+SWEEP_TYPES = ["F16", "BF16", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K"]
+
+
+def run_gemv_sweep(args):
+    """GB/s of the quantized GEMV per type, shape and batch.
+
+    W ~ N(0, 0.02) quantized on the host, x ~ N(0, 1); each cell times `iters`
+    back-to-back launches with CUDA events after 3 warm-up launches.  Shapes
+    smaller than L2 partly run from L2 when repeated; 152064x3584 exceeds L2.
+    Parity of every row is covered by tests/test_gpu_gemv.py."""
+    import torch
+    lrs = load_pkg()
+    be = lrs.CudaBackend(0)
+    ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", 0))
+    hbm, peak_kind = peaks()
+    types = args.types.split(",") if args.types else SWEEP_TYPES
+    shapes = args.shapes.split(",") if args.shapes else SWEEP_SHAPES
+    batches = [int(b) for b in args.batches.split(",")]
+    rng = np.random.default_rng(0)
+    cells = []
+    for shape in shapes:
+        rows, cols = (int(v) for v in shape.split("x"))
+        v = rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02)
+        for qt in types:
+            t = lrs.QuantTensor.quantize(v, rows, cols, lrs.QuantType[qt])
+            if t.quant_type != lrs.QuantType[qt]:
+                cells.append({"type": qt, "shape": shape, "skipped":
+                              f"cols % block != 0 (the reference falls back to {t.quant_type.name})"})
+                continue
+            be.upload(t)
+            for b in batches:
+                x = torch.randn(b, cols, device="cuda", dtype=torch.float32)
+                y = torch.empty(b, rows, device="cuda", dtype=torch.float32)
+                torch.cuda.synchronize()
+                for _ in range(3):
+                    be.matvec_device(t, x.data_ptr(), b, y.data_ptr())
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(ext)
+                for _ in range(args.iters):
+                    be.matvec_device(t, x.data_ptr(), b, y.data_ptr())
+                e1.record(ext)
+                torch.cuda.synchronize()
+                be.synchronize()
+                ms = e0.elapsed_time(e1) / args.iters
+                nbytes = t.data.size + b * (cols + rows) * 4
+                gbs = nbytes / (ms / 1e3) / 1e9
+                cells.append({"type": qt, "shape": shape, "batch": b, "us": round(ms * 1e3, 2),
+                              "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                              "weight_mb": round(t.data.size / 1e6, 2)})
+            be.release(t)
+    print(json.dumps({"metric": "gemv_sweep", "peak_gbs": hbm, "peak_kind": peak_kind,
+                      "cells": cells}), flush=True)
+    be.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -363,9 +419,17 @@ def main():
     ap.add_argument("--kv-bf16", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
+    ap.add_argument("--gemv-sweep", action="store_true", help="BASELINE config 1 GEMV sweep")
+    ap.add_argument("--types", default="")
+    ap.add_argument("--shapes", default="")
+    ap.add_argument("--batches", default="1,8,64")
+    ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.gemv_sweep:
+        run_gemv_sweep(args)
+        return
     wl = WORKLOADS[args.config]
     if args.impl == "reference":
         run_reference(args, wl)

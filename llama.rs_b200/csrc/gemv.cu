@@ -22,10 +22,12 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.h"
 #include "device_common.cuh"
 #include "gemv.cuh"
+#include "gemv_fast.cuh"
 
 namespace lrs {
 namespace {
@@ -278,30 +280,225 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   }
 }
 
-struct KernelInfo {
-  int smem = -1, blocks = 0;
-};
+// ---- batch-1 kernel with factored per-type dots ---------------------------
+// Work item = (block of rr rows, one piece): the piece's x values are read
+// from shared memory once and applied to rr rows (and to both matrices of a
+// gate/up pair), which keeps shared-memory traffic within the SM's budget.
+constexpr int kFastRed = kWarps * 32 * 4 * 2;  // red[warp][lane][k<4] x 2 matrices
 
-template <int NB, bool PAIR>
-int occupancy(int smem) {
+__host__ __device__ inline int fast_stage_offset() { return (64 + kFastRed * 4 + 127) & ~127; }
+
+template <int T, bool PAIR>
+__device__ void fast_tile(const GemvParams& p, const GemvSeg& s, int tile, const uint8_t* stage,
+                          const float* xs, const float* xs8, float* red) {
+  using BT = BlockTraits<T>;
+  constexpr int PV = fast::Piece<T>::kValues;
+  constexpr int PPU = fast::pieces_per_unit<T>();
+  constexpr int NRUN = PV / 8;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rt = s.rt, R = s.rr, nrb = rt / R;
+  const int r0 = (tile - s.tile0) * rt;
+  const int nr = min(rt, s.rows - r0);
+  const size_t off = (size_t)r0 * s.rb;
+  const int mis = (int)(off & 15);
+  const uint8_t* st = stage + mis;
+  const uint8_t* st2 = stage + round16(mis + nr * s.rb) + mis;
+  const int rbi = tid % nrb;
+  const int ppr = p.cols / PV;
+  const int pstep = kGemvThreads / nrb;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int pc = tid / nrb; pc < ppr; pc += pstep) {
+    const int unit = pc / PPU, sub = pc % PPU;
+    float x[PV], X[NRUN];
+#pragma unroll
+    for (int r = 0; r < NRUN; r++) {
+      const int col = unit * BT::kValues + fast::run_col<T>(sub, r);
+      const float4* q = reinterpret_cast<const float4*>(xs + xs_index(col));
+      const float4 a = q[0], b = q[1];
+      x[8 * r + 0] = a.x, x[8 * r + 1] = a.y, x[8 * r + 2] = a.z, x[8 * r + 3] = a.w;
+      x[8 * r + 4] = b.x, x[8 * r + 5] = b.y, x[8 * r + 6] = b.z, x[8 * r + 7] = b.w;
+      X[r] = xs8[col >> 3];
+    }
+    const size_t uoff = (size_t)unit * BT::kBytes;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      if (k < R) {
+        const int row = rbi * R + k;
+        if (row < nr) {
+          acc[k] += fast::piece_dot<T>(st + (size_t)row * s.rb + uoff, sub, x, X);
+          if constexpr (PAIR)
+            acc2[k] += fast::piece_dot<T>(st2 + (size_t)row * s.rb + uoff, sub, x, X);
+        }
+      }
+    }
+  }
+  // Lanes with the same row block (lane == rbi mod nrb) reduce together.
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    if (k < R) {
+      for (int o = 16; o >= nrb; o >>= 1) {
+        acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
+        if constexpr (PAIR) acc2[k] += __shfl_xor_sync(0xffffffffu, acc2[k], o);
+      }
+      if (lane < nrb) {
+        red[(warp * 32 + lane) * 4 + k] = acc[k];
+        if constexpr (PAIR) red[kWarps * 32 * 4 + (warp * 32 + lane) * 4 + k] = acc2[k];
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float y = 0.0f, y2 = 0.0f;
+    const int r = r0 + tid;
+    if (tid < nr) {
+      const int b = tid / R, k = tid % R;
+      for (int wv = 0; wv < kWarps; wv++) {
+        y += red[(wv * 32 + b) * 4 + k];
+        if constexpr (PAIR) y2 += red[kWarps * 32 * 4 + (wv * 32 + b) * 4 + k];
+      }
+      float* out = s.out ? s.out + r : nullptr;
+      switch (p.epi) {
+        case EPI_STORE:
+          if (s.bias) y += s.bias[r];
+          *out = y;
+          break;
+        case EPI_ADD:
+          *out += y;
+          break;
+        case EPI_SWIGLU:
+          *out = (y / (1.0f + expf(-y))) * y2;
+          break;
+        default:
+          if (out) *out = y;
+          break;
+      }
+    }
+    if (p.epi == EPI_ARGMAX) {
+      unsigned long long key = tid < nr ? argmax_pack(y, (uint32_t)r) : 0ull;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        unsigned long long other = shfl_xor_u64(key, o);
+        key = other > key ? other : key;
+      }
+      if (tid == 0) atomicMax(&p.argmax_keys[0], key);
+    }
+  }
+  __syncthreads();
+}
+
+template <bool PAIR>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    gemv1_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  float* red = reinterpret_cast<float*>(smem + 64);
+  uint8_t* stage_base = smem + fast_stage_offset();
+  float* xs = reinterpret_cast<float*>(stage_base + (size_t)p.stages * p.stage_bytes);
+  float* xs8 = xs + xs_index(p.cols) + 8;
+  const int tid = threadIdx.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; s++) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t policy = evict_first_policy();
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; s++) {
+      int tile = blockIdx.x + s * gridDim.x;
+      if (tile < p.total_tiles) issue_tile(p, tile, stage_base + s * p.stage_bytes, &bars[s], policy);
+    }
+  }
+  pdl_wait();  // x / residual come from the previous kernel
+  if (p.norm_w) {
+    // RMSNorm::forward, src/model.rs:65-73: x * (inv_rms * w)
+    float ss = 0.0f;
+    for (int c = tid; c < p.cols; c += kGemvThreads) ss = fmaf(p.x[c], p.x[c], ss);
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < kWarps; w++) tot += red[w];
+    const float inv = 1.0f / sqrtf(tot / (float)p.cols + p.norm_eps);
+    for (int c = tid; c < p.cols; c += kGemvThreads) xs[xs_index(c)] = p.x[c] * (inv * p.norm_w[c]);
+  } else {
+    for (int c = tid; c < p.cols; c += kGemvThreads) xs[xs_index(c)] = p.x[c];
+  }
+  __syncthreads();
+  for (int j = tid; j < p.cols / 8; j += kGemvThreads) {
+    const float* q = xs + xs_index(j * 8);
+    xs8[j] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+  }
+  __syncthreads();
+
+  int i = 0;
+  for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, i++) {
+    const int s = i % p.stages;
+    const uint32_t parity = (uint32_t)((i / p.stages) & 1);
+    if (tile + (int)gridDim.x >= p.total_tiles) pdl_launch_dependents();
+    if (!mbar_wait_bounded(&bars[s], parity)) {
+      if (tid == 0) {
+        atomicExch(p.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+        for (int k = 1; k < p.stages; k++) {  // let copies already queued land
+          int tk = tile + k * gridDim.x;
+          if (tk >= p.total_tiles) break;
+          mbar_wait_bounded(&bars[(i + k) % p.stages], (uint32_t)(((i + k) / p.stages) & 1));
+        }
+      }
+      return;
+    }
+    const GemvSeg sg = find_seg(p, tile);
+    const uint8_t* stage = stage_base + s * p.stage_bytes;
+    switch (sg.type) {
+      case LRS_GGML_F32: fast_tile<LRS_GGML_F32, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_F16: fast_tile<LRS_GGML_F16, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_BF16: fast_tile<LRS_GGML_BF16, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q4_0: fast_tile<LRS_GGML_Q4_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q4_1: fast_tile<LRS_GGML_Q4_1, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q5_0: fast_tile<LRS_GGML_Q5_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q5_1: fast_tile<LRS_GGML_Q5_1, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q8_0: fast_tile<LRS_GGML_Q8_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q4_K: fast_tile<LRS_GGML_Q4_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q5_K: fast_tile<LRS_GGML_Q5_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+      case LRS_GGML_Q6_K: fast_tile<LRS_GGML_Q6_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
+    }
+    if (tid == 0) {
+      int next = tile + p.stages * gridDim.x;
+      if (next < p.total_tiles) {
+        fence_proxy_async();
+        issue_tile(p, next, stage_base + s * p.stage_bytes, &bars[s], policy);
+      }
+    }
+  }
+}
+
+int fast_piece_values(uint32_t t) {
+  return (t == LRS_GGML_Q4_K || t == LRS_GGML_Q5_K) ? 64 : 32;
+}
+
+size_t fast_smem_bytes(const GemvParams& p) {
+  return fast_stage_offset() + (size_t)p.stages * p.stage_bytes +
+         ((size_t)xs_index(p.cols) + 8 + p.cols / 8) * 4 + 16;
+}
+
+// Resident CTAs per SM of `kernel` at `smem` bytes (cached per device, kernel, size).
+int occupancy(const void* kernel, int smem) {
+  struct Entry {
+    int dev;
+    const void* k;
+    int smem, blocks;
+  };
   static std::mutex mu;
-  static KernelInfo cache[8];
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
   std::lock_guard<std::mutex> g(mu);
   for (auto& c : cache)
-    if (c.smem == smem) return c.blocks;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gemv_kernel<NB, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr = true;
-  }
+    if (c.dev == dev && c.k == kernel && c.smem == smem) return c.blocks;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   int blocks = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, gemv_kernel<NB, PAIR>, kGemvThreads, smem);
-  for (auto& c : cache)
-    if (c.smem < 0) {
-      c.smem = smem;
-      c.blocks = blocks;
-      break;
-    }
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kGemvThreads, smem);
+  cache.push_back({dev, kernel, smem, blocks});
   return blocks;
 }
 
@@ -362,16 +559,58 @@ int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch) 
   if (batch == 1) {
     p->x_in_smem = 1;
     if (smem_bytes(*p, 1) > 227 * 1024) p->x_in_smem = 0;
+    // Factored batch-1 kernel: per segment pick rows per item (rr, the x
+    // reuse factor: 4, or 2 for a gate/up pair) and tile rows rt so that a
+    // tile has >= 224 work items and fits a stage of <= 48 KiB.
+    const int pf = pair ? 2 : 1;
+    GemvParams q = *p;
+    int fneed = 0;
+    tile0 = 0;
+    for (int i = 0; i < nmat; i++) {
+      GemvSeg& s = q.seg[i];
+      const int ppr = cols / fast_piece_values(s.type);
+      int R = pair ? 2 : 4, rt = R;
+      for (;;) {
+        rt = R;
+        while (rt < 32 && (rt / R) * ppr < 224) rt *= 2;
+        while (rt > R && pf * (rt * s.rb + 32) > 48 * 1024) rt /= 2;
+        if (pf * (rt * s.rb + 32) <= 48 * 1024 || R == 1) break;
+        R /= 2;
+      }
+      s.rr = R;
+      s.rt = rt;
+      s.tiles = (s.rows + rt - 1) / rt;
+      s.tile0 = tile0;
+      tile0 += s.tiles;
+      fneed = std::max(fneed, pf * (rt * s.rb + 32));
+    }
+    q.total_tiles = tile0;
+    q.stage_bytes = (fneed + 127) & ~127;
+    const size_t fixed = fast_stage_offset() + ((size_t)xs_index(cols) + 8 + cols / 8) * 4 + 16;
+    q.stages = 4;
+    while (q.stages > 2 && fixed + (size_t)q.stages * q.stage_bytes > 227 * 1024) q.stages--;
+    if (fixed + (size_t)q.stages * q.stage_bytes <= 227 * 1024) {
+      q.fast = 1;
+      *p = q;
+    }
   }
   return LRS_OK;
 }
 
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
   const int nb = gemv_nb(p.batch);
-  const size_t smem = smem_bytes(p, nb);
   const bool pair = p.epi == EPI_SWIGLU;
-  int occ = nb == 1 ? (pair ? occupancy<1, true>((int)smem) : occupancy<1, false>((int)smem))
-                    : (pair ? occupancy<8, true>((int)smem) : occupancy<8, false>((int)smem));
+  const void* kernel;
+  size_t smem;
+  if (p.fast) {
+    kernel = pair ? (const void*)gemv1_kernel<true> : (const void*)gemv1_kernel<false>;
+    smem = fast_smem_bytes(p);
+  } else {
+    smem = smem_bytes(p, nb);
+    kernel = nb == 1 ? (pair ? (const void*)gemv_kernel<1, true> : (const void*)gemv_kernel<1, false>)
+                     : (pair ? (const void*)gemv_kernel<8, true> : (const void*)gemv_kernel<8, false>);
+  }
+  int occ = occupancy(kernel, (int)smem);
   if (occ < 1) occ = 1;
   int grid = std::min(p.total_tiles, num_sms * occ);
   if (grid < 1) return cudaSuccess;
@@ -385,11 +624,8 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (nb == 1)
-    return pair ? cudaLaunchKernelEx(&cfg, gemv_kernel<1, true>, p)
-                : cudaLaunchKernelEx(&cfg, gemv_kernel<1, false>, p);
-  return pair ? cudaLaunchKernelEx(&cfg, gemv_kernel<8, true>, p)
-              : cudaLaunchKernelEx(&cfg, gemv_kernel<8, false>, p);
+  void* args[] = {const_cast<GemvParams*>(&p)};
+  return cudaLaunchKernelExC(&cfg, kernel, args);
 }
 
 }  // namespace lrs

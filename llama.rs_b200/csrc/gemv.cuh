@@ -23,6 +23,7 @@ struct GemvSeg {
   const float* bias;  // [rows] or null
   float* out;         // out[b * out_ld + r]
   int type, rows, rb, rt, tiles, tile0, out_ld;
+  int rr;  // batch-1 kernel: rows per work item (x reuse factor); rt % rr == 0
 };
 
 struct GemvParams {
@@ -34,6 +35,7 @@ struct GemvParams {
   float norm_eps;
   unsigned long long* argmax_keys;  // [batch], EPI_ARGMAX
   int stage_bytes, stages, x_in_smem;
+  int fast;  // 1: batch-1 kernel with factored per-type dots (gemv_fast.cuh)
   int* error_flag;
 };
 
