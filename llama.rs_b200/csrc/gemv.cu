@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -40,6 +41,16 @@ __host__ __device__ inline int stage_offset(int nb) {
   return (64 + red_floats(nb) * 4 + 127) & ~127;
 }
 __host__ __device__ inline int xs_index(int c) { return c + (c >> 5) * 4; }
+// Shared-memory x layout of the direct kernel: one 16-byte pad per 2^S columns,
+// S chosen per type so that the 8 lanes of each quarter-warp phase read x from
+// distinct bank groups (lanes walk consecutive pieces: 64-value pairs for
+// Q4_K/Q5_K, (half, octet) pieces for Q6_K, 32-value blocks otherwise).
+template <int T>
+__host__ __device__ constexpr int xs_shift() {
+  return (T == LRS_GGML_Q4_K || T == LRS_GGML_Q5_K) ? 6 : (T == LRS_GGML_Q6_K ? 7 : 5);
+}
+template <int T>
+__host__ __device__ inline int xs_idx(int c) { return c + ((c >> xs_shift<T>()) << 2); }
 
 // Selects the segment of `tile` with constant indices (a dynamic index into the
 // kernel parameters would force a copy to local memory).
@@ -280,213 +291,278 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   }
 }
 
-// ---- batch-1 kernel with factored per-type dots ---------------------------
-// Work item = (block of rr rows, one piece): the piece's x values are read
-// from shared memory once and applied to rr rows (and to both matrices of a
-// gate/up pair), which keeps shared-memory traffic within the SM's budget.
-constexpr int kFastRed = kWarps * 32 * 4 * 2;  // red[warp][lane][k<4] x 2 matrices
-
-__host__ __device__ inline int fast_stage_offset() { return (64 + kFastRed * 4 + 127) & ~127; }
+// ---- batch-1 kernel: direct loads, int8-split x, dp4a -------------------------
+// x is staged once per CTA in shared memory, per 8-column run r split as
+//     x ~= s_r * (xh + xl / 256),  xh, xl int8,  s_r = max|x_run| / 127,
+// (about 15 bits of x; the dot's error is ~1e-5 relative) together with the
+// exact float sum X_r of the run.  The layout is piece-transposed: 16-byte
+// chunk k of piece p sits at (k * npieces + p) * 16, so the lanes of a warp,
+// which handle consecutive pieces, read consecutive chunks.
+// Each warp then owns groups of R rows (R = 4, or 2 rows of a gate/up pair):
+// lane l walks pieces l, l+32, ... of the group, loads the piece bytes of
+// all its rows straight from global memory (R loads in flight per lane, no
+// staging, no block barrier), multiplies codes by xh and xl with dp4a into
+// exact int32 sums per run, and applies the scales (gemv_fast.cuh).  One warp
+// reduction per row ends the group.  Dense types (F32/F16/BF16) keep float x.
+template <int T>
+struct XLayout {
+  using P = fast::Piece<T>;
+  static constexpr bool kDense = T == LRS_GGML_F32 || T == LRS_GGML_F16 || T == LRS_GGML_BF16;
+  static constexpr int PV = P::kValues;        // values per piece
+  static constexpr int NRUN = PV / 8;          // 8-column runs per piece
+  static constexpr int CH = PV / 16;           // 16-byte chunks of xh (and of xl) per piece
+  // bytes of the staged x for `npieces` pieces
+  __host__ __device__ static size_t bytes(int npieces) {
+    if constexpr (kDense) return (size_t)npieces * PV * 4;
+    return (size_t)npieces * (2 * CH * 16 + NRUN * 8);
+  }
+};
 
 template <int T, bool PAIR>
-__device__ void fast_tile(const GemvParams& p, const GemvSeg& s, int tile, const uint8_t* stage,
-                          const float* xs, const float* xs8, float* red) {
+__global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_constant__ GemvParams p) {
   using BT = BlockTraits<T>;
-  constexpr int PV = fast::Piece<T>::kValues;
-  constexpr int PPU = fast::pieces_per_unit<T>();
-  constexpr int NRUN = PV / 8;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int rt = s.rt, R = s.rr, nrb = rt / R;
-  const int r0 = (tile - s.tile0) * rt;
-  const int nr = min(rt, s.rows - r0);
-  const size_t off = (size_t)r0 * s.rb;
-  const int mis = (int)(off & 15);
-  const uint8_t* st = stage + mis;
-  const uint8_t* st2 = stage + round16(mis + nr * s.rb) + mis;
-  const int rbi = tid % nrb;
-  const int ppr = p.cols / PV;
-  const int pstep = kGemvThreads / nrb;
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int pc = tid / nrb; pc < ppr; pc += pstep) {
-    const int unit = pc / PPU, sub = pc % PPU;
-    float x[PV], X[NRUN];
-#pragma unroll
-    for (int r = 0; r < NRUN; r++) {
-      const int col = unit * BT::kValues + fast::run_col<T>(sub, r);
-      const float4* q = reinterpret_cast<const float4*>(xs + xs_index(col));
-      const float4 a = q[0], b = q[1];
-      x[8 * r + 0] = a.x, x[8 * r + 1] = a.y, x[8 * r + 2] = a.z, x[8 * r + 3] = a.w;
-      x[8 * r + 4] = b.x, x[8 * r + 5] = b.y, x[8 * r + 6] = b.z, x[8 * r + 7] = b.w;
-      X[r] = xs8[col >> 3];
-    }
-    const size_t uoff = (size_t)unit * BT::kBytes;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      if (k < R) {
-        const int row = rbi * R + k;
-        if (row < nr) {
-          acc[k] += fast::piece_dot<T>(st + (size_t)row * s.rb + uoff, sub, x, X);
-          if constexpr (PAIR)
-            acc2[k] += fast::piece_dot<T>(st2 + (size_t)row * s.rb + uoff, sub, x, X);
-        }
-      }
-    }
-  }
-  // Lanes with the same row block (lane == rbi mod nrb) reduce together.
-#pragma unroll
-  for (int k = 0; k < 4; k++) {
-    if (k < R) {
-      for (int o = 16; o >= nrb; o >>= 1) {
-        acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
-        if constexpr (PAIR) acc2[k] += __shfl_xor_sync(0xffffffffu, acc2[k], o);
-      }
-      if (lane < nrb) {
-        red[(warp * 32 + lane) * 4 + k] = acc[k];
-        if constexpr (PAIR) red[kWarps * 32 * 4 + (warp * 32 + lane) * 4 + k] = acc2[k];
-      }
-    }
-  }
-  __syncthreads();
-  if (tid < 32) {
-    float y = 0.0f, y2 = 0.0f;
-    const int r = r0 + tid;
-    if (tid < nr) {
-      const int b = tid / R, k = tid % R;
-      for (int wv = 0; wv < kWarps; wv++) {
-        y += red[(wv * 32 + b) * 4 + k];
-        if constexpr (PAIR) y2 += red[kWarps * 32 * 4 + (wv * 32 + b) * 4 + k];
-      }
-      float* out = s.out ? s.out + r : nullptr;
-      switch (p.epi) {
-        case EPI_STORE:
-          if (s.bias) y += s.bias[r];
-          *out = y;
-          break;
-        case EPI_ADD:
-          *out += y;
-          break;
-        case EPI_SWIGLU:
-          *out = (y / (1.0f + expf(-y))) * y2;
-          break;
-        default:
-          if (out) *out = y;
-          break;
-      }
-    }
-    if (p.epi == EPI_ARGMAX) {
-      unsigned long long key = tid < nr ? argmax_pack(y, (uint32_t)r) : 0ull;
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) {
-        unsigned long long other = shfl_xor_u64(key, o);
-        key = other > key ? other : key;
-      }
-      if (tid == 0) atomicMax(&p.argmax_keys[0], key);
-    }
-  }
-  __syncthreads();
-}
-
-template <bool PAIR>
-__global__ void __launch_bounds__(kGemvThreads, 1)
-    gemv1_kernel(const __grid_constant__ GemvParams p) {
+  using P = fast::Piece<T>;
+  using XL = XLayout<T>;
+  constexpr int NM = PAIR ? 2 : 1;
+  constexpr int R = PAIR ? 2 : 4;
+  constexpr int PV = XL::PV, NRUN = XL::NRUN, CH = XL::CH, NW = P::kWords;
+  constexpr bool kDense = XL::kDense;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  float* red = reinterpret_cast<float*>(smem + 64);
-  uint8_t* stage_base = smem + fast_stage_offset();
-  float* xs = reinterpret_cast<float*>(stage_base + (size_t)p.stages * p.stage_bytes);
-  float* xs8 = xs + xs_index(p.cols) + 8;
-  const int tid = threadIdx.x;
+  float* red = reinterpret_cast<float*>(smem);
+  uint8_t* xq = smem + 128;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int npieces = p.cols / PV;
+  // piece-transposed arrays
+  uint4* xh4 = reinterpret_cast<uint4*>(xq);                      // [CH][npieces]
+  uint4* xl4 = xh4 + (size_t)CH * npieces;                        // [CH][npieces]
+  float* sxa = reinterpret_cast<float*>(xl4 + (size_t)CH * npieces);  // [NRUN][npieces]
+  float* Xa = sxa + (size_t)NRUN * npieces;                       // [NRUN][npieces]
+  float* xf = reinterpret_cast<float*>(xq);                       // dense: [npieces][PV]
 
-  if (tid == 0) {
-    for (int s = 0; s < p.stages; s++) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  const uint64_t policy = evict_first_policy();
-  if (tid == 0) {
-    for (int s = 0; s < p.stages; s++) {
-      int tile = blockIdx.x + s * gridDim.x;
-      if (tile < p.total_tiles) issue_tile(p, tile, stage_base + s * p.stage_bytes, &bars[s], policy);
-    }
-  }
   pdl_wait();  // x / residual come from the previous kernel
+  float inv_rms = 1.0f;
   if (p.norm_w) {
     // RMSNorm::forward, src/model.rs:65-73: x * (inv_rms * w)
     float ss = 0.0f;
     for (int c = tid; c < p.cols; c += kGemvThreads) ss = fmaf(p.x[c], p.x[c], ss);
     for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    if (lane == 0) red[warp] = ss;
     __syncthreads();
     float tot = 0.0f;
     for (int w = 0; w < kWarps; w++) tot += red[w];
-    const float inv = 1.0f / sqrtf(tot / (float)p.cols + p.norm_eps);
-    for (int c = tid; c < p.cols; c += kGemvThreads) xs[xs_index(c)] = p.x[c] * (inv * p.norm_w[c]);
-  } else {
-    for (int c = tid; c < p.cols; c += kGemvThreads) xs[xs_index(c)] = p.x[c];
+    inv_rms = 1.0f / sqrtf(tot / (float)p.cols + p.norm_eps);
   }
-  __syncthreads();
-  for (int j = tid; j < p.cols / 8; j += kGemvThreads) {
-    const float* q = xs + xs_index(j * 8);
-    xs8[j] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
-  }
-  __syncthreads();
-
-  int i = 0;
-  for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, i++) {
-    const int s = i % p.stages;
-    const uint32_t parity = (uint32_t)((i / p.stages) & 1);
-    if (tile + (int)gridDim.x >= p.total_tiles) pdl_launch_dependents();
-    if (!mbar_wait_bounded(&bars[s], parity)) {
-      if (tid == 0) {
-        atomicExch(p.error_flag, LRS_ERR_DEVICE_TIMEOUT);
-        for (int k = 1; k < p.stages; k++) {  // let copies already queued land
-          int tk = tile + k * gridDim.x;
-          if (tk >= p.total_tiles) break;
-          mbar_wait_bounded(&bars[(i + k) % p.stages], (uint32_t)(((i + k) / p.stages) & 1));
+  // One thread per (piece, run): gather the run's 8 values, normalize, split.
+  for (int t = tid; t < npieces * NRUN; t += kGemvThreads) {
+    const int pc = t % npieces, r = t / npieces;
+    const int unit = pc / P::kPieces, sub = pc % P::kPieces;
+    const int col = unit * BT::kValues + P::col(sub, 2 * r);
+    float v[8];
+    const float4 a = *reinterpret_cast<const float4*>(p.x + col);
+    const float4 b = *reinterpret_cast<const float4*>(p.x + col + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    if (p.norm_w) {
+      const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + col);
+      const float4 wb = *reinterpret_cast<const float4*>(p.norm_w + col + 4);
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int c = 0; c < 8; c++) v[c] = v[c] * (inv_rms * w[c]);
+    }
+    if constexpr (kDense) {
+#pragma unroll
+      for (int c = 0; c < 8; c++) xf[(size_t)pc * PV + 8 * r + c] = v[c];
+    } else {
+      float mx = 0.0f, sum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; c++) mx = fmaxf(mx, fabsf(v[c]));
+      sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+      const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+      const float inv = 1.0f / sc;
+      uint32_t hw[2], lw[2];
+#pragma unroll
+      for (int w = 0; w < 2; w++) {
+        hw[w] = lw[w] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float q = v[4 * w + c] * inv;
+          const float h = rintf(q);
+          const float l = fminf(fmaxf(rintf((q - h) * 256.0f), -127.0f), 127.0f);
+          hw[w] |= ((uint32_t)(int)h & 0xffu) << (8 * c);
+          lw[w] |= ((uint32_t)(int)l & 0xffu) << (8 * c);
         }
       }
-      return;
+      // run r = words 2r, 2r+1 of the piece = 8 bytes of chunk r / 2
+      uint32_t* hc = reinterpret_cast<uint32_t*>(xh4 + (size_t)(r >> 1) * npieces + pc) + 2 * (r & 1);
+      uint32_t* lc = reinterpret_cast<uint32_t*>(xl4 + (size_t)(r >> 1) * npieces + pc) + 2 * (r & 1);
+      hc[0] = hw[0], hc[1] = hw[1];
+      lc[0] = lw[0], lc[1] = lw[1];
+      sxa[(size_t)r * npieces + pc] = sc * (1.0f / 256.0f);
+      Xa[(size_t)r * npieces + pc] = sum;
     }
-    const GemvSeg sg = find_seg(p, tile);
-    const uint8_t* stage = stage_base + s * p.stage_bytes;
-    switch (sg.type) {
-      case LRS_GGML_F32: fast_tile<LRS_GGML_F32, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_F16: fast_tile<LRS_GGML_F16, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_BF16: fast_tile<LRS_GGML_BF16, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q4_0: fast_tile<LRS_GGML_Q4_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q4_1: fast_tile<LRS_GGML_Q4_1, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q5_0: fast_tile<LRS_GGML_Q5_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q5_1: fast_tile<LRS_GGML_Q5_1, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q8_0: fast_tile<LRS_GGML_Q8_0, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q4_K: fast_tile<LRS_GGML_Q4_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q5_K: fast_tile<LRS_GGML_Q5_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-      case LRS_GGML_Q6_K: fast_tile<LRS_GGML_Q6_K, PAIR>(p, sg, tile, stage, xs, xs8, red); break;
-    }
-    if (tid == 0) {
-      int next = tile + p.stages * gridDim.x;
-      if (next < p.total_tiles) {
-        fence_proxy_async();
-        issue_tile(p, next, stage_base + s * p.stage_bytes, &bars[s], policy);
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  const int nwarps = gridDim.x * kWarps;
+  for (int g = blockIdx.x * kWarps + warp; g < p.total_tiles; g += nwarps) {
+    const GemvSeg sg = find_seg(p, g);
+    const int r0 = (g - sg.tile0) * R;
+    const int nr = min(R, sg.rows - r0);
+    const uint8_t* base[NM];
+    base[0] = sg.w + (size_t)r0 * sg.rb;
+    if constexpr (PAIR) base[1] = sg.w2 + (size_t)r0 * sg.rb;
+    float acc[NM][R];
+#pragma unroll
+    for (int m = 0; m < NM; m++)
+#pragma unroll
+      for (int r = 0; r < R; r++) acc[m][r] = 0.0f;
+    for (int pc = lane; pc < npieces; pc += 32) {
+      const int unit = pc / P::kPieces, sub = pc % P::kPieces;
+      const size_t uoff = (size_t)unit * BT::kBytes;
+      P pr[NM][R];
+#pragma unroll
+      for (int m = 0; m < NM; m++)
+#pragma unroll
+        for (int r = 0; r < R; r++)  // rows past nr re-read row 0 (discarded)
+          pr[m][r].template load<false>(base[m] + (size_t)(r < nr ? r : 0) * sg.rb + uoff, sub);
+      if constexpr (kDense) {
+        const float4* xp = reinterpret_cast<const float4*>(xf + (size_t)pc * PV);
+        fast::f2 xa[NW], xb[NW];
+#pragma unroll
+        for (int i = 0; i < NW; i++) {
+          const float4 v = xp[i];
+          xa[i] = fast::pk(v.x, v.y);
+          xb[i] = fast::pk(v.z, v.w);
+        }
+#pragma unroll
+        for (int m = 0; m < NM; m++)
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            fast::f2 S0 = 0ull, S1 = 0ull;
+#pragma unroll
+            for (int i = 0; i < NW; i++) {
+              fast::f2 a, b;
+              pr[m][r].weights(i, a, b);
+              fast::fma2(S0, a, xa[i]);
+              fast::fma2(S1, b, xb[i]);
+            }
+            acc[m][r] += fast::hsum2(S0) + fast::hsum2(S1);
+          }
+      } else {
+        uint32_t xh[PV / 4], xl[PV / 4];
+#pragma unroll
+        for (int k = 0; k < CH; k++) {
+          const uint4 h = xh4[(size_t)k * npieces + pc], l = xl4[(size_t)k * npieces + pc];
+          xh[4 * k] = h.x, xh[4 * k + 1] = h.y, xh[4 * k + 2] = h.z, xh[4 * k + 3] = h.w;
+          xl[4 * k] = l.x, xl[4 * k + 1] = l.y, xl[4 * k + 2] = l.z, xl[4 * k + 3] = l.w;
+        }
+        float sx[NRUN], X8[NRUN];
+#pragma unroll
+        for (int r = 0; r < NRUN; r++) {
+          sx[r] = sxa[(size_t)r * npieces + pc];
+          X8[r] = Xa[(size_t)r * npieces + pc];
+        }
+#pragma unroll
+        for (int m = 0; m < NM; m++)
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            float qx[NRUN];
+#pragma unroll
+            for (int u = 0; u < NRUN; u++) {
+              const uint32_t c0 = pr[m][r].icode(2 * u, sub), c1 = pr[m][r].icode(2 * u + 1, sub);
+              int hs = __dp4a((int)c0, (int)xh[2 * u], 0);
+              hs = __dp4a((int)c1, (int)xh[2 * u + 1], hs);
+              int ls = __dp4a((int)c0, (int)xl[2 * u], hs << 8);
+              ls = __dp4a((int)c1, (int)xl[2 * u + 1], ls);
+              qx[u] = sx[u] * (float)ls;
+            }
+            acc[m][r] += pr[m][r].finish_i(qx, X8, sub);
+          }
       }
+    }
+#pragma unroll
+    for (int m = 0; m < NM; m++)
+#pragma unroll
+      for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc[m][r] += __shfl_xor_sync(0xffffffffu, acc[m][r], o);
+    if (lane == 0) {
+      unsigned long long key = 0ull;
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        if (r >= nr) break;
+        const int row = r0 + r;
+        float y = acc[0][r];
+        float* out = sg.out ? sg.out + row : nullptr;
+        switch (p.epi) {
+          case EPI_STORE:
+            if (sg.bias) y += sg.bias[row];
+            *out = y;
+            break;
+          case EPI_ADD:
+            *out += y;
+            break;
+          case EPI_SWIGLU:
+            *out = (y / (1.0f + expf(-y))) * acc[NM - 1][r];
+            break;
+          default: {
+            if (out) *out = y;
+            const unsigned long long k2 = argmax_pack(y, (uint32_t)row);
+            key = k2 > key ? k2 : key;
+          }
+        }
+      }
+      if (p.epi == EPI_ARGMAX) atomicMax(&p.argmax_keys[0], key);
     }
   }
 }
 
-int fast_piece_values(uint32_t t) {
-  return (t == LRS_GGML_Q4_K || t == LRS_GGML_Q5_K) ? 64 : 32;
+size_t fast_x_bytes(uint32_t type, int cols) {
+#define LRS_XB(T) \
+  case T: return XLayout<T>::bytes(cols / XLayout<T>::PV);
+  switch (type) {
+    LRS_XB(LRS_GGML_F32)
+    LRS_XB(LRS_GGML_F16)
+    LRS_XB(LRS_GGML_BF16)
+    LRS_XB(LRS_GGML_Q4_0)
+    LRS_XB(LRS_GGML_Q4_1)
+    LRS_XB(LRS_GGML_Q5_0)
+    LRS_XB(LRS_GGML_Q5_1)
+    LRS_XB(LRS_GGML_Q8_0)
+    LRS_XB(LRS_GGML_Q4_K)
+    LRS_XB(LRS_GGML_Q5_K)
+    LRS_XB(LRS_GGML_Q6_K)
+  }
+#undef LRS_XB
+  return 0;
 }
 
-size_t fast_smem_bytes(const GemvParams& p) {
-  return fast_stage_offset() + (size_t)p.stages * p.stage_bytes +
-         ((size_t)xs_index(p.cols) + 8 + p.cols / 8) * 4 + 16;
+const void* fast_kernel(int type, bool pair) {
+#define LRS_FK(T) \
+  case T: return pair ? (const void*)gemv5_kernel<T, true> : (const void*)gemv5_kernel<T, false>;
+  switch (type) {
+    LRS_FK(LRS_GGML_F32)
+    LRS_FK(LRS_GGML_F16)
+    LRS_FK(LRS_GGML_BF16)
+    LRS_FK(LRS_GGML_Q4_0)
+    LRS_FK(LRS_GGML_Q4_1)
+    LRS_FK(LRS_GGML_Q5_0)
+    LRS_FK(LRS_GGML_Q5_1)
+    LRS_FK(LRS_GGML_Q8_0)
+    LRS_FK(LRS_GGML_Q4_K)
+    LRS_FK(LRS_GGML_Q5_K)
+    LRS_FK(LRS_GGML_Q6_K)
+  }
+#undef LRS_FK
+  return nullptr;
 }
 
 // Resident CTAs per SM of `kernel` at `smem` bytes (cached per device, kernel, size).
-int occupancy(const void* kernel, int smem) {
+int occupancy(const void* kernel, int smem, int threads = kGemvThreads) {
   struct Entry {
     int dev;
     const void* k;
-    int smem, blocks;
+    int smem, blocks, threads;
   };
   static std::mutex mu;
   static std::vector<Entry> cache;
@@ -494,11 +570,11 @@ int occupancy(const void* kernel, int smem) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> g(mu);
   for (auto& c : cache)
-    if (c.dev == dev && c.k == kernel && c.smem == smem) return c.blocks;
+    if (c.dev == dev && c.k == kernel && c.smem == smem && c.threads == threads) return c.blocks;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   int blocks = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kGemvThreads, smem);
-  cache.push_back({dev, kernel, smem, blocks});
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem);
+  cache.push_back({dev, kernel, smem, blocks, threads});
   return blocks;
 }
 
@@ -559,37 +635,23 @@ int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch) 
   if (batch == 1) {
     p->x_in_smem = 1;
     if (smem_bytes(*p, 1) > 227 * 1024) p->x_in_smem = 0;
-    // Factored batch-1 kernel: per segment pick rows per item (rr, the x
-    // reuse factor: 4, or 2 for a gate/up pair) and tile rows rt so that a
-    // tile has >= 224 work items and fits a stage of <= 48 KiB.
-    const int pf = pair ? 2 : 1;
+    // Direct-load batch-1 kernel: groups of 4 rows (2 for a gate/up pair) per warp.
     GemvParams q = *p;
-    int fneed = 0;
+    const int R = pair ? 2 : 4;
     tile0 = 0;
+    bool fits = true;
     for (int i = 0; i < nmat; i++) {
       GemvSeg& s = q.seg[i];
-      const int ppr = cols / fast_piece_values(s.type);
-      int R = pair ? 2 : 4, rt = R;
-      for (;;) {
-        rt = R;
-        while (rt < 32 && (rt / R) * ppr < 224) rt *= 2;
-        while (rt > R && pf * (rt * s.rb + 32) > 48 * 1024) rt /= 2;
-        if (pf * (rt * s.rb + 32) <= 48 * 1024 || R == 1) break;
-        R /= 2;
-      }
-      s.rr = R;
-      s.rt = rt;
-      s.tiles = (s.rows + rt - 1) / rt;
+      s.rt = s.rr = R;
+      s.tiles = (s.rows + R - 1) / R;
       s.tile0 = tile0;
       tile0 += s.tiles;
-      fneed = std::max(fneed, pf * (rt * s.rb + 32));
+      fits = fits && 128 + fast_x_bytes(s.type, cols) <= 200 * 1024;
     }
     q.total_tiles = tile0;
-    q.stage_bytes = (fneed + 127) & ~127;
-    const size_t fixed = fast_stage_offset() + ((size_t)xs_index(cols) + 8 + cols / 8) * 4 + 16;
-    q.stages = 4;
-    while (q.stages > 2 && fixed + (size_t)q.stages * q.stage_bytes > 227 * 1024) q.stages--;
-    if (fixed + (size_t)q.stages * q.stage_bytes <= 227 * 1024) {
+    q.stages = 0;
+    q.stage_bytes = 0;
+    if (fits) {
       q.fast = 1;
       *p = q;
     }
@@ -597,26 +659,13 @@ int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch) 
   return LRS_OK;
 }
 
-cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
-  const int nb = gemv_nb(p.batch);
-  const bool pair = p.epi == EPI_SWIGLU;
-  const void* kernel;
-  size_t smem;
-  if (p.fast) {
-    kernel = pair ? (const void*)gemv1_kernel<true> : (const void*)gemv1_kernel<false>;
-    smem = fast_smem_bytes(p);
-  } else {
-    smem = smem_bytes(p, nb);
-    kernel = nb == 1 ? (pair ? (const void*)gemv_kernel<1, true> : (const void*)gemv_kernel<1, false>)
-                     : (pair ? (const void*)gemv_kernel<8, true> : (const void*)gemv_kernel<8, false>);
-  }
-  int occ = occupancy(kernel, (int)smem);
-  if (occ < 1) occ = 1;
-  int grid = std::min(p.total_tiles, num_sms * occ);
-  if (grid < 1) return cudaSuccess;
+namespace {
+
+cudaError_t launch_cfg(const void* kernel, size_t smem, int grid, int threads,
+                       cudaStream_t stream, bool pdl, const GemvParams& p) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -626,6 +675,47 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
   cfg.numAttrs = 1;
   void* args[] = {const_cast<GemvParams*>(&p)};
   return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
+}  // namespace
+
+cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
+  const bool pair = p.epi == EPI_SWIGLU;
+  if (p.fast) {
+    // Direct-load batch-1 kernel, one launch per run of same-type segments.
+    int i = 0;
+    while (i < p.nseg) {
+      int j = i + 1;
+      while (j < p.nseg && p.seg[j].type == p.seg[i].type) j++;
+      GemvParams q = p;
+      q.nseg = j - i;
+      const int t0 = p.seg[i].tile0;
+      for (int k = 0; k < q.nseg; k++) {
+        q.seg[k] = p.seg[i + k];
+        q.seg[k].tile0 -= t0;
+      }
+      q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
+      const void* kernel = fast_kernel(q.seg[0].type, pair);
+      const size_t smem = 128 + fast_x_bytes(q.seg[0].type, q.cols);
+      const int occ = std::max(1, occupancy(kernel, (int)smem, kGemvThreads));
+      const int grid = std::min((q.total_tiles + kWarps - 1) / kWarps, num_sms * occ);
+      if (grid > 0) {
+        cudaError_t e = launch_cfg(kernel, smem, grid, kGemvThreads, stream, pdl, q);
+        if (e != cudaSuccess) return e;
+      }
+      i = j;
+    }
+    return cudaSuccess;
+  }
+  const int nb = gemv_nb(p.batch);
+  const size_t smem = smem_bytes(p, nb);
+  const void* kernel =
+      nb == 1 ? (pair ? (const void*)gemv_kernel<1, true> : (const void*)gemv_kernel<1, false>)
+              : (pair ? (const void*)gemv_kernel<8, true> : (const void*)gemv_kernel<8, false>);
+  int occ = std::max(1, occupancy(kernel, (int)smem));
+  const int grid = std::min(p.total_tiles, num_sms * occ);
+  if (grid < 1) return cudaSuccess;
+  return launch_cfg(kernel, smem, grid, kGemvThreads, stream, pdl, p);
 }
 
 }  // namespace lrs

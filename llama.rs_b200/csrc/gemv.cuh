@@ -14,7 +14,7 @@ enum GemvEpilogue : int {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxSeg = 3;
-constexpr int kGemvMaxStages = 4;
+constexpr int kGemvMaxStages = 8;
 
 // One output segment: rows of one matrix (or of a gate/up pair for EPI_SWIGLU).
 struct GemvSeg {

@@ -1,16 +1,21 @@
-// gemv_fast.cuh -- factored per-type piece dots for the batch-1 GEMV.
+// gemv_fast.cuh -- per-type piece loaders and factored dots for the batch-1 GEMV.
 //
 // The reference multiplies every dequantized weight by x (dot_row_scalar,
-// src/quant.rs:458-648).  On the GPU that costs ~7 instructions per weight,
-// twice what HBM bandwidth leaves.  These routines compute the same dot in
-// factored form: per group of values sharing a scale,
+// src/quant.rs:458-648), ~7 GPU instructions per weight: twice what HBM
+// bandwidth leaves.  Here the same dot is computed in factored form: per group
+// of values sharing a scale,
 //     sum_k w_k x_k = scale * sum_k q_k x_k + offset * sum_k x_k,
-// where sum_k x_k comes precomputed per 8-column run (xs8) and sum_k q_k x_k is
-// accumulated from codes turned into floats with one byte-permute each:
-// a code q < 128 placed in bits 16..22 of 0x3F000000 is the float
-// f = 0.5 + q/256 exactly, so  sum q x = 256 * sum f x - 128 * sum x.
-// Products accumulate with packed fma.rn.f32x2.  The result agrees with the
-// reference dot to ~1e-6 relative (the parity bar is 1e-3).
+// with sum_k x_k precomputed per 8-column run, and sum_k q_k x_k accumulated
+// from codes turned into floats by one byte-permute each: a code q < 128 in
+// bits 16..22 of 0x3F000000 is the float f = 0.5 + q/256 exactly, so
+//     sum q x = 256 * sum f x - 128 * sum x.
+// Products accumulate with packed fma.rn.f32x2.  Agreement with the reference
+// dot is ~1e-6 relative (the parity bar is 1e-3).
+//
+// A "piece" is the unit one lane handles: 64 values (a group pair) for
+// Q4_K/Q5_K, 32 values otherwise.  load() reads its bytes straight from global
+// memory into registers; code_word(i) yields 4 codes for x columns
+// col(sub, i)..+3; finish() applies the scales.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -35,6 +40,14 @@ __device__ __forceinline__ float hsum2(f2 v) {
 __device__ __forceinline__ void fma2(f2& acc, f2 a, f2 b) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
 }
+// The same product-sum as fma2 with two scalar fma.rn.f32.
+__device__ __forceinline__ void fma1(f2& acc, f2 a, f2 b) {
+  float a0, a1, b0, b1, c0, c1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(b0), "=f"(b1) : "l"(b));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(c0), "=f"(c1) : "l"(acc));
+  acc = pk(fmaf(a0, b0, c0), fmaf(a1, b1, c1));
+}
 __device__ __forceinline__ void add2(f2& acc, f2 a) {
   asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc) : "l"(a));
 }
@@ -42,26 +55,9 @@ __device__ __forceinline__ void add2(f2& acc, f2 a) {
 __device__ __forceinline__ float fq(uint32_t w, int k) {
   return __int_as_float(__byte_perm(w, 0x3F000000u, 0x7044u | ((uint32_t)k << 8)));
 }
-// Byte k of w as the float 2^23 + byte (exact), for signed codes.
+// Byte k of w as the float 2^23 + byte (exact).
 __device__ __forceinline__ float fq23(uint32_t w, int k) {
   return __int_as_float(__byte_perm(w, 0x4B000000u, 0x7650u | (uint32_t)k));
-}
-// sum over 4 codes (bytes of w, each < 128) of f(code) * x[0..3]
-__device__ __forceinline__ void dot4(f2& acc, uint32_t w, const float* x) {
-  fma2(acc, pk(fq(w, 0), fq(w, 1)), pk(x[0], x[1]));
-  fma2(acc, pk(fq(w, 2), fq(w, 3)), pk(x[2], x[3]));
-}
-// Realigned little-endian words of the bytes at p (p 2-byte aligned, shared memory).
-template <int N>
-__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t* w) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* b = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-  const uint32_t sh = (uint32_t)(a & 3) * 8;
-  uint32_t r[N + 1];
-#pragma unroll
-  for (int i = 0; i <= N; i++) r[i] = b[i];
-#pragma unroll
-  for (int i = 0; i < N; i++) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
 }
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return f16_bits((uint16_t)(w & 0xffff)); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return f16_bits((uint16_t)(w >> 16)); }
@@ -70,277 +66,298 @@ __device__ __forceinline__ uint32_t spread4(uint32_t b) {
   return ((b & 15u) * 0x00204081u & 0x01010101u) << 4;
 }
 
-// ---- per-type traits: values per piece, pieces per unit -------------------
+// ---- loads (global with SM = false, shared memory with SM = true) --------
+template <bool SM>
+__device__ __forceinline__ uint32_t ld32(const uint8_t* p) {
+  if constexpr (SM) return *reinterpret_cast<const uint32_t*>(p);
+  uint32_t v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+template <bool SM>
+__device__ __forceinline__ uint4 ld128(const uint8_t* p) {
+  if constexpr (SM) return *reinterpret_cast<const uint4*>(p);
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+template <bool SM>
+__device__ __forceinline__ uint2 ld64(const uint8_t* p) {
+  if constexpr (SM) return *reinterpret_cast<const uint2*>(p);
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+// N little-endian words of the bytes at p (p at least 2-byte aligned).
+template <bool SM, int N>
+__device__ __forceinline__ void ld_words(const uint8_t* p, uint32_t* w) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 2) * 8;
+  uint32_t r[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; i++) r[i] = ld32<SM>(b + 4 * i);
+#pragma unroll
+  for (int i = 0; i < N; i++) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
+}
+
+// ---- per-type pieces -------------------------------------------------------
+// kValues: values per piece; kWords: 4-value code words; kGroups: scale groups.
 template <int T>
-struct Piece {
-  static constexpr int kValues = 32;
+struct Piece;
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1: one 32-value block (src/quant.rs:357-398).
+// Word i < 4: low nibbles of qs bytes 4i..4i+3 (columns 4i..); i >= 4: high
+// nibbles (columns 16 + 4(i-4)..) -- i.e. column 4i for every i.
+template <int T>
+struct Piece32Block {
+  static constexpr int kValues = 32, kWords = 8, kGroups = 1, kPieces = 1;
+  static constexpr bool kFive = T == LRS_GGML_Q5_0 || T == LRS_GGML_Q5_1;
+  static constexpr bool kAffine = T == LRS_GGML_Q4_1 || T == LRS_GGML_Q5_1;
+  float d, m;
+  uint32_t qh, qs[4];
+  template <bool SM>
+  __device__ __forceinline__ void load(const uint8_t* u, int) {
+    if constexpr (T == LRS_GGML_Q4_0) {  // 18 bytes, 2-aligned: d, qs[16]
+      uint32_t w[5];
+      ld_words<SM, 5>(u, w);
+      d = h2f_lo(w[0]);
+#pragma unroll
+      for (int i = 0; i < 4; i++) qs[i] = __funnelshift_r(w[i], w[i + 1], 16);
+    } else if constexpr (T == LRS_GGML_Q4_1) {  // 20 bytes, 4-aligned: d, m, qs[16]
+      const uint32_t h = ld32<SM>(u);
+      d = h2f_lo(h);
+      m = h2f_hi(h);
+#pragma unroll
+      for (int i = 0; i < 4; i++) qs[i] = ld32<SM>(u + 4 + 4 * i);
+    } else if constexpr (T == LRS_GGML_Q5_0) {  // 22 bytes, 2-aligned: d, qh[4], qs[16]
+      uint32_t w[6];
+      ld_words<SM, 6>(u, w);
+      d = h2f_lo(w[0]);
+      qh = __funnelshift_r(w[0], w[1], 16);
+#pragma unroll
+      for (int i = 0; i < 4; i++) qs[i] = __funnelshift_r(w[1 + i], w[2 + i], 16);
+    } else {  // Q5_1: 24 bytes, 8-aligned: d, m, qh[4], qs[16]
+      const uint2 a = ld64<SM>(u), b = ld64<SM>(u + 8), c = ld64<SM>(u + 16);
+      d = h2f_lo(a.x);
+      m = h2f_hi(a.x);
+      qh = a.y;
+      qs[0] = b.x, qs[1] = b.y, qs[2] = c.x, qs[3] = c.y;
+    }
+  }
+  __device__ __forceinline__ static int col(int, int i) { return 4 * i; }
+  __device__ __forceinline__ static int group(int) { return 0; }
+  __device__ __forceinline__ uint32_t icode(int i, int s) const { return code_word(i, s); }
+  // qx[r]: sum over run r (8 columns) of code * x
+  __device__ __forceinline__ float finish_i(const float* qx, const float* X8, int) const {
+    const float xs = (X8[0] + X8[1]) + (X8[2] + X8[3]);
+    const float t = (qx[0] + qx[1]) + (qx[2] + qx[3]);
+    if constexpr (kAffine) return d * t + m * xs;
+    return d * (t - (kFive ? 16.0f : 8.0f) * xs);
+  }
+  __device__ __forceinline__ uint32_t code_word(int i, int) const {
+    const uint32_t q = i < 4 ? (qs[i] & 0x0F0F0F0Fu) : ((qs[i - 4] >> 4) & 0x0F0F0F0Fu);
+    if constexpr (kFive) return q | spread4(qh >> (4 * i));
+    return q;
+  }
+  // xsum: sum of x over the piece's 32 columns
+  __device__ __forceinline__ float finish(const float* S, const float* X8, int) const {
+    const float xs = (X8[0] + X8[1]) + (X8[2] + X8[3]);
+    const float off = kFive ? 16.0f : 8.0f;
+    if constexpr (kAffine) return d * (256.0f * S[0] - 128.0f * xs) + m * xs;
+    return d * (256.0f * S[0] - (128.0f + off) * xs);
+  }
 };
 template <>
-struct Piece<LRS_GGML_Q4_K> {
-  static constexpr int kValues = 64;
+struct Piece<LRS_GGML_Q4_0> : Piece32Block<LRS_GGML_Q4_0> {};
+template <>
+struct Piece<LRS_GGML_Q4_1> : Piece32Block<LRS_GGML_Q4_1> {};
+template <>
+struct Piece<LRS_GGML_Q5_0> : Piece32Block<LRS_GGML_Q5_0> {};
+template <>
+struct Piece<LRS_GGML_Q5_1> : Piece32Block<LRS_GGML_Q5_1> {};
+
+// Q8_0: 34 bytes, 2-aligned: d, qs[32] signed (src/quant.rs:399-402).  Codes
+// are signed: handled by the caller through kSigned.
+template <>
+struct Piece<LRS_GGML_Q8_0> {
+  static constexpr int kValues = 32, kWords = 8, kGroups = 1, kPieces = 1;
+  float d;
+  uint32_t qs[8];
+  template <bool SM>
+  __device__ __forceinline__ void load(const uint8_t* u, int) {
+    uint32_t w[9];
+    ld_words<SM, 9>(u, w);
+    d = h2f_lo(w[0]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) qs[i] = __funnelshift_r(w[i], w[i + 1], 16);
+  }
+  __device__ __forceinline__ static int col(int, int i) { return 4 * i; }
+  __device__ __forceinline__ static int group(int) { return 0; }
+  __device__ __forceinline__ uint32_t code_word(int i, int) const { return qs[i] ^ 0x80808080u; }
+  __device__ __forceinline__ uint32_t icode(int i, int) const { return qs[i]; }  // signed bytes
+  __device__ __forceinline__ float finish_i(const float* qx, const float*, int) const {
+    return d * ((qx[0] + qx[1]) + (qx[2] + qx[3]));
+  }
+  __device__ __forceinline__ float finish(const float* S, const float*, int) const { return d * S[0]; }
 };
-template <>
-struct Piece<LRS_GGML_Q5_K> {
-  static constexpr int kValues = 64;
-};
+
+// Q4_K / Q5_K: piece = group pair p (64 values): d*sc*q - dmin*m
+// (src/quant.rs:403-436).  Word i < 8: low nibbles of qs[32p + 4i ..]
+// (group 2p, columns 4i..); i >= 8: high nibbles (group 2p+1, columns 32 + 4(i-8)..).
 template <int T>
-__host__ __device__ constexpr int pieces_per_unit() {
-  return BlockTraits<T>::kValues / Piece<T>::kValues;
-}
-
-// Column (within the unit) of the 8-wide run r of piece `sub`; the x
-// registers of a piece are run-major, 8 per run.
-template <int T>
-__device__ __forceinline__ int run_col(int sub, int r) {
-  if constexpr (T == LRS_GGML_Q6_K) return (sub >> 2) * 128 + r * 32 + (sub & 3) * 8;
-  else return sub * Piece<T>::kValues + r * 8;
-}
-
-// Contribution of one piece of one row.  u = the unit (block) in shared
-// memory, x = the piece's x values (run-major), X = the piece's 8-run sums.
-template <int T>
-__device__ __forceinline__ float piece_dot(const uint8_t* u, int sub, const float* x,
-                                           const float* X);
-
-// Q4_0: d * (q - 8); sum (q-8) x = 256 S - 136 X   (value_at, src/quant.rs:357-366)
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q4_0>(const uint8_t* u, int, const float* x,
-                                                          const float* X) {
-  uint32_t w[5];
-  load_words<5>(u, w);  // bytes 0..19: d, qs[16]
-  const float d = h2f_lo(w[0]);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16);
-    dot4(s, q & 0x0F0F0F0Fu, x + 4 * i);
-    dot4(s, (q >> 4) & 0x0F0F0F0Fu, x + 16 + 4 * i);
+struct PieceK4 {
+  static constexpr int kValues = 64, kWords = 16, kGroups = 2, kPieces = 4;
+  static constexpr bool kFive = T == LRS_GGML_Q5_K;
+  uint32_t hd[4];  // d|dmin, scales[0..11]
+  uint32_t q[8], h[8];
+  template <bool SM>
+  __device__ __forceinline__ void load(const uint8_t* u, int p) {
+    const uint4 hdr = ld128<SM>(u);
+    hd[0] = hdr.x, hd[1] = hdr.y, hd[2] = hdr.z, hd[3] = hdr.w;
+    const int qs0 = kFive ? 48 : 16;
+    const uint4 a = ld128<SM>(u + qs0 + 32 * p), b = ld128<SM>(u + qs0 + 32 * p + 16);
+    q[0] = a.x, q[1] = a.y, q[2] = a.z, q[3] = a.w, q[4] = b.x, q[5] = b.y, q[6] = b.z,
+    q[7] = b.w;
+    if constexpr (kFive) {
+      const uint4 c = ld128<SM>(u + 16), e = ld128<SM>(u + 32);
+      h[0] = c.x, h[1] = c.y, h[2] = c.z, h[3] = c.w, h[4] = e.x, h[5] = e.y, h[6] = e.z,
+      h[7] = e.w;
+    }
   }
-  const float xs = (X[0] + X[1]) + (X[2] + X[3]);
-  return d * (256.0f * hsum2(s) - 136.0f * xs);
-}
-
-// Q4_1: d * q + m; sum = d (256 S - 128 X) + m X   (src/quant.rs:367-376)
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q4_1>(const uint8_t* u, int, const float* x,
-                                                          const float* X) {
-  const uint32_t* p = reinterpret_cast<const uint32_t*>(u);  // 4-byte aligned (20-byte blocks)
-  const uint32_t h = p[0];
-  const float d = h2f_lo(h), m = h2f_hi(h);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint32_t q = p[1 + i];
-    dot4(s, q & 0x0F0F0F0Fu, x + 4 * i);
-    dot4(s, (q >> 4) & 0x0F0F0F0Fu, x + 16 + 4 * i);
+  __device__ __forceinline__ static int col(int p, int i) { return p * 64 + 4 * i; }
+  __device__ __forceinline__ static int group(int i) { return i >> 3; }
+  __device__ __forceinline__ uint32_t icode(int i, int p) const { return code_word(i, p); }
+  __device__ __forceinline__ float finish_i(const float* qx, const float* X8, int p) const {
+    float S[2];
+    S[0] = ((qx[0] + qx[1]) + (qx[2] + qx[3])) * (1.0f / 256.0f) +
+           0.5f * ((X8[0] + X8[1]) + (X8[2] + X8[3]));
+    S[1] = ((qx[4] + qx[5]) + (qx[6] + qx[7])) * (1.0f / 256.0f) +
+           0.5f * ((X8[4] + X8[5]) + (X8[6] + X8[7]));
+    return finish(S, X8, p);
   }
-  const float xs = (X[0] + X[1]) + (X[2] + X[3]);
-  return d * (256.0f * hsum2(s) - 128.0f * xs) + m * xs;
-}
-
-// Q5_0: d * (q - 16); sum = 256 S - 144 X   (src/quant.rs:377-398)
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q5_0>(const uint8_t* u, int, const float* x,
-                                                          const float* X) {
-  uint32_t w[6];
-  load_words<6>(u, w);  // bytes 0..23: d, qh[4], qs[16]
-  const float d = h2f_lo(w[0]);
-  const uint32_t qh = __funnelshift_r(w[0], w[1], 16);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint32_t q = __funnelshift_r(w[1 + i], w[2 + i], 16);
-    dot4(s, (q & 0x0F0F0F0Fu) | spread4(qh >> (4 * i)), x + 4 * i);
-    dot4(s, ((q >> 4) & 0x0F0F0F0Fu) | spread4(qh >> (16 + 4 * i)), x + 16 + 4 * i);
+  __device__ __forceinline__ uint32_t code_word(int i, int p) const {
+    const int k = i & 7;
+    uint32_t c = i < 8 ? (q[k] & 0x0F0F0F0Fu) : ((q[k] >> 4) & 0x0F0F0F0Fu);
+    if constexpr (kFive) c |= ((h[k] >> (2 * p + (i >> 3))) & 0x01010101u) << 4;
+    return c;
   }
-  const float xs = (X[0] + X[1]) + (X[2] + X[3]);
-  return d * (256.0f * hsum2(s) - 144.0f * xs);
-}
-
-// Q5_1: d * q + m   (src/quant.rs:377-398)
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q5_1>(const uint8_t* u, int, const float* x,
-                                                          const float* X) {
-  const uint32_t* p = reinterpret_cast<const uint32_t*>(u);  // 8-byte aligned (24-byte blocks)
-  const float d = h2f_lo(p[0]), m = h2f_hi(p[0]);
-  const uint32_t qh = p[1];
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint32_t q = p[2 + i];
-    dot4(s, (q & 0x0F0F0F0Fu) | spread4(qh >> (4 * i)), x + 4 * i);
-    dot4(s, ((q >> 4) & 0x0F0F0F0Fu) | spread4(qh >> (16 + 4 * i)), x + 16 + 4 * i);
-  }
-  const float xs = (X[0] + X[1]) + (X[2] + X[3]);
-  return d * (256.0f * hsum2(s) - 128.0f * xs) + m * xs;
-}
-
-// Q8_0: d * q with signed q: byte ^ 0x80 placed under exponent 2^23 gives
-// 2^23 + 128 + q exactly; subtracting 2^23 + 128 recovers q.   (src/quant.rs:399-402)
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q8_0>(const uint8_t* u, int, const float* x,
-                                                          const float*) {
-  uint32_t w[9];
-  load_words<9>(u, w);  // bytes 0..35: d, qs[32]
-  const float d = h2f_lo(w[0]);
-  const f2 bias = pk(-8388736.0f, -8388736.0f);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;
-    f2 a = pk(fq23(q, 0), fq23(q, 1)), b = pk(fq23(q, 2), fq23(q, 3));
-    add2(a, bias);
-    add2(b, bias);
-    fma2(s, a, pk(x[4 * i], x[4 * i + 1]));
-    fma2(s, b, pk(x[4 * i + 2], x[4 * i + 3]));
-  }
-  return d * hsum2(s);
-}
-
-// Q4_K / Q5_K pair piece p (groups 2p, 2p+1): d*sc*q - dmin*m   (src/quant.rs:403-436)
-template <int HIGHBITS>
-__device__ __forceinline__ float k4_pair(const uint8_t* u, int p, const float* x, const float* X) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(u);  // d, dmin, scales[12]
-  const float d = h2f_lo(hdr.x), dmin = h2f_hi(hdr.x);
-  // scale_min_k4 (src/quant.rs:338-347) on scales[0..3] = hdr.y, [4..7] = hdr.z, [8..11] = hdr.w
-  float sc[2], mn[2];
-#pragma unroll
-  for (int k = 0; k < 2; k++) {
-    const int g = 2 * p + k;
-    const int j = g & 3;
-    const uint32_t b0 = (hdr.y >> (8 * j)) & 0xff, b1 = (hdr.z >> (8 * j)) & 0xff;
-    const uint32_t b2 = (hdr.w >> (8 * j)) & 0xff;
-    uint32_t a, b;
-    if (g < 4) {
-      a = b0 & 63;
-      b = b1 & 63;
+  // scale_min_k4 (src/quant.rs:338-347): scales[0..3] = hd[1], [4..7] = hd[2], [8..11] = hd[3].
+  // Group pair p: p < 2 -> groups 2p, 2p+1 < 4; p >= 2 -> both >= 4.
+  __device__ __forceinline__ float finish(const float* S, const float* X8, int p) const {
+    const uint32_t sh = 16 * (p & 1);  // byte offset 2(p&1) within the word
+    const uint32_t w0 = hd[1] >> sh, w1 = hd[2] >> sh, w2 = hd[3] >> sh;
+    uint32_t sc0, sc1, mn0, mn1;
+    if (p < 2) {
+      sc0 = w0 & 63, sc1 = (w0 >> 8) & 63, mn0 = w1 & 63, mn1 = (w1 >> 8) & 63;
     } else {
-      a = (b2 & 0x0f) | ((b0 >> 6) << 4);
-      b = (b2 >> 4) | ((b1 >> 6) << 4);
+      sc0 = (w2 & 0x0f) | ((w0 >> 2) & 0x30), sc1 = ((w2 >> 8) & 0x0f) | ((w0 >> 10) & 0x30);
+      mn0 = ((w2 >> 4) & 0x0f) | ((w1 >> 2) & 0x30), mn1 = ((w2 >> 12) & 0x0f) | ((w1 >> 10) & 0x30);
     }
-    sc[k] = (float)a;
-    mn[k] = (float)b;
+    const float x0 = (X8[0] + X8[1]) + (X8[2] + X8[3]);
+    const float x1 = (X8[4] + X8[5]) + (X8[6] + X8[7]);
+    const float qx0 = 256.0f * S[0] - 128.0f * x0, qx1 = 256.0f * S[1] - 128.0f * x1;
+    return h2f_lo(hd[0]) * ((float)sc0 * qx0 + (float)sc1 * qx1) -
+           h2f_hi(hd[0]) * ((float)mn0 * x0 + (float)mn1 * x1);
   }
-  const int qs0 = HIGHBITS ? 48 : 16;
-  const uint4 q0 = *reinterpret_cast<const uint4*>(u + qs0 + 32 * p);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(u + qs0 + 32 * p + 16);
-  const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint32_t h[8];
-  if (HIGHBITS) {
-    const uint4 h0 = *reinterpret_cast<const uint4*>(u + 16);
-    const uint4 h1 = *reinterpret_cast<const uint4*>(u + 32);
-    h[0] = h0.x, h[1] = h0.y, h[2] = h0.z, h[3] = h0.w;
-    h[4] = h1.x, h[5] = h1.y, h[6] = h1.z, h[7] = h1.w;
-  }
-  f2 slo = 0, shi = 0;
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
-    if (HIGHBITS) {
-      lo |= ((h[i] >> (2 * p)) & 0x01010101u) << 4;
-      hi |= ((h[i] >> (2 * p + 1)) & 0x01010101u) << 4;
-    }
-    dot4(slo, lo, x + 4 * i);
-    dot4(shi, hi, x + 32 + 4 * i);
-  }
-  const float x0 = (X[0] + X[1]) + (X[2] + X[3]);
-  const float x1 = (X[4] + X[5]) + (X[6] + X[7]);
-  const float qx0 = 256.0f * hsum2(slo) - 128.0f * x0;
-  const float qx1 = 256.0f * hsum2(shi) - 128.0f * x1;
-  return d * (sc[0] * qx0 + sc[1] * qx1) - dmin * (mn[0] * x0 + mn[1] * x1);
-}
+};
 template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q4_K>(const uint8_t* u, int p, const float* x,
-                                                          const float* X) {
-  return k4_pair<0>(u, p, x, X);
-}
+struct Piece<LRS_GGML_Q4_K> : PieceK4<LRS_GGML_Q4_K> {};
 template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q5_K>(const uint8_t* u, int p, const float* x,
-                                                          const float* X) {
-  return k4_pair<1>(u, p, x, X);
-}
+struct Piece<LRS_GGML_Q5_K> : PieceK4<LRS_GGML_Q5_K> {};
 
-// Q6_K piece (half, octet): d * sc * (q - 32);  sum (q-32) x = 256 S - 160 X
-// per 8-value run (one scale each).   (src/quant.rs:437-454)
+// Q6_K: piece (half, octet) = 32 values {half*128 + q*32 + oct*8 + i}
+// (src/quant.rs:437-454): d * sc_q * (code - 32);  sum (code-32) x =
+// 256 S - 160 X per quarter q.  Word i: quarter i/2, lanes oct*8 + 4(i%2)..
 template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_Q6_K>(const uint8_t* u, int sub,
-                                                          const float* x, const float* X) {
-  const int half = sub >> 2, oct = sub & 3;
-  uint32_t la[2], lb[2], hb[2], dw[1], sca[1], scb[1];
-  load_words<2>(u + half * 64 + oct * 8, la);
-  load_words<2>(u + half * 64 + 32 + oct * 8, lb);
-  load_words<2>(u + 128 + half * 32 + oct * 8, hb);
-  load_words<1>(u + 208, dw);
-  load_words<1>(u + 192 + half * 8, sca);  // scales of the half, bytes 0..3
-  load_words<1>(u + 196 + half * 8, scb);  // bytes 4..7
-  const float d = h2f_lo(dw[0]);
-  const int so = oct >> 1;
-  float acc = 0.0f;
+struct Piece<LRS_GGML_Q6_K> {
+  static constexpr int kValues = 32, kWords = 8, kGroups = 4, kPieces = 8;
+  float d, sc[4];
+  uint32_t la[2], lb[2], hb[2];
+  template <bool SM>
+  __device__ __forceinline__ void load(const uint8_t* u, int sub) {
+    const int half = sub >> 2, oct = sub & 3;
+    ld_words<SM, 2>(u + half * 64 + oct * 8, la);
+    ld_words<SM, 2>(u + half * 64 + 32 + oct * 8, lb);
+    ld_words<SM, 2>(u + 128 + half * 32 + oct * 8, hb);
+    uint32_t s[2], dw[1];
+    ld_words<SM, 2>(u + 192 + half * 8, s);
+    ld_words<SM, 1>(u + 208, dw);
+    d = h2f_lo(dw[0]);
+    const int so = oct >> 1;
 #pragma unroll
-  for (int r = 0; r < 4; r++) {
-    const uint32_t* l = (r & 1) ? lb : la;
-    const int nsh = (r >> 1) * 4;
-    f2 s = 0;
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-      const uint32_t q = ((l[k] >> nsh) & 0x0F0F0F0Fu) | (((hb[k] >> (2 * r)) & 0x03030303u) << 4);
-      dot4(s, q, x + r * 8 + 4 * k);
+    for (int q = 0; q < 4; q++) {
+      const int si = 2 * q + so;
+      const uint32_t sw = si < 4 ? s[0] : s[1];
+      sc[q] = (float)(int8_t)((sw >> (8 * (si & 3))) & 0xff);
     }
-    const int si = r * 2 + so;  // scale index within the half
-    const uint32_t sb = si < 4 ? (sca[0] >> (8 * si)) : (scb[0] >> (8 * (si - 4)));
-    const float scv = (float)(int8_t)(sb & 0xff);
-    acc += scv * (256.0f * hsum2(s) - 160.0f * X[r]);
   }
-  return d * acc;
-}
+  __device__ __forceinline__ static int col(int sub, int i) {
+    return (sub >> 2) * 128 + (i >> 1) * 32 + (sub & 3) * 8 + 4 * (i & 1);
+  }
+  __device__ __forceinline__ static int group(int i) { return i >> 1; }
+  __device__ __forceinline__ uint32_t icode(int i, int s) const { return code_word(i, s); }
+  __device__ __forceinline__ float finish_i(const float* qx, const float* X8, int) const {
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) acc += sc[q] * (qx[q] - 32.0f * X8[q]);
+    return d * acc;
+  }
+  __device__ __forceinline__ uint32_t code_word(int i, int) const {
+    const int r = i >> 1, k = i & 1;
+    const uint32_t l = (r & 1) ? lb[k] : la[k];
+    return ((l >> ((r >> 1) * 4)) & 0x0F0F0F0Fu) | (((hb[k] >> (2 * r)) & 0x03030303u) << 4);
+  }
+  __device__ __forceinline__ float finish(const float* S, const float* X8, int) const {
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) acc += sc[q] * (256.0f * S[q] - 160.0f * X8[q]);
+    return d * acc;
+  }
+};
 
-// Dense types: piece = 32 consecutive columns.
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_F32>(const uint8_t* u, int sub, const float* x,
-                                                         const float*) {
-  const float4* p = reinterpret_cast<const float4*>(u + sub * 128);
-  f2 s = 0;
+// Dense types: 32 consecutive columns, floats used directly.
+template <int T>
+struct PieceDense {
+  static constexpr int kValues = 32, kWords = 8, kGroups = 1, kPieces = 1;
+  uint32_t v[T == LRS_GGML_F32 ? 32 : 16];
+  template <bool SM>
+  __device__ __forceinline__ void load(const uint8_t* u, int) {
+    constexpr int n16 = T == LRS_GGML_F32 ? 8 : 4;
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const float4 v = p[i];
-    fma2(s, pk(v.x, v.y), pk(x[4 * i], x[4 * i + 1]));
-    fma2(s, pk(v.z, v.w), pk(x[4 * i + 2], x[4 * i + 3]));
-  }
-  return hsum2(s);
-}
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_F16>(const uint8_t* u, int sub, const float* x,
-                                                         const float*) {
-  const uint4* p = reinterpret_cast<const uint4*>(u + sub * 64);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint4 v = p[i];
-    const uint32_t a[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&a[k]));
-      fma2(s, pk(f.x, f.y), pk(x[8 * i + 2 * k], x[8 * i + 2 * k + 1]));
+    for (int i = 0; i < n16; i++) {
+      const uint4 a = ld128<SM>(u + 16 * i);
+      v[4 * i] = a.x, v[4 * i + 1] = a.y, v[4 * i + 2] = a.z, v[4 * i + 3] = a.w;
     }
   }
-  return hsum2(s);
-}
-template <>
-__device__ __forceinline__ float piece_dot<LRS_GGML_BF16>(const uint8_t* u, int sub,
-                                                          const float* x, const float*) {
-  const uint4* p = reinterpret_cast<const uint4*>(u + sub * 64);
-  f2 s = 0;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint4 v = p[i];
-    const uint32_t a[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int k = 0; k < 4; k++)
-      fma2(s, pk(__uint_as_float(a[k] << 16), __uint_as_float(a[k] & 0xffff0000u)),
-           pk(x[8 * i + 2 * k], x[8 * i + 2 * k + 1]));
+  __device__ __forceinline__ static int col(int, int i) { return 4 * i; }
+  __device__ __forceinline__ static int group(int) { return 0; }
+  __device__ __forceinline__ uint32_t code_word(int i, int) const { return v[i]; }
+  // the 4 weights of word i
+  __device__ __forceinline__ void weights(int i, f2& a, f2& b) const {
+    if constexpr (T == LRS_GGML_F32) {
+      a = pk(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]));
+      b = pk(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+    } else if constexpr (T == LRS_GGML_F16) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&v[2 * i]));
+      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&v[2 * i + 1]));
+      a = pk(x.x, x.y);
+      b = pk(y.x, y.y);
+    } else {
+      a = pk(__uint_as_float(v[2 * i] << 16), __uint_as_float(v[2 * i] & 0xffff0000u));
+      b = pk(__uint_as_float(v[2 * i + 1] << 16), __uint_as_float(v[2 * i + 1] & 0xffff0000u));
+    }
   }
-  return hsum2(s);
-}
+  __device__ __forceinline__ float finish(const float* S, const float*, int) const { return S[0]; }
+};
+template <>
+struct Piece<LRS_GGML_F32> : PieceDense<LRS_GGML_F32> {};
+template <>
+struct Piece<LRS_GGML_F16> : PieceDense<LRS_GGML_F16> {};
+template <>
+struct Piece<LRS_GGML_BF16> : PieceDense<LRS_GGML_BF16> {};
 
 }  // namespace fast
 }  // namespace lrs
