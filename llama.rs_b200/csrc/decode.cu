@@ -85,52 +85,57 @@ __device__ __forceinline__ size_t kv_offset(const StepIO& io, int b, int p, int 
   return (((size_t)page * nkv + kvh) * kPageSize + (p % kPageSize)) * hd;
 }
 
-__global__ void __launch_bounds__(256)
+// One CTA per (item, head): heads [0, nh) rotate q in place; heads
+// [nh, nh + nkv) rotate k and store k and v of the item's position.
+__global__ void __launch_bounds__(64)
     rope_store_kernel(float* q, const float* k, const float* v, const float* cos_t,
                       const float* sin_t, StepIO io, int nh, int nkv, int hd, void* kpool,
                       void* vpool, int kv_bf16) {
-  const int b = blockIdx.x;
+  const int b = blockIdx.x, h = blockIdx.y;
   const int half = hd / 2;
   const int pos = io.pos[b];
   const float* c = cos_t + (size_t)pos * half;
   const float* s = sin_t + (size_t)pos * half;
-  float* qb = q + (size_t)b * nh * hd;
   // apply_rope_inplace, src/model.rs:86-95 (unfused, as the reference)
-  for (int idx = threadIdx.x; idx < nh * half; idx += 256) {
-    const int h = idx / half, i = idx % half;
-    float re = qb[h * hd + i], im = qb[h * hd + i + half];
-    qb[h * hd + i] = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
-    qb[h * hd + i + half] = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
-  }
-  const float* kb = k + (size_t)b * nkv * hd;
-  const float* vb = v + (size_t)b * nkv * hd;
-  for (int idx = threadIdx.x; idx < nkv * half; idx += 256) {
-    const int h = idx / half, i = idx % half;
-    float re = kb[h * hd + i], im = kb[h * hd + i + half];
-    float k0 = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
-    float k1 = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
-    size_t o = kv_offset(io, b, pos, nkv, h, hd);
-    if (kv_bf16) {
-      reinterpret_cast<__nv_bfloat16*>(kpool)[o + i] = __float2bfloat16_rn(k0);
-      reinterpret_cast<__nv_bfloat16*>(kpool)[o + i + half] = __float2bfloat16_rn(k1);
-    } else {
-      reinterpret_cast<float*>(kpool)[o + i] = k0;
-      reinterpret_cast<float*>(kpool)[o + i + half] = k1;
+  if (h < nh) {
+    float* qh = q + ((size_t)b * nh + h) * hd;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float re = qh[i], im = qh[i + half];
+      qh[i] = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
+      qh[i + half] = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
     }
+    return;
   }
-  for (int idx = threadIdx.x; idx < nkv * hd; idx += 256) {
-    const int h = idx / hd, d = idx % hd;
-    size_t o = kv_offset(io, b, pos, nkv, h, hd);
-    if (kv_bf16)
-      reinterpret_cast<__nv_bfloat16*>(vpool)[o + d] = __float2bfloat16_rn(vb[idx]);
-    else
-      reinterpret_cast<float*>(vpool)[o + d] = vb[idx];
+  const int kvh = h - nh;
+  const float* kh = k + ((size_t)b * nkv + kvh) * hd;
+  const float* vh = v + ((size_t)b * nkv + kvh) * hd;
+  const size_t o = kv_offset(io, b, pos, nkv, kvh, hd);
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float re = kh[i], im = kh[i + half];
+    const float k0 = __fsub_rn(__fmul_rn(re, c[i]), __fmul_rn(im, s[i]));
+    const float k1 = __fadd_rn(__fmul_rn(re, s[i]), __fmul_rn(im, c[i]));
+    if (kv_bf16) {
+      __nv_bfloat16* kp = reinterpret_cast<__nv_bfloat16*>(kpool) + o;
+      __nv_bfloat16* vp = reinterpret_cast<__nv_bfloat16*>(vpool) + o;
+      kp[i] = __float2bfloat16_rn(k0);
+      kp[i + half] = __float2bfloat16_rn(k1);
+      vp[i] = __float2bfloat16_rn(vh[i]);
+      vp[i + half] = __float2bfloat16_rn(vh[i + half]);
+    } else {
+      float* kp = reinterpret_cast<float*>(kpool) + o;
+      float* vp = reinterpret_cast<float*>(vpool) + o;
+      kp[i] = k0;
+      kp[i + half] = k1;
+      vp[i] = vh[i];
+      vp[i + half] = vh[i + half];
+    }
   }
 }
 
 // ---- split-K GQA decode attention ------------------------------------------
 constexpr int kMaxGroup = 8;  // query heads per KV head handled by one CTA
 constexpr int kAttnWarps = 4;
+constexpr int kMinSplit = kAttnWarps * 8;  // positions per split (8 per warp at least)
 
 template <int HD, bool BF16>
 __device__ __forceinline__ void load_row(const void* pool, size_t off, int d0, float* out) {
@@ -151,24 +156,49 @@ __device__ __forceinline__ void load_row(const void* pool, size_t off, int d0, f
   }
 }
 
+// Reduces v[0..7] over the warp; lane l ends with the total of index
+// ((l >> 4) & 1) * 4 + ((l >> 3) & 1) * 2 + ((l >> 2) & 1)  (9 shuffles).
+__device__ __forceinline__ float transpose_reduce8(const float* v, int lane) {
+  float k4[4], k2[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    k4[i] = (h16 ? v[i + 4] : v[i]) + __shfl_xor_sync(0xffffffffu, h16 ? v[i] : v[i + 4], 16);
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    k2[i] = (h8 ? k4[i + 2] : k4[i]) + __shfl_xor_sync(0xffffffffu, h8 ? k4[i] : k4[i + 2], 8);
+  float k1 = (h4 ? k2[1] : k2[0]) + __shfl_xor_sync(0xffffffffu, h4 ? k2[0] : k2[1], 4);
+  k1 += __shfl_xor_sync(0xffffffffu, k1, 2);
+  k1 += __shfl_xor_sync(0xffffffffu, k1, 1);
+  return k1;
+}
+
+// One CTA per (split, kv head, item) serves all G query heads of the GQA
+// group, so each K/V row is read once per group.  Warps take positions
+// s0 + warp, s0 + warp + 4, ...; the lanes of a warp cover the head
+// dimension (coalesced row reads).  Scores of the G heads meet in one
+// transpose-reduce, the online softmax runs per head in lane-uniform
+// registers, and each lane accumulates its slice of the G output rows.
 template <int HD, bool BF16>
 __global__ void __launch_bounds__(kAttnWarps * 32)
     attn_split_kernel(const float* q, StepIO io, int nh, int nkv, const void* kpool,
                       const void* vpool, int nsplit, float scale, float* part) {
-  constexpr int DPL = HD / 32;
+  constexpr int DPL = HD / 32;  // dims per lane
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = nh / nkv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int L = io.pos[b] + 1;
-  const int chunk = (L + nsplit - 1) / nsplit;
+  const int chunk = max((L + nsplit - 1) / nsplit, kMinSplit);
   const int s0 = split * chunk, s1 = min(L, s0 + chunk);
-  __shared__ float qs[kMaxGroup][HD];
   __shared__ float wm[kAttnWarps][kMaxGroup], wl[kAttnWarps][kMaxGroup];
   __shared__ float wo[kAttnWarps][kMaxGroup][HD];
-  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x)
-    qs[idx / HD][idx % HD] = q[(size_t)b * nh * HD + (size_t)(kvh * G) * HD + idx];
-  __syncthreads();
 
+  float qv[kMaxGroup][DPL];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; g++)
+#pragma unroll
+    for (int k = 0; k < DPL; k++)
+      qv[g][k] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + lane * DPL + k] * scale : 0.0f;
   float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][DPL];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; g++) {
@@ -177,63 +207,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 #pragma unroll
     for (int k = 0; k < DPL; k++) o[g][k] = 0.0f;
   }
-  for (int base = s0 + warp * 32; base < s1; base += kAttnWarps * 32) {
-    const int p = base + lane;
-    const bool valid = p < s1;
-    float sc[kMaxGroup];
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.0f;
-    if (valid) {
-      const size_t off = kv_offset(io, b, p, nkv, kvh, HD);
-      for (int d = 0; d < HD; d += 4) {
-        float kk[4];
-        if constexpr (BF16) {
-          const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(kpool) + off + d;
-#pragma unroll
-          for (int t = 0; t < 4; t++) kk[t] = __bfloat162float(kp[t]);
-        } else {
-          float4 t4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kpool) + off + d);
-          kk[0] = t4.x, kk[1] = t4.y, kk[2] = t4.z, kk[3] = t4.w;
-        }
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++)
-          if (g < G)
-#pragma unroll
-            for (int t = 0; t < 4; t++) sc[g] = fmaf(qs[g][d + t], kk[t], sc[g]);
-      }
-    }
-    float pe[kMaxGroup];
+  const int hsel = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+  for (int p = s0 + warp; p < s1; p += kAttnWarps) {
+    const size_t off = kv_offset(io, b, p, nkv, kvh, HD);
+    float kk[DPL], vv[DPL];
+    load_row<HD, BF16>(kpool, off, lane * DPL, kk);
+    load_row<HD, BF16>(vpool, off, lane * DPL, vv);
+    float part_s[kMaxGroup];
 #pragma unroll
     for (int g = 0; g < kMaxGroup; g++) {
-      if (g >= G) {
-        pe[g] = 0.0f;
-        continue;
-      }
-      float s = valid ? sc[g] * scale : -INFINITY;
-      float cm = s;
-      for (int w = 16; w >= 1; w >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, w));
-      const float mn = fmaxf(m[g], cm);
+      float t = 0.0f;
+#pragma unroll
+      for (int k = 0; k < DPL; k++) t = fmaf(qv[g][k], kk[k], t);
+      part_s[g] = t;
+    }
+    // score of head hsel on lanes with (lane & 3) == 0; broadcast each head's
+    const float red = transpose_reduce8(part_s, lane);
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) {
+      if (g >= G) break;
+      const int src = ((g >> 2) & 1) * 16 + ((g >> 1) & 1) * 8 + (g & 1) * 4;
+      const float sc = __shfl_sync(0xffffffffu, red, src);
+      const float mn = fmaxf(m[g], sc);
       const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
-      float e = valid ? expf(s - mn) : 0.0f;
-      float es = e;
-      for (int w = 16; w >= 1; w >>= 1) es += __shfl_xor_sync(0xffffffffu, es, w);
-      l[g] = l[g] * corr + es;
+      const float e = expf(sc - mn);
+      l[g] = l[g] * corr + e;
 #pragma unroll
-      for (int k = 0; k < DPL; k++) o[g][k] *= corr;
+      for (int k = 0; k < DPL; k++) o[g][k] = fmaf(e, vv[k], o[g][k] * corr);
       m[g] = mn;
-      pe[g] = e;
     }
-    const int nvalid = min(32, s1 - base);
-    for (int j = 0; j < nvalid; j++) {
-      float vv[DPL];
-      load_row<HD, BF16>(vpool, kv_offset(io, b, base + j, nkv, kvh, HD), lane * DPL, vv);
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; g++) {
-        const float pj = __shfl_sync(0xffffffffu, pe[g], j);
-#pragma unroll
-        for (int k = 0; k < DPL; k++) o[g][k] = fmaf(pj, vv[k], o[g][k]);
-      }
-    }
+    (void)hsel;
   }
 #pragma unroll
   for (int g = 0; g < kMaxGroup; g++) {
@@ -267,21 +270,34 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 }
 
 template <int HD>
-__global__ void __launch_bounds__(HD) attn_combine_kernel(const float* part, int nh, int nsplit,
-                                                          float* att) {
+__global__ void __launch_bounds__(HD) attn_combine_kernel(const float* part, const int* pos,
+                                                          int nh, int nsplit, float* att) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const float* pp = part + ((size_t)b * nh + h) * nsplit * (HD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[s * (HD + 2)]);
-  float Ls = 0.0f, O = 0.0f;
-  for (int s = 0; s < nsplit; s++) {
-    const float ms = pp[s * (HD + 2)];
-    if (ms == -INFINITY) continue;
-    const float f = expf(ms - M);
-    Ls += pp[s * (HD + 2) + 1] * f;
-    O += pp[s * (HD + 2) + 2 + d] * f;
+  const int L = pos[b] + 1;
+  const int chunk = max((L + nsplit - 1) / nsplit, kMinSplit);
+  const int nact = min(nsplit, (L + chunk - 1) / chunk);  // splits that saw positions
+  __shared__ float wsh[64];
+  __shared__ float Lsum;
+  if (d < 32) {
+    // weights exp(m_s - M) of the active splits, and the total softmax denominator
+    float m0 = d < nact ? pp[d * (HD + 2)] : -INFINITY;
+    float m1 = d + 32 < nact ? pp[(d + 32) * (HD + 2)] : -INFINITY;
+    float M = fmaxf(m0, m1);
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float w0 = m0 == -INFINITY ? 0.0f : expf(m0 - M);
+    const float w1 = m1 == -INFINITY ? 0.0f : expf(m1 - M);
+    float l = (d < nact ? pp[d * (HD + 2) + 1] * w0 : 0.0f) +
+              (d + 32 < nact ? pp[(d + 32) * (HD + 2) + 1] * w1 : 0.0f);
+    for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    wsh[d] = w0;
+    wsh[d + 32] = w1;
+    if (d == 0) Lsum = l;
   }
-  att[((size_t)b * nh + h) * HD + d] = O / Ls;
+  __syncthreads();
+  float O = 0.0f;
+  for (int s = 0; s < nact; s++) O += pp[s * (HD + 2) + 2 + d] * wsh[s];
+  att[((size_t)b * nh + h) * HD + d] = O / Lsum;
 }
 
 __global__ void advance_kernel(const unsigned long long* keys, int* tok, int* pos, int batch,
@@ -319,21 +335,21 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int
 cudaError_t launch_rope_store(float* q, const float* k, const float* v, const float* cos_t,
                               const float* sin_t, StepIO io, int batch, int nh, int nkv, int hd,
                               void* kpool, void* vpool, int kv_bf16, cudaStream_t st) {
-  rope_store_kernel<<<batch, 256, 0, st>>>(q, k, v, cos_t, sin_t, io, nh, nkv, hd, kpool, vpool,
-                                           kv_bf16);
+  rope_store_kernel<<<dim3(batch, nh + nkv), 64, 0, st>>>(q, k, v, cos_t, sin_t, io, nh, nkv, hd,
+                                                          kpool, vpool, kv_bf16);
   return cudaGetLastError();
 }
 
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
                              const void* kpool, const void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, cudaStream_t st) {
-  if (nh / nkv > kMaxGroup) return cudaErrorInvalidValue;
+  if (nh / nkv > kMaxGroup || nsplit > 64) return cudaErrorInvalidValue;
   const float scale = 1.0f / sqrtf((float)hd);
   dim3 g(nsplit, nkv, batch);
 #define LRS_ATTN(HD, BF)                                                                         \
   attn_split_kernel<HD, BF><<<g, kAttnWarps * 32, 0, st>>>(q, io, nh, nkv, kpool, vpool, nsplit, \
                                                             scale, part);                        \
-  attn_combine_kernel<HD><<<dim3(nh, batch), HD, 0, st>>>(part, nh, nsplit, att);
+  attn_combine_kernel<HD><<<dim3(nh, batch), HD, 0, st>>>(part, io.pos, nh, nsplit, att);
   if (hd == 128) {
     if (kv_bf16) {
       LRS_ATTN(128, true)

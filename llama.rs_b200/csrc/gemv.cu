@@ -318,6 +318,21 @@ struct XLayout {
   }
 };
 
+// Bulk-prefetches the rows of row group g (R rows, both matrices of a pair)
+// into L2 so that the lanes' loads of the group hit L2 instead of HBM.
+template <int R, bool PAIR>
+__device__ __forceinline__ void prefetch_group(const GemvParams& p, int g) {
+  if (g >= p.total_tiles) return;
+  const GemvSeg sg = find_seg(p, g);
+  const int r0 = (g - sg.tile0) * R;
+  const int nr = min(R, sg.rows - r0);
+  const size_t lo = (size_t)r0 * sg.rb, hi = lo + (size_t)nr * sg.rb;
+  const size_t alo = lo & ~size_t(15);
+  const uint32_t bytes = (uint32_t)(((hi - alo) + 15) & ~size_t(15));
+  prefetch_l2(sg.w + alo, bytes);
+  if (PAIR) prefetch_l2(sg.w2 + alo, bytes);
+}
+
 template <int T, bool PAIR>
 __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_constant__ GemvParams p) {
   using BT = BlockTraits<T>;
@@ -328,8 +343,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
   constexpr int PV = XL::PV, NRUN = XL::NRUN, CH = XL::CH, NW = P::kWords;
   constexpr bool kDense = XL::kDense;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem);
-  uint8_t* xq = smem + 128;
+  float* red = reinterpret_cast<float*>(smem);  // 256 B
+  uint8_t* xq = smem + 256;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int npieces = p.cols / PV;
   // piece-transposed arrays
@@ -338,6 +353,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
   float* sxa = reinterpret_cast<float*>(xl4 + (size_t)CH * npieces);  // [NRUN][npieces]
   float* Xa = sxa + (size_t)NRUN * npieces;                       // [NRUN][npieces]
   float* xf = reinterpret_cast<float*>(xq);                       // dense: [npieces][PV]
+  // The weights do not depend on the previous kernel: pull this CTA's first
+  // two passes of row groups into L2 while it finishes.
+  const int gpc0 = kWarps / p.wpg;
+  if (tid < 2 * gpc0) prefetch_group<R, PAIR>(p, blockIdx.x * gpc0 + (tid / gpc0) * gridDim.x * gpc0 + tid % gpc0);
 
   pdl_wait();  // x / residual come from the previous kernel
   float inv_rms = 1.0f;
@@ -403,11 +422,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
   __syncthreads();
   pdl_launch_dependents();
 
-  const int nwarps = gridDim.x * kWarps;
-  for (int g = blockIdx.x * kWarps + warp; g < p.total_tiles; g += nwarps) {
-    const GemvSeg sg = find_seg(p, g);
-    const int r0 = (g - sg.tile0) * R;
-    const int nr = min(R, sg.rows - r0);
+  // wpg warps share a row group, each taking every wpg-th 32-piece slice;
+  // the CTA's 8 warps serve 8 / wpg groups per pass (uniform trip count).
+  const int wpg = p.wpg, gpc = kWarps / wpg;
+  const int sub_w = warp % wpg;
+  for (int gb = blockIdx.x * gpc; gb < p.total_tiles; gb += gridDim.x * gpc) {
+    const int g = gb + warp / wpg;
+    const bool live = g < p.total_tiles;
+    // keep two passes ahead in L2
+    if (lane == 0 && sub_w == 0) prefetch_group<R, PAIR>(p, g + 2 * gridDim.x * gpc);
+    const GemvSeg sg = find_seg(p, live ? g : gb);
+    const int r0 = ((live ? g : gb) - sg.tile0) * R;
+    const int nr = live ? min(R, sg.rows - r0) : 0;
     const uint8_t* base[NM];
     base[0] = sg.w + (size_t)r0 * sg.rb;
     if constexpr (PAIR) base[1] = sg.w2 + (size_t)r0 * sg.rb;
@@ -416,7 +442,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
     for (int m = 0; m < NM; m++)
 #pragma unroll
       for (int r = 0; r < R; r++) acc[m][r] = 0.0f;
-    for (int pc = lane; pc < npieces; pc += 32) {
+    for (int pc = lane + 32 * sub_w; live && pc < npieces; pc += 32 * wpg) {
       const int unit = pc / P::kPieces, sub = pc % P::kPieces;
       const size_t uoff = (size_t)unit * BT::kBytes;
       P pr[NM][R];
@@ -486,7 +512,25 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
       for (int r = 0; r < R; r++)
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) acc[m][r] += __shfl_xor_sync(0xffffffffu, acc[m][r], o);
-    if (lane == 0) {
+    if (wpg > 1) {  // combine the warps of a group (fixed order: deterministic)
+      __syncthreads();
+      if (lane == 0)
+#pragma unroll
+        for (int m = 0; m < NM; m++)
+#pragma unroll
+          for (int r = 0; r < R; r++) red[(warp * NM + m) * R + r] = acc[m][r];
+      __syncthreads();
+      if (sub_w == 0 && lane == 0)
+#pragma unroll
+        for (int m = 0; m < NM; m++)
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            float t = 0.0f;
+            for (int w = 0; w < wpg; w++) t += red[((warp + w) * NM + m) * R + r];
+            acc[m][r] = t;
+          }
+    }
+    if (lane == 0 && sub_w == 0 && live) {
       unsigned long long key = 0ull;
 #pragma unroll
       for (int r = 0; r < R; r++) {
@@ -646,7 +690,7 @@ int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch) 
       s.tiles = (s.rows + R - 1) / R;
       s.tile0 = tile0;
       tile0 += s.tiles;
-      fits = fits && 128 + fast_x_bytes(s.type, cols) <= 200 * 1024;
+      fits = fits && 256 + fast_x_bytes(s.type, cols) <= 200 * 1024;
     }
     q.total_tiles = tile0;
     q.stages = 0;
@@ -696,9 +740,15 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
       }
       q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
       const void* kernel = fast_kernel(q.seg[0].type, pair);
-      const size_t smem = 128 + fast_x_bytes(q.seg[0].type, q.cols);
+      const size_t smem = 256 + fast_x_bytes(q.seg[0].type, q.cols);
       const int occ = std::max(1, occupancy(kernel, (int)smem, kGemvThreads));
-      const int grid = std::min((q.total_tiles + kWarps - 1) / kWarps, num_sms * occ);
+      // Long rows: several warps per row group, ~4 pieces per lane.
+      const int pv = (q.seg[0].type == LRS_GGML_Q4_K || q.seg[0].type == LRS_GGML_Q5_K) ? 64 : 32;
+      const int ppr = q.cols / pv;
+      q.wpg = 1;
+      while (q.wpg < kWarps && ppr >= 32 * 4 * 2 * q.wpg) q.wpg *= 2;
+      const int gpc = kWarps / q.wpg;
+      const int grid = std::min((q.total_tiles + gpc - 1) / gpc, num_sms * occ);
       if (grid > 0) {
         cudaError_t e = launch_cfg(kernel, smem, grid, kGemvThreads, stream, pdl, q);
         if (e != cudaSuccess) return e;

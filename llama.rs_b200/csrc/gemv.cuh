@@ -35,7 +35,8 @@ struct GemvParams {
   float norm_eps;
   unsigned long long* argmax_keys;  // [batch], EPI_ARGMAX
   int stage_bytes, stages, x_in_smem;
-  int fast;  // 1: batch-1 kernel with factored per-type dots (gemv_fast.cuh)
+  int fast;  // 1: batch-1 direct-load kernel (int8-split x, dp4a)
+  int wpg;   // batch-1 kernel: warps sharing one row group (long rows split across warps)
   int* error_flag;
 };
 
