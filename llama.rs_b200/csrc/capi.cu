@@ -170,6 +170,7 @@ void lrs_backend_destroy(lrs_backend* be) {
   cudaFree(be->d_err);
   cudaFree(be->d_x);
   cudaFree(be->d_y);
+  cudaFree(be->d_scratch);
   cudaStreamDestroy(be->stream);
   delete be;
 }
@@ -236,6 +237,19 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
   p.x = d_in;
   p.x_ld = w->t.cols;
   p.error_flag = be->d_err;
+  if (batch > 1 && gemm_supported(p)) {
+    const size_t need = gemm_scratch_bytes((int)batch, w->t.cols, be->sms);
+    if (be->scratch_cap < need) {
+      cudaFree(be->d_scratch);  // synchronizes with work that may still use it
+      be->d_scratch = nullptr;
+      be->scratch_cap = 0;
+      if (cudaMalloc(&be->d_scratch, need) != cudaSuccess)
+        return fail(LRS_ERR_OOM, "cudaMalloc of matmul scratch failed");
+      be->scratch_cap = need;
+    }
+    p.scratch = be->d_scratch;
+    p.scratch_bytes = be->scratch_cap;
+  }
   cudaStream_t st = stream ? (cudaStream_t)stream : be->stream;
   LRS_CUDA(gemv_launch(p, st, be->sms, false));
   return LRS_OK;
@@ -312,6 +326,8 @@ struct lrs_model {
   int max_items = 0, max_split = 64;
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+  void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
+  size_t gemm_scratch_bytes = 0;
   unsigned long long* keys = nullptr;
   int *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_step = nullptr;
   uint32_t* d_last = nullptr;
@@ -332,7 +348,10 @@ int32_t model_alloc(lrs_model* m, void** p, size_t bytes) {
   return LRS_OK;
 }
 
-cudaError_t model_gemv(lrs_model* m, const GemvParams& p, cudaStream_t st, int sms) {
+cudaError_t model_gemv(lrs_model* m, const GemvParams& p0, cudaStream_t st, int sms) {
+  GemvParams p = p0;
+  p.scratch = m->gemm_scratch;
+  p.scratch_bytes = m->gemm_scratch_bytes;
   if (!m->prof) return gemv_launch(p, st, sms, true);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
@@ -633,6 +652,8 @@ lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
       (rc = model_alloc(m.get(), (void**)&m->d_step, 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
     return cleanup(rc);
+  m->gemm_scratch_bytes = gemm_scratch_bytes((int)B, std::max(h, I), m->be->sms);
+  if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
   LRS_CUDA(cudaDeviceSynchronize());
   *out = m.release();
   return LRS_OK;

@@ -725,6 +725,9 @@ cudaError_t launch_cfg(const void* kernel, size_t smem, int grid, int threads,
 
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
   const bool pair = p.epi == EPI_SWIGLU;
+  if (p.batch >= 2 && p.scratch && gemm_supported(p) &&
+      p.scratch_bytes >= gemm_scratch_bytes(p.batch, p.cols, num_sms))
+    return gemm_launch(p, p.scratch, num_sms, stream);
   if (p.fast) {
     // Direct-load batch-1 kernel, one launch per run of same-type segments.
     int i = 0;

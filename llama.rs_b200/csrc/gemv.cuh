@@ -38,6 +38,10 @@ struct GemvParams {
   int fast;  // 1: batch-1 direct-load kernel (int8-split x, dp4a)
   int wpg;   // batch-1 kernel: warps sharing one row group (long rows split across warps)
   int* error_flag;
+  // Device scratch for the batched tensor-core path (gemm_i8.cu); when null or
+  // smaller than gemm_scratch_bytes, batches run on the CUDA-core kernel.
+  void* scratch;
+  size_t scratch_bytes;
 };
 
 // Host helpers (gemv.cu).
@@ -53,5 +57,10 @@ struct GemvMat {
 int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch);
 // Launches on `stream` (with programmatic dependent launch when pdl != 0).
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl);
+
+// Batched (2..) quantized matmul on the integer tensor cores (gemm_i8.cu).
+bool gemm_supported(const GemvParams& p);
+size_t gemm_scratch_bytes(int batch, int max_cols, int sms);
+cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
 
 }  // namespace lrs

@@ -13,6 +13,8 @@ struct lrs_backend {
   float* d_x = nullptr;
   float* d_y = nullptr;
   size_t x_cap = 0, y_cap = 0;
+  void* d_scratch = nullptr;  // batched tensor-core matmul scratch
+  size_t scratch_cap = 0;
 };
 
 struct DevTensor {

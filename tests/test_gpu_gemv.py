@@ -64,7 +64,7 @@ def test_dequant_bit_exact_and_ragged_rows(lrs, orc, backend, qt):
 
 
 @pytest.mark.parametrize("qt", ALL_TYPES)
-@pytest.mark.parametrize("batch", [1, 3, 8, 11])
+@pytest.mark.parametrize("batch", [1, 3, 8, 11, 64])
 def test_matvec_matches_scalar_dot(lrs, orc, backend, qt, batch):
     rows, cols = 333, 1024
     t = _matrix(lrs, qt, rows, cols, 2)
@@ -78,6 +78,23 @@ def test_matvec_matches_scalar_dot(lrs, orc, backend, qt, batch):
         y = np.empty(rows, dtype=np.float32)
         backend.matvec(t, x[0], y)
         assert np.array_equal(y, got[0])
+    backend.release(t)
+
+
+@pytest.mark.parametrize("qt", ["Q4_0", "Q5_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K"])
+def test_batched_matmul_single_k_group_and_ragged_chunk(lrs, orc, backend, qt):
+    # 40000 rows fill the GPU with row CTAs alone (epilogue inside the matmul
+    # kernel); 768 columns end in a half-filled 512-column chunk.
+    rows, cols, batch = 40000, 768, 5
+    if qt in ("Q4_K", "Q5_K", "Q6_K"):
+        cols = 1280
+    t = _matrix(lrs, qt, rows, cols, 4)
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    got = backend.matvec_batched(t, x)
+    for b in range(batch):
+        ref = orc.matvec(orc.SCALAR, t.data, int(t.quant_type), rows, cols, x[b])
+        _check_rows(got[b], ref)
     backend.release(t)
 
 

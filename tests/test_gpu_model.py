@@ -114,3 +114,20 @@ def test_c3_width_two_layers(lrs, orc, backend):
         lrs, orc, backend, cfg, lrs.LoadQuantization.Q4KM, 2, 16, 128, max_seq=4096)
     assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
     _assert_tokens(ref, toks)
+
+
+def test_c3_width_64_sequences(lrs, orc, backend):
+    """The c3 data-parallel decode shape: 64 sequences per step at Qwen2.5-7B widths
+    (2 layers); sequences 0, 31 and 63 are checked against the oracle."""
+    cfg = lrs.config_c3()
+    cfg.num_hidden_layers = 2
+    sm = lrs.SynthModel(cfg, 3, lrs.LoadQuantization.Q4KM)
+    B, n_dec = 64, 16
+    m = lrs.CudaQwen2Model(backend, sm.desc(), max_seq_len=256, max_sequences=B)
+    prompts = [lrs.prompt_tokens(200 + s, 8 + s % 5, cfg.vocab_size) for s in range(B)]
+    firsts = [m.prefill(p, 0, seq=s)[1] for s, p in enumerate(prompts)]
+    produced = m.decode_greedy(firsts, [len(p) for p in prompts], n_dec, list(range(B)))
+    fed = np.concatenate([np.array(firsts, np.uint32)[None, :], produced[:-1]], axis=0)
+    for s in (0, 31, 63):
+        ref = orc.OracleModel(sm.desc(), 256).benchmark_tokens(prompts[s], n_dec)
+        _assert_tokens(ref, fed[:, s])
