@@ -156,49 +156,54 @@ __device__ __forceinline__ void load_row(const void* pool, size_t off, int d0, f
   }
 }
 
-// Reduces v[0..7] over the warp; lane l ends with the total of index
-// ((l >> 4) & 1) * 4 + ((l >> 3) & 1) * 2 + ((l >> 2) & 1)  (9 shuffles).
-__device__ __forceinline__ float transpose_reduce8(const float* v, int lane) {
-  float k4[4], k2[2];
-  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-    k4[i] = (h16 ? v[i + 4] : v[i]) + __shfl_xor_sync(0xffffffffu, h16 ? v[i] : v[i + 4], 16);
-#pragma unroll
-  for (int i = 0; i < 2; i++)
-    k2[i] = (h8 ? k4[i + 2] : k4[i]) + __shfl_xor_sync(0xffffffffu, h8 ? k4[i] : k4[i + 2], 8);
-  float k1 = (h4 ? k2[1] : k2[0]) + __shfl_xor_sync(0xffffffffu, h4 ? k2[0] : k2[1], 4);
-  k1 += __shfl_xor_sync(0xffffffffu, k1, 2);
-  k1 += __shfl_xor_sync(0xffffffffu, k1, 1);
-  return k1;
+// Positions of split `split` of a context of L positions: [s0, s1) with
+// chunks a multiple of 32 (blocks of 32 positions never straddle a KV page).
+__device__ __forceinline__ int split_chunk(int L, int nsplit) {
+  const int c = max((L + nsplit - 1) / nsplit, kMinSplit);
+  return (c + 31) & ~31;
+}
+
+// Four consecutive K or V values of a row.
+template <bool BF16>
+__device__ __forceinline__ float4 load4(const void* pool, size_t off) {
+  if constexpr (BF16) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(
+        reinterpret_cast<const __nv_bfloat16*>(pool) + off));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  } else {
+    return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pool) + off));
+  }
 }
 
 // One CTA per (split, kv head, item) serves all G query heads of the GQA
-// group, so each K/V row is read once per group.  Warps take positions
-// s0 + warp, s0 + warp + 4, ...; the lanes of a warp cover the head
-// dimension (coalesced row reads).  Scores of the G heads meet in one
-// transpose-reduce, the online softmax runs per head in lane-uniform
-// registers, and each lane accumulates its slice of the G output rows.
+// group, so each K/V row is read once per group.  Warps take blocks of 32
+// positions (s0 + 32 * warp, then every 128).  Scores: lane i owns position
+// i of the block and dots its K row with the G scaled query rows (shared
+// memory broadcasts).  The block's softmax update is one warp max / sum per
+// head; the probabilities go through shared memory to the PV product, where
+// the lanes cover the head dimension and V rows are read coalesced.
 template <int HD, bool BF16>
 __global__ void __launch_bounds__(kAttnWarps * 32)
     attn_split_kernel(const float* q, StepIO io, int nh, int nkv, const void* kpool,
                       const void* vpool, int nsplit, float scale, float* part) {
-  constexpr int DPL = HD / 32;  // dims per lane
+  constexpr int DPL = HD / 32;  // dims per lane in the PV product
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = nh / nkv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int L = io.pos[b] + 1;
-  const int chunk = max((L + nsplit - 1) / nsplit, kMinSplit);
+  const int chunk = split_chunk(L, nsplit);
   const int s0 = split * chunk, s1 = min(L, s0 + chunk);
+  __shared__ float4 qs[kMaxGroup][HD / 4];
+  __shared__ float ps[kAttnWarps][kMaxGroup][32];
   __shared__ float wm[kAttnWarps][kMaxGroup], wl[kAttnWarps][kMaxGroup];
   __shared__ float wo[kAttnWarps][kMaxGroup][HD];
 
-  float qv[kMaxGroup][DPL];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; g++)
-#pragma unroll
-    for (int k = 0; k < DPL; k++)
-      qv[g][k] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + lane * DPL + k] * scale : 0.0f;
+  for (int i = threadIdx.x; i < kMaxGroup * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    reinterpret_cast<float*>(qs)[i] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + d] * scale : 0.0f;
+  }
+  __syncthreads();
   float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][DPL];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; g++) {
@@ -207,36 +212,71 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 #pragma unroll
     for (int k = 0; k < DPL; k++) o[g][k] = 0.0f;
   }
-  const int hsel = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-  for (int p = s0 + warp; p < s1; p += kAttnWarps) {
-    const size_t off = kv_offset(io, b, p, nkv, kvh, HD);
-    float kk[DPL], vv[DPL];
-    load_row<HD, BF16>(kpool, off, lane * DPL, kk);
-    load_row<HD, BF16>(vpool, off, lane * DPL, vv);
-    float part_s[kMaxGroup];
+  for (int blk = s0 + 32 * warp; blk < s1; blk += 32 * kAttnWarps) {
+    const size_t base = kv_offset(io, b, blk, nkv, kvh, HD);  // row blk; rows follow at +HD
+    const bool valid = blk + lane < s1;
+    float sc[kMaxGroup];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) {
-      float t = 0.0f;
+    for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.0f;
+    if (valid) {
+      const size_t kr = base + (size_t)lane * HD;
+#pragma unroll 8
+      for (int i = 0; i < HD / 4; i++) {
+        const float4 kv = load4<BF16>(kpool, kr + 4 * i);
 #pragma unroll
-      for (int k = 0; k < DPL; k++) t = fmaf(qv[g][k], kk[k], t);
-      part_s[g] = t;
+        for (int g = 0; g < kMaxGroup; g++) {
+          if (g < G) {
+            const float4 qq = qs[g][i];
+            sc[g] = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, fmaf(qq.w, kv.w, sc[g]))));
+          }
+        }
+      }
     }
-    // score of head hsel on lanes with (lane & 3) == 0; broadcast each head's
-    const float red = transpose_reduce8(part_s, lane);
 #pragma unroll
     for (int g = 0; g < kMaxGroup; g++) {
       if (g >= G) break;
-      const int src = ((g >> 2) & 1) * 16 + ((g >> 1) & 1) * 8 + (g & 1) * 4;
-      const float sc = __shfl_sync(0xffffffffu, red, src);
-      const float mn = fmaxf(m[g], sc);
+      const float s = valid ? sc[g] : -INFINITY;
+      float bm = s;
+      for (int w = 16; w >= 1; w >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, w));
+      const float mn = fmaxf(m[g], bm);  // finite: lane 0 is always valid
       const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
-      const float e = expf(sc - mn);
-      l[g] = l[g] * corr + e;
-#pragma unroll
-      for (int k = 0; k < DPL; k++) o[g][k] = fmaf(e, vv[k], o[g][k] * corr);
+      const float e = valid ? expf(s - mn) : 0.0f;
+      float es = e;
+      for (int w = 16; w >= 1; w >>= 1) es += __shfl_xor_sync(0xffffffffu, es, w);
+      l[g] = l[g] * corr + es;
       m[g] = mn;
+      ps[warp][g][lane] = e;
+#pragma unroll
+      for (int k = 0; k < DPL; k++) o[g][k] *= corr;
     }
-    (void)hsel;
+    __syncwarp();
+    const int nv = min(32, s1 - blk);
+#pragma unroll 4
+    for (int j = 0; j < nv; j++) {
+      const size_t vr = base + (size_t)j * HD + lane * DPL;
+      float v[DPL];
+      if constexpr (DPL == 4) {
+        const float4 t = load4<BF16>(vpool, vr);
+        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < DPL; k++) {
+          if constexpr (BF16)
+            v[k] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(vpool)[vr + k]);
+          else
+            v[k] = __ldg(reinterpret_cast<const float*>(vpool) + vr + k);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; g++) {
+        if (g < G) {
+          const float pj = ps[warp][g][j];
+#pragma unroll
+          for (int k = 0; k < DPL; k++) o[g][k] = fmaf(pj, v[k], o[g][k]);
+        }
+      }
+    }
+    __syncwarp();
   }
 #pragma unroll
   for (int g = 0; g < kMaxGroup; g++) {
@@ -275,7 +315,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* part, con
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const float* pp = part + ((size_t)b * nh + h) * nsplit * (HD + 2);
   const int L = pos[b] + 1;
-  const int chunk = max((L + nsplit - 1) / nsplit, kMinSplit);
+  const int chunk = split_chunk(L, nsplit);
   const int nact = min(nsplit, (L + chunk - 1) / chunk);  // splits that saw positions
   __shared__ float wsh[64];
   __shared__ float Lsum;

@@ -22,18 +22,29 @@
 // is formed exactly in int32 by two MMAs (the second one accumulates onto the
 // first one's result shifted left by 8).  The A operand is the weight codes,
 // decoded straight from the GGML block bytes into the m16n8k32 fragment
-// layout; B is the split x staged in shared memory.  Scales and the offset
-// term are applied in fp32 per (row, group).  The result matches the
+// layout; B is the split x.  Scales and the offset term are applied in fp32
+// per (row, group); sum_k x_k is the exact f32 sum.  The result matches the
 // reference's f32 dot to about 1e-5 relative.
 //
-// Work split: a CTA of 8 warps owns 128 rows (16 per warp) of one matrix and
-// a run of K chunks of 512 columns; per chunk the split x of all items is
-// staged in shared memory once and each warp streams its rows' blocks from
-// HBM exactly once, holding fp32 accumulators for up to 64 items.  When the
-// row CTAs alone fill the GPU the epilogue (bias, residual add, SwiGLU,
-// greedy argmax) runs in the kernel; otherwise K is split across CTAs, the
-// partial sums go to scratch and gemm_epilogue_kernel adds them in a fixed
-// order, so results never depend on scheduling.
+// Layout of the split x ("fragment order"): for every 32-column group g and
+// tile j of 8 items, 32 records of 16 bytes, one per lane of the consuming
+// warp: lane (gid, t) gets {xh[4t..4t+3], xh[16+4t..+3], xl[4t..+3],
+// xl[16+4t..+3]} of item 8j + gid -- the B fragments of both MMAs in one
+// 16-byte shared-memory load.  Per (g, j, t) a 32-byte record holds, for
+// items 8j+2t and 8j+2t+1 (the C fragment's columns), {s/256, s/256,
+// X32, X32, Xa, Xa, Xb, Xb} with X32 = sum of x over the group and Xa, Xb
+// over its two 16-column halves (Q6_K).
+//
+// Work split: a CTA of 16 warps (8 for a gate/up pair) owns 16 rows per warp
+// of one matrix and a run of K chunks of 512 columns.  The split x of the
+// chunk (16 groups x the item tiles) is copied to shared memory with cp.async,
+// double-buffered so the next chunk lands while this one is multiplied; each
+// warp streams its rows' blocks from HBM exactly once, the next group's codes
+// loaded one group ahead.  When the row CTAs alone fill the GPU the epilogue
+// (bias, residual add, SwiGLU, greedy argmax) runs in the kernel; otherwise K
+// is split across CTAs, the partial sums go to scratch and
+// gemm_epilogue_kernel adds them in a fixed order, so results never depend on
+// scheduling.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -45,12 +56,19 @@
 namespace lrs {
 namespace {
 
-constexpr int kKC = 512;       // columns per K chunk
-constexpr int kWarps = 8;
-constexpr int kRowsCTA = 16 * kWarps;
-constexpr int kMaxItems = 64;  // items per launch (larger batches loop)
-constexpr int kXPad = 16;      // padding bytes per staged x row: conflict-free B fragments
-constexpr int kXStride = kKC + kXPad;
+constexpr int kGroupsPerChunk = 16;  // 512 columns
+constexpr int kChunkCols = 32 * kGroupsPerChunk;
+constexpr int kMaxTiles = 8;          // 64 items per launch (larger batches loop)
+constexpr int kMaxItems = 8 * kMaxTiles;
+constexpr int kXRec = 512;            // bytes of x records per (group, tile)
+constexpr int kSRec = 128;            // bytes of scale records per (group, tile)
+
+template <bool PAIR>
+struct Shape {
+  static constexpr int kWarps = PAIR ? 8 : 16;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kRows = 16 * kWarps;
+};
 
 __device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
   uint32_t v;
@@ -82,6 +100,18 @@ __device__ __forceinline__ uint32_t spread4(uint32_t nib) {
 }
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xffu; }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void mma_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                         uint32_t b1, const int (&c)[4]) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -99,38 +129,58 @@ __device__ __forceinline__ void mma_k16(int (&d)[4], const uint32_t (&a)[2], uin
 }
 
 // ---- x preparation ---------------------------------------------------------
-// xh/xl: [B][cols] int8; sx: [B][cols/32] (scale/256); X16: [B][cols/16] sums
-// of x over 16-column halves.  One warp per (item, 32-column group).
+// One warp per (item, 32-column group); items >= batch (tile padding) get
+// zero records.  xq: [groups][tiles][32] x 16 B; xs: [groups][tiles][4] x 32 B.
 __global__ void __launch_bounds__(256)
-    xsplit_kernel(const float* x, int x_ld, int cols, int8_t* xh, int8_t* xl, float* sx,
-                  float* X16) {
+    xsplit_kernel(const float* x, int x_ld, int cols, int batch, int tiles, uint8_t* xq,
+                  float* xs) {
   const int b = blockIdx.y;
   const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (g * 32 >= cols) return;
-  const float v = x[(size_t)b * x_ld + g * 32 + lane];
+  const float v = b < batch ? x[(size_t)b * x_ld + g * 32 + lane] : 0.0f;
   float mx = fabsf(v);
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float s16 = v;
   for (int o = 8; o >= 1; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
+  const float other = __shfl_xor_sync(0xffffffffu, s16, 16);
   const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
   const float q = v / sc;
-  const float h = fminf(fmaxf(rintf(q), -127.0f), 127.0f);
-  const float l = fminf(fmaxf(rintf((q - h) * 256.0f), -127.0f), 127.0f);
-  xh[(size_t)b * cols + g * 32 + lane] = (int8_t)h;
-  xl[(size_t)b * cols + g * 32 + lane] = (int8_t)l;
-  if (lane == 0) sx[(size_t)b * (cols / 32) + g] = sc * (1.0f / 256.0f);
-  if ((lane & 15) == 0) X16[(size_t)b * (cols / 16) + g * 2 + (lane >> 4)] = s16;
+  const float hf = fminf(fmaxf(rintf(q), -127.0f), 127.0f);
+  const float lf = fminf(fmaxf(rintf((q - hf) * 256.0f), -127.0f), 127.0f);
+  uint32_t h = (uint32_t)(int)hf & 0xffu, l = (uint32_t)(int)lf & 0xffu;
+  // gather 4 consecutive columns into one word (lanes 4k)
+  h |= __shfl_down_sync(0xffffffffu, h, 1) << 8;
+  l |= __shfl_down_sync(0xffffffffu, l, 1) << 8;
+  h |= __shfl_down_sync(0xffffffffu, h, 2) << 16;
+  l |= __shfl_down_sync(0xffffffffu, l, 2) << 16;
+  const int j = b >> 3, gid = b & 7;
+  if ((lane & 3) == 0) {
+    const int t = (lane & 15) >> 2, half = lane >> 4;
+    uint32_t* rec = reinterpret_cast<uint32_t*>(xq + ((size_t)g * tiles + j) * kXRec +
+                                                (gid * 4 + t) * 16);
+    rec[half] = h;
+    rec[2 + half] = l;
+  }
+  float* srec = xs + (((size_t)g * tiles + j) * 4 + (gid >> 1)) * 8 + (gid & 1);
+  if (lane == 0) {
+    srec[0] = sc * (1.0f / 256.0f);
+    srec[2] = s16 + other;
+    srec[4] = s16;
+  } else if (lane == 16) {
+    srec[6] = s16;
+  }
 }
 
 // ---- A fragments -------------------------------------------------------------
 // For one row (block bytes at rp), 32-column group gc and thread t of the
 // quad: the code words of columns 4t..4t+3 (w0) and 16+4t..16+4t+3 (w1) and
-// the affine maps of the two 16-column halves (equal except for Q6_K).
+// the affine maps of the two 16-column halves (equal except for Q6_K); ndm
+// holds -dm.
 template <int T>
 struct AFrag {
   uint32_t w0, w1;
-  float ds0, dm0, ds1, dm1;
+  float ds0, ndm0, ds1, ndm1;
 
   __device__ __forceinline__ void load(const uint8_t* rp, int gc, int t) {
     if constexpr (T == LRS_GGML_Q4_K || T == LRS_GGML_Q5_K) {
@@ -158,7 +208,7 @@ struct AFrag {
         mn = (byte_of(hd.w, j) >> 4) | ((byte_of(hd.z, j) >> 6) << 4);
       }
       ds0 = ds1 = f16_bits((uint16_t)(hd.x & 0xffffu)) * (float)sc;
-      dm0 = dm1 = f16_bits((uint16_t)(hd.x >> 16)) * (float)mn;
+      ndm0 = ndm1 = -f16_bits((uint16_t)(hd.x >> 16)) * (float)mn;
     } else if constexpr (T == LRS_GGML_Q6_K) {
       // ql[128], qh[64], scales[16] (i8), d; value_at, src/quant.rs:441-456
       const uint8_t* u = rp + (size_t)(gc >> 3) * 210;
@@ -174,8 +224,8 @@ struct AFrag {
       const uint16_t sp = ldg16(u + 192 + half * 8 + quarter * 2);
       ds0 = d * (float)(int8_t)(sp & 0xffu);
       ds1 = d * (float)(int8_t)(sp >> 8);
-      dm0 = 32.0f * ds0;
-      dm1 = 32.0f * ds1;
+      ndm0 = -32.0f * ds0;
+      ndm1 = -32.0f * ds1;
     } else {
       // 32-value blocks: d, (m), (qh[4]), qs[16] or Q8_0 d, qs[32]
       const uint8_t* u = rp + (size_t)gc * BlockTraits<T>::kBytes;
@@ -184,7 +234,7 @@ struct AFrag {
       if constexpr (T == LRS_GGML_Q8_0) {
         w0 = ldg32_a2(u + 2 + 4 * t);
         w1 = ldg32_a2(u + 18 + 4 * t);
-        dm0 = dm1 = 0.0f;
+        ndm0 = ndm1 = 0.0f;
       } else {
         constexpr int qs = T == LRS_GGML_Q4_0 ? 2 : T == LRS_GGML_Q4_1 ? 4 : T == LRS_GGML_Q5_0 ? 6 : 8;
         const uint32_t q = ldg32_a2(u + qs + 4 * t);
@@ -196,9 +246,9 @@ struct AFrag {
           w1 |= spread4(qh >> (16 + 4 * t)) << 4;
         }
         if constexpr (T == LRS_GGML_Q4_1 || T == LRS_GGML_Q5_1) {
-          dm0 = dm1 = -f16_bits(ldg16(u + 2));
+          ndm0 = ndm1 = f16_bits(ldg16(u + 2));
         } else {
-          dm0 = dm1 = (T == LRS_GGML_Q4_0 ? 8.0f : 16.0f) * d;
+          ndm0 = ndm1 = (T == LRS_GGML_Q4_0 ? -8.0f : -16.0f) * d;
         }
       }
     }
@@ -208,82 +258,91 @@ struct AFrag {
 struct GemmArgs {
   GemvSeg seg[kGemvMaxSeg];
   int cta0[kGemvMaxSeg + 1];  // first row-CTA of each segment
-  int nseg, cols, batch, epi, kper, kgroups;
-  const int8_t* xh;  // [batch][cols]
-  const int8_t* xl;
-  const float* sx;   // [batch][cols/32]
-  const float* X16;  // [batch][cols/16]
+  int nseg, cols, batch, epi, kgroups, tiles;  // tiles: item tiles of the x layout
+  const uint8_t* xq;  // records of tile 0 of this launch's items
+  const float* xs;
   float* part[kGemvMaxSeg];  // [pair][kgroups][batch][rows], kgroups > 1
   unsigned long long* keys;  // [batch], EPI_ARGMAX
 };
 
-// Adds one 32-column group of 16 rows x (8 * ntile) items into acc.
-template <int T>
-__device__ __forceinline__ void group_mma(float (&acc)[8][4], const AFrag<T>& fa,
-                                          const AFrag<T>& fb, const int8_t* sxh,
-                                          const int8_t* sxl, const float* ssx, const float* sX16,
-                                          int g, int ntile, int gid, int t) {
+// Adds one 32-column group of 16 rows x 8*NT items into acc.
+template <int T, int NT>
+__device__ __forceinline__ void group_mma(float (&acc)[NT][4], const AFrag<T>& fa,
+                                          const AFrag<T>& fb, const uint4* xr,
+                                          const float4* sr) {
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    if (j >= ntile) break;
-    const int bn = 8 * j + gid;
-    const uint32_t* xh = reinterpret_cast<const uint32_t*>(sxh + bn * kXStride + g * 32 + 4 * t);
-    const uint32_t* xl = reinterpret_cast<const uint32_t*>(sxl + bn * kXStride + g * 32 + 4 * t);
-    const uint32_t bh0 = xh[0], bh1 = xh[4], bl0 = xl[0], bl1 = xl[4];
-    const int i0 = 8 * j + 2 * t;
-    const float2 s = *reinterpret_cast<const float2*>(ssx + g * kMaxItems + i0);
-    const float2 xa = *reinterpret_cast<const float2*>(sX16 + (2 * g) * kMaxItems + i0);
-    const float2 xb = *reinterpret_cast<const float2*>(sX16 + (2 * g + 1) * kMaxItems + i0);
+  for (int j = 0; j < NT; j++) {
+    const uint4 xv = xr[j * 32];
+    const float4 sv = sr[j * 8];  // {s0, s1, X0, X1}
     const int z[4] = {0, 0, 0, 0};
     if constexpr (T != LRS_GGML_Q6_K) {
       const uint32_t A[4] = {fa.w0, fb.w0, fa.w1, fb.w1};
       int d[4], e[4];
-      mma_k32(d, A, bh0, bh1, z);
+      mma_k32(d, A, xv.x, xv.y, z);
       const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-      mma_k32(e, A, bl0, bl1, c);
-      const float X0 = xa.x + xb.x, X1 = xa.y + xb.y;
-      // e[0], e[1]: row gid, items i0, i0+1; e[2], e[3]: row gid+8
-      acc[j][0] = fmaf(fa.ds0, s.x * (float)e[0], fmaf(-fa.dm0, X0, acc[j][0]));
-      acc[j][1] = fmaf(fa.ds0, s.y * (float)e[1], fmaf(-fa.dm0, X1, acc[j][1]));
-      acc[j][2] = fmaf(fb.ds0, s.x * (float)e[2], fmaf(-fb.dm0, X0, acc[j][2]));
-      acc[j][3] = fmaf(fb.ds0, s.y * (float)e[3], fmaf(-fb.dm0, X1, acc[j][3]));
+      mma_k32(e, A, xv.z, xv.w, c);
+      // e[0], e[1]: row gid, items 2t, 2t+1; e[2], e[3]: row gid+8
+      acc[j][0] = fmaf(fa.ds0, sv.x * (float)e[0], fmaf(fa.ndm0, sv.z, acc[j][0]));
+      acc[j][1] = fmaf(fa.ds0, sv.y * (float)e[1], fmaf(fa.ndm0, sv.w, acc[j][1]));
+      acc[j][2] = fmaf(fb.ds0, sv.x * (float)e[2], fmaf(fb.ndm0, sv.z, acc[j][2]));
+      acc[j][3] = fmaf(fb.ds0, sv.y * (float)e[3], fmaf(fb.ndm0, sv.w, acc[j][3]));
     } else {
+      const float4 hv = sr[j * 8 + 1];  // {Xa0, Xa1, Xb0, Xb1}
       {
         const uint32_t A[2] = {fa.w0, fb.w0};
         int d[4], e[4];
-        mma_k16(d, A, bh0, z);
+        mma_k16(d, A, xv.x, z);
         const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-        mma_k16(e, A, bl0, c);
-        acc[j][0] = fmaf(fa.ds0, s.x * (float)e[0], fmaf(-fa.dm0, xa.x, acc[j][0]));
-        acc[j][1] = fmaf(fa.ds0, s.y * (float)e[1], fmaf(-fa.dm0, xa.y, acc[j][1]));
-        acc[j][2] = fmaf(fb.ds0, s.x * (float)e[2], fmaf(-fb.dm0, xa.x, acc[j][2]));
-        acc[j][3] = fmaf(fb.ds0, s.y * (float)e[3], fmaf(-fb.dm0, xa.y, acc[j][3]));
+        mma_k16(e, A, xv.z, c);
+        acc[j][0] = fmaf(fa.ds0, sv.x * (float)e[0], fmaf(fa.ndm0, hv.x, acc[j][0]));
+        acc[j][1] = fmaf(fa.ds0, sv.y * (float)e[1], fmaf(fa.ndm0, hv.y, acc[j][1]));
+        acc[j][2] = fmaf(fb.ds0, sv.x * (float)e[2], fmaf(fb.ndm0, hv.x, acc[j][2]));
+        acc[j][3] = fmaf(fb.ds0, sv.y * (float)e[3], fmaf(fb.ndm0, hv.y, acc[j][3]));
       }
       {
         const uint32_t A[2] = {fa.w1, fb.w1};
         int d[4], e[4];
-        mma_k16(d, A, bh1, z);
+        mma_k16(d, A, xv.y, z);
         const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-        mma_k16(e, A, bl1, c);
-        acc[j][0] = fmaf(fa.ds1, s.x * (float)e[0], fmaf(-fa.dm1, xb.x, acc[j][0]));
-        acc[j][1] = fmaf(fa.ds1, s.y * (float)e[1], fmaf(-fa.dm1, xb.y, acc[j][1]));
-        acc[j][2] = fmaf(fb.ds1, s.x * (float)e[2], fmaf(-fb.dm1, xb.x, acc[j][2]));
-        acc[j][3] = fmaf(fb.ds1, s.y * (float)e[3], fmaf(-fb.dm1, xb.y, acc[j][3]));
+        mma_k16(e, A, xv.w, c);
+        acc[j][0] = fmaf(fa.ds1, sv.x * (float)e[0], fmaf(fa.ndm1, hv.z, acc[j][0]));
+        acc[j][1] = fmaf(fa.ds1, sv.y * (float)e[1], fmaf(fa.ndm1, hv.w, acc[j][1]));
+        acc[j][2] = fmaf(fb.ds1, sv.x * (float)e[2], fmaf(fb.ndm1, hv.z, acc[j][2]));
+        acc[j][3] = fmaf(fb.ds1, sv.y * (float)e[3], fmaf(fb.ndm1, hv.w, acc[j][3]));
       }
     }
   }
 }
 
-template <int T, bool PAIR>
-__global__ void __launch_bounds__(kWarps * 32) gemm_i8_kernel(const __grid_constant__ GemmArgs a) {
+// Copies the x records of chunk kc (all NT tiles) into buffer `buf`.
+template <int NT, int THREADS>
+__device__ __forceinline__ void stage_chunk(const GemmArgs& a, int kc, uint8_t* buf) {
+  const int g0 = kc * kGroupsPerChunk;
+  const int ng = min(kGroupsPerChunk, a.cols / 32 - g0);
+  uint8_t* sx = buf;
+  uint8_t* ss = buf + kGroupsPerChunk * NT * kXRec;
+  constexpr int kXU = NT * kXRec / 16, kSU = NT * kSRec / 16;  // 16-byte units per group
+  for (int i = threadIdx.x; i < ng * (kXU + kSU); i += THREADS) {
+    const int g = i / (kXU + kSU), u = i % (kXU + kSU);
+    if (u < kXU) {
+      cp_async16(sx + (g * kXU + u) * 16,
+                 a.xq + ((size_t)(g0 + g) * a.tiles) * kXRec + u * 16);
+    } else {
+      cp_async16(ss + (g * kSU + (u - kXU)) * 16,
+                 reinterpret_cast<const uint8_t*>(a.xs) + ((size_t)(g0 + g) * a.tiles) * kSRec +
+                     (u - kXU) * 16);
+    }
+  }
+}
+
+template <int T, bool PAIR, int NT>
+__global__ void __launch_bounds__(Shape<PAIR>::kThreads)
+    gemm_i8_kernel(const __grid_constant__ GemmArgs a) {
+  using S = Shape<PAIR>;
+  constexpr int kBuf = kGroupsPerChunk * NT * (kXRec + kSRec);
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ unsigned long long skeys[kMaxItems];
   const int B = a.batch;
-  const int ntile = (B + 7) >> 3, Bp = ntile * 8;
-  int8_t* sxh = reinterpret_cast<int8_t*>(smem);
-  int8_t* sxl = sxh + Bp * kXStride;
-  float* ssx = reinterpret_cast<float*>(sxl + Bp * kXStride);  // [kKC/32][kMaxItems]
-  float* sX16 = ssx + (kKC / 32) * kMaxItems;                   // [kKC/16][kMaxItems]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, t = lane & 3;
 
@@ -292,91 +351,85 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_i8_kernel(const __grid_const
   const uint8_t* W = a.seg[s].w;
   const uint8_t* W2 = a.seg[s].w2;
   const int rows = a.seg[s].rows, rb = a.seg[s].rb;
-  const int rbase = ((int)blockIdx.x - a.cta0[s]) * kRowsCTA + warp * 16;
+  const int rbase = ((int)blockIdx.x - a.cta0[s]) * S::kRows + warp * 16;
   const int ra = min(rbase + gid, rows - 1), rbr = min(rbase + gid + 8, rows - 1);
   const uint8_t* rpa = W + (size_t)ra * rb;
   const uint8_t* rpb = W + (size_t)rbr * rb;
   const uint8_t* upa = PAIR ? W2 + (size_t)ra * rb : nullptr;
   const uint8_t* upb = PAIR ? W2 + (size_t)rbr * rb : nullptr;
+  const bool active = rbase < rows;
   if (tid < kMaxItems) skeys[tid] = 0ull;
 
-  float acc[8][4], acc2[PAIR ? 8 : 1][4];
+  float acc[NT][4], acc2[PAIR ? NT : 1][4];
 #pragma unroll
-  for (int j = 0; j < 8; j++)
+  for (int j = 0; j < NT; j++)
 #pragma unroll
     for (int c = 0; c < 4; c++) acc[j][c] = 0.0f;
 #pragma unroll
-  for (int j = 0; j < (PAIR ? 8 : 1); j++)
+  for (int j = 0; j < (PAIR ? NT : 1); j++)
 #pragma unroll
     for (int c = 0; c < 4; c++) acc2[j][c] = 0.0f;
 
-  const int kch = (a.cols + kKC - 1) / kKC;
-  const int k0 = blockIdx.y * a.kper, k1 = min(kch, k0 + a.kper);
-  for (int kc = k0; kc < k1; kc++) {
-    const int c0 = kc * kKC;
-    const int ncol = min(kKC, a.cols - c0);
-    const int ng = ncol >> 5;
-    __syncthreads();
-    for (int i = tid; i < Bp * (ncol >> 4); i += kWarps * 32) {
-      const int b = i / (ncol >> 4), c = (i % (ncol >> 4)) * 16;
-      uint4 vh = make_uint4(0, 0, 0, 0), vl = vh;
-      if (b < B) {
-        vh = *reinterpret_cast<const uint4*>(a.xh + (size_t)b * a.cols + c0 + c);
-        vl = *reinterpret_cast<const uint4*>(a.xl + (size_t)b * a.cols + c0 + c);
-      }
-      *reinterpret_cast<uint4*>(sxh + b * kXStride + c) = vh;
-      *reinterpret_cast<uint4*>(sxl + b * kXStride + c) = vl;
-    }
-    for (int i = tid; i < Bp * ng; i += kWarps * 32) {
-      const int g = i / Bp, b = i % Bp;
-      float v = 0.0f, h0 = 0.0f, h1 = 0.0f;
-      if (b < B) {
-        v = a.sx[(size_t)b * (a.cols >> 5) + (c0 >> 5) + g];
-        h0 = a.X16[(size_t)b * (a.cols >> 4) + (c0 >> 4) + 2 * g];
-        h1 = a.X16[(size_t)b * (a.cols >> 4) + (c0 >> 4) + 2 * g + 1];
-      }
-      ssx[g * kMaxItems + b] = v;
-      sX16[(2 * g) * kMaxItems + b] = h0;
-      sX16[(2 * g + 1) * kMaxItems + b] = h1;
-    }
-    __syncthreads();
-    if (rbase >= rows) continue;
-    const int gc0 = c0 >> 5;
-    AFrag<T> fa, fb, ua, ub;
-    fa.load(rpa, gc0, t);
-    fb.load(rpb, gc0, t);
+  const int kch = (a.cols + kChunkCols - 1) / kChunkCols;
+  const int k0 = (int)((long long)blockIdx.y * kch / a.kgroups);
+  const int k1 = (int)((long long)(blockIdx.y + 1) * kch / a.kgroups);
+  const int gend = min(k1 * kGroupsPerChunk, a.cols / 32);
+  stage_chunk<NT, S::kThreads>(a, k0, smem);
+  cp_async_commit();
+
+  AFrag<T> fa, fb, ua, ub;
+  int gc = k0 * kGroupsPerChunk;
+  if (active) {
+    fa.load(rpa, gc, t);
+    fb.load(rpb, gc, t);
     if constexpr (PAIR) {
-      ua.load(upa, gc0, t);
-      ub.load(upb, gc0, t);
+      ua.load(upa, gc, t);
+      ub.load(upb, gc, t);
     }
-    for (int g = 0; g < ng; g++) {
-      AFrag<T> na, nb, nua, nub;
-      const int gn = g + 1 < ng ? g + 1 : g;  // prefetch the next group's codes
-      na.load(rpa, gc0 + gn, t);
-      nb.load(rpb, gc0 + gn, t);
-      if constexpr (PAIR) {
-        nua.load(upa, gc0 + gn, t);
-        nub.load(upb, gc0 + gn, t);
-      }
-      group_mma<T>(acc, fa, fb, sxh, sxl, ssx, sX16, g, ntile, gid, t);
-      if constexpr (PAIR) group_mma<T>(acc2, ua, ub, sxh, sxl, ssx, sX16, g, ntile, gid, t);
-      fa = na;
-      fb = nb;
-      if constexpr (PAIR) {
-        ua = nua;
-        ub = nub;
+  }
+  for (int kc = k0; kc < k1; kc++) {
+    uint8_t* buf = smem + ((kc - k0) & 1) * kBuf;
+    if (kc + 1 < k1) {
+      stage_chunk<NT, S::kThreads>(a, kc + 1, smem + ((kc + 1 - k0) & 1) * kBuf);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int ng = min(kGroupsPerChunk, a.cols / 32 - kc * kGroupsPerChunk);
+    if (active) {
+      const uint4* xr = reinterpret_cast<const uint4*>(buf) + lane;
+      const float4* sr = reinterpret_cast<const float4*>(buf + kGroupsPerChunk * NT * kXRec) + t * 2;
+      for (int g = 0; g < ng; g++, gc++) {
+        AFrag<T> na, nb, nua, nub;
+        const int gn = gc + 1 < gend ? gc + 1 : gc;  // next group's codes, one group ahead
+        na.load(rpa, gn, t);
+        nb.load(rpb, gn, t);
+        if constexpr (PAIR) {
+          nua.load(upa, gn, t);
+          nub.load(upb, gn, t);
+        }
+        group_mma<T, NT>(acc, fa, fb, xr + g * NT * 32, sr + g * NT * 8);
+        if constexpr (PAIR) group_mma<T, NT>(acc2, ua, ub, xr + g * NT * 32, sr + g * NT * 8);
+        fa = na;
+        fb = nb;
+        if constexpr (PAIR) {
+          ua = nua;
+          ub = nub;
+        }
       }
     }
+    __syncthreads();  // buffer kc is refilled by iteration kc + 1's stage of kc + 2
   }
 
   // ---- output ----
   if (a.kgroups > 1) {
-    if (rbase < rows) {
+    if (active) {
       float* pp = a.part[s] + (size_t)blockIdx.y * B * rows;
       float* pp2 = pp + (size_t)a.kgroups * B * rows;
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        if (j >= ntile) break;
+      for (int j = 0; j < NT; j++)
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int i = 8 * j + 2 * t + (c & 1), r = rbase + gid + (c >> 1) * 8;
@@ -385,7 +438,6 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_i8_kernel(const __grid_const
             if constexpr (PAIR) pp2[(size_t)i * rows + r] = acc2[PAIR ? j : 0][c];
           }
         }
-      }
     }
     return;
   }
@@ -393,13 +445,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_i8_kernel(const __grid_const
   float* out = a.seg[s].out;
   const int out_ld = a.seg[s].out_ld;
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    if (j >= ntile) break;
+  for (int j = 0; j < NT; j++) {
     unsigned long long key[2] = {0ull, 0ull};
 #pragma unroll
     for (int c = 0; c < 4; c++) {
       const int i = 8 * j + 2 * t + (c & 1), r = rbase + gid + (c >> 1) * 8;
-      if (i < B && r < rows) {
+      if (active && i < B && r < rows) {
         float y = acc[j][c];
         float* o = out ? out + (size_t)i * out_ld + r : nullptr;
         if (a.epi == EPI_STORE) {
@@ -481,37 +532,46 @@ __global__ void __launch_bounds__(256) gemm_epilogue_kernel(const __grid_constan
   }
 }
 
-size_t gemm_smem(int batch) {
-  const int Bp = (batch + 7) & ~7;
-  return (size_t)Bp * kXStride * 2 + (size_t)(kKC / 32) * kMaxItems * 4 +
-         (size_t)(kKC / 16) * kMaxItems * 4;
+template <int NT>
+constexpr size_t smem_for() {
+  return 2 * (size_t)kGroupsPerChunk * NT * (kXRec + kSRec);
 }
 
-template <int T, bool PAIR>
+template <int T, bool PAIR, int NT>
 cudaError_t launch_t(const GemmArgs& a, dim3 grid, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<T, PAIR>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<T, PAIR, NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemm_smem(kMaxItems));
+                                         (int)smem_for<NT>());
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gemm_i8_kernel<T, PAIR><<<grid, kWarps * 32, gemm_smem(a.batch), st>>>(a);
+  gemm_i8_kernel<T, PAIR, NT><<<grid, Shape<PAIR>::kThreads, smem_for<NT>(), st>>>(a);
   return cudaGetLastError();
 }
 
+template <int T, bool PAIR>
+cudaError_t launch_nt(int nt, const GemmArgs& a, dim3 grid, cudaStream_t st) {
+  switch (nt) {
+    case 1: return launch_t<T, PAIR, 1>(a, grid, st);
+    case 2: return launch_t<T, PAIR, 2>(a, grid, st);
+    case 4: return launch_t<T, PAIR, 4>(a, grid, st);
+    default: return launch_t<T, PAIR, 8>(a, grid, st);
+  }
+}
+
 template <bool PAIR>
-cudaError_t launch_type(int type, const GemmArgs& a, dim3 grid, cudaStream_t st) {
+cudaError_t launch_type(int type, int nt, const GemmArgs& a, dim3 grid, cudaStream_t st) {
   switch (type) {
-    case LRS_GGML_Q4_0: return launch_t<LRS_GGML_Q4_0, PAIR>(a, grid, st);
-    case LRS_GGML_Q4_1: return launch_t<LRS_GGML_Q4_1, PAIR>(a, grid, st);
-    case LRS_GGML_Q5_0: return launch_t<LRS_GGML_Q5_0, PAIR>(a, grid, st);
-    case LRS_GGML_Q5_1: return launch_t<LRS_GGML_Q5_1, PAIR>(a, grid, st);
-    case LRS_GGML_Q8_0: return launch_t<LRS_GGML_Q8_0, PAIR>(a, grid, st);
-    case LRS_GGML_Q4_K: return launch_t<LRS_GGML_Q4_K, PAIR>(a, grid, st);
-    case LRS_GGML_Q5_K: return launch_t<LRS_GGML_Q5_K, PAIR>(a, grid, st);
-    case LRS_GGML_Q6_K: return launch_t<LRS_GGML_Q6_K, PAIR>(a, grid, st);
+    case LRS_GGML_Q4_0: return launch_nt<LRS_GGML_Q4_0, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q4_1: return launch_nt<LRS_GGML_Q4_1, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q5_0: return launch_nt<LRS_GGML_Q5_0, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q5_1: return launch_nt<LRS_GGML_Q5_1, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q8_0: return launch_nt<LRS_GGML_Q8_0, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q4_K: return launch_nt<LRS_GGML_Q4_K, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q5_K: return launch_nt<LRS_GGML_Q5_K, PAIR>(nt, a, grid, st);
+    case LRS_GGML_Q6_K: return launch_nt<LRS_GGML_Q6_K, PAIR>(nt, a, grid, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -525,13 +585,16 @@ bool quantized(int type) {
   return false;
 }
 
-// K groups for a launch of `row_ctas` row CTAs over `kch` chunks: 1 when the
-// rows alone give every SM two CTAs, else enough K groups to get there.
-int kgroups_for(int row_ctas, int kch, int sms, int* kper) {
-  int kg = 1;
-  if (row_ctas < 2 * sms) kg = std::min(kch, (2 * sms + row_ctas - 1) / row_ctas);
-  *kper = (kch + kg - 1) / kg;
-  return (kch + *kper - 1) / *kper;
+int tiles_for(int items) {  // item tiles of one launch: 1, 2, 4 or 8
+  const int need = (items + 7) / 8;
+  return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+}
+
+// Tiles of the split-x layout for `batch` items: 8 per full 64-item block
+// plus the last block's (padded) tile count.
+int layout_tiles(int batch) {
+  const int full = (batch - 1) / kMaxItems;
+  return full * kMaxTiles + tiles_for(batch - full * kMaxItems);
 }
 
 }  // namespace
@@ -544,33 +607,34 @@ bool gemm_supported(const GemvParams& p) {
 }
 
 size_t gemm_scratch_bytes(int batch, int max_cols, int sms) {
-  const size_t B = std::min(batch, kMaxItems);
-  const size_t xq = (size_t)batch * max_cols * 2 + (size_t)batch * (max_cols / 32) * 4 +
-                    (size_t)batch * (max_cols / 16) * 4 + 1024;
-  // kgroups > 1 only when row CTAs < 2*sms, and then kgroups * rows is at
-  // most (2*sms + row_ctas) * kRowsCTA per matrix of the pair.
-  const size_t parts = (size_t)(4 * sms) * kRowsCTA * B * 4 * 2 + 1024;
+  const size_t tiles = layout_tiles(std::max(batch, 1));
+  const size_t xq = (size_t)(max_cols / 32) * tiles * (kXRec + kSRec) + 1024;
+  // kgroups > 1 only when the row CTAs do not fill the SMs; then kgroups *
+  // rows <= 2 * sms * 256 for a launch (a pair has half the rows of a CTA).
+  const size_t parts = (size_t)(2 * sms) * 256 * std::min(batch, kMaxItems) * 4 + 1024;
   return xq + parts;
 }
 
 cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t st) {
   const int Ball = p.batch, cols = p.cols;
   const bool pair = p.epi == EPI_SWIGLU;
-  const int kch = (cols + kKC - 1) / kKC;
+  const int kch = (cols + kChunkCols - 1) / kChunkCols;
+  const int tiles = layout_tiles(Ball);
   auto align = [](void* q) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255));
   };
-  int8_t* xh = reinterpret_cast<int8_t*>(align(scratch));
-  int8_t* xl = xh + (size_t)Ball * cols;
-  float* sx = reinterpret_cast<float*>(align(xl + (size_t)Ball * cols));
-  float* X16 = sx + (size_t)Ball * (cols / 32);
-  float* part = reinterpret_cast<float*>(align(X16 + (size_t)Ball * (cols / 16)));
-  xsplit_kernel<<<dim3((cols / 32 + 7) / 8, Ball), 256, 0, st>>>(p.x, p.x_ld, cols, xh, xl, sx,
-                                                                  X16);
+  uint8_t* xq = align(scratch);
+  float* xs = reinterpret_cast<float*>(xq + (size_t)(cols / 32) * tiles * kXRec);
+  float* part = reinterpret_cast<float*>(
+      align(reinterpret_cast<uint8_t*>(xs) + (size_t)(cols / 32) * tiles * kSRec));
+  xsplit_kernel<<<dim3((cols / 32 + 7) / 8, tiles * 8), 256, 0, st>>>(p.x, p.x_ld, cols, Ball,
+                                                                       tiles, xq, xs);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  const int rows_cta = pair ? Shape<true>::kRows : Shape<false>::kRows;
   for (int b0 = 0; b0 < Ball; b0 += kMaxItems) {
     const int B = std::min(kMaxItems, Ball - b0);
+    const int nt = tiles_for(B);
     // one launch per run of same-type segments
     int i = 0;
     while (i < p.nseg) {
@@ -581,20 +645,20 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
       a.cols = cols;
       a.batch = B;
       a.epi = p.epi;
-      a.xh = xh + (size_t)b0 * cols;
-      a.xl = xl + (size_t)b0 * cols;
-      a.sx = sx + (size_t)b0 * (cols / 32);
-      a.X16 = X16 + (size_t)b0 * (cols / 16);
+      a.tiles = tiles;
+      a.xq = xq + (size_t)(b0 / 8) * kXRec;
+      a.xs = xs + (size_t)(b0 / 8) * (kSRec / 4);
       a.keys = p.argmax_keys ? p.argmax_keys + b0 : nullptr;
       int ctas = 0;
       for (int k = 0; k < a.nseg; k++) {
         a.seg[k] = p.seg[i + k];
         if (a.seg[k].out) a.seg[k].out += (size_t)b0 * a.seg[k].out_ld;
         a.cta0[k] = ctas;
-        ctas += (a.seg[k].rows + kRowsCTA - 1) / kRowsCTA;
+        ctas += (a.seg[k].rows + rows_cta - 1) / rows_cta;
       }
       a.cta0[a.nseg] = ctas;
-      a.kgroups = kgroups_for(ctas, kch, sms, &a.kper);
+      // one wave: at most `sms` CTAs (one resident CTA per SM)
+      a.kgroups = ctas >= sms ? 1 : std::min(kch, sms / ctas);
       EpiArgs ea = {};
       if (a.kgroups > 1) {
         float* cur = part;
@@ -615,8 +679,8 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
         ea.keys = a.keys;
       }
       const dim3 grid(ctas, a.kgroups);
-      e = pair ? launch_type<true>(a.seg[0].type, a, grid, st)
-               : launch_type<false>(a.seg[0].type, a, grid, st);
+      e = pair ? launch_type<true>(a.seg[0].type, nt, a, grid, st)
+               : launch_type<false>(a.seg[0].type, nt, a, grid, st);
       if (e != cudaSuccess) return e;
       if (a.kgroups > 1) {
         gemm_epilogue_kernel<<<dim3((ea.row0[ea.nseg] + 255) / 256, B), 256, 0, st>>>(ea);
