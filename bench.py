@@ -125,9 +125,30 @@ def launches_per_step(layers, batch):
     return 1 + layers * per_layer + (2 if batch == 1 else 3)
 
 
-def build_model(lrs, wl, threads=0):
-    cfg = getattr(lrs, wl["cfg"])()
-    return cfg, lrs.SynthModel(cfg, wl["seed"], lrs.LoadQuantization[wl["recipe"]], threads=threads)
+def model_cache_path(wl):
+    return os.path.join(tempfile.gettempdir(),
+                        f"llamars_{wl['cfg']}_s{wl['seed']}_{wl['recipe']}_v1.lrs")
+
+
+def build_model(lrs, wl, threads=0, barrier=None, builder=True):
+    """The workload's synthetic model.  The pre-quantized bytes are cached in a
+    flat file under the temp directory: the builder (local rank 0) generates
+    and writes it when absent, the other ranks wait at `barrier` and map it."""
+    path = model_cache_path(wl)
+    if builder and not os.path.exists(path):
+        cfg = getattr(lrs, wl["cfg"])()
+        sm = lrs.SynthModel(cfg, wl["seed"], lrs.LoadQuantization[wl["recipe"]], threads=threads)
+        try:
+            lrs.save_model_file(sm.desc(), path)
+        except OSError:
+            if barrier is None:
+                return cfg, sm
+            raise
+        del sm
+    if barrier is not None:
+        barrier()
+    mf = lrs.ModelFile(path)
+    return mf.config, mf
 
 
 def cpu_decode_rate(orc, lrs, sm, cfg, wl, threads, budget_s=15.0):
@@ -215,7 +236,7 @@ def run_ours(args, wl):
     ncpu = os.cpu_count() or 1
 
     t_build = time.perf_counter()
-    cfg, sm = build_model(lrs, wl, max(1, ncpu // world))
+    cfg, sm = build_model(lrs, wl, ncpu, barrier if world > 1 else None, builder=local == 0)
     build_s = time.perf_counter() - t_build
     be = lrs.CudaBackend(local)
     model = lrs.CudaQwen2Model(be, sm.desc(), max_seq_len=wl["ctx"], max_sequences=B,

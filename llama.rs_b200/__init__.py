@@ -479,6 +479,116 @@ class SynthModel:
                            QuantType(td.ggml_type))
 
 
+_MF_MAGIC = b"LRSMODL1"
+_MF_LAYER_TENSORS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+_MF_LAYER_VECS = ("input_layernorm", "post_attention_layernorm", "q_bias", "k_bias", "v_bias")
+
+
+def save_model_file(desc, path: str) -> None:
+    """Writes the host model behind an lrs_model_desc as one flat file: the
+    pre-quantized tensors (GGML block bytes, as the load-time quantizers of
+    src/loader.rs:406-447 left them), norms and biases, plus a JSON index.
+    A tied head (same bytes as the embedding) is stored once.  The file is
+    written under a temporary name and renamed, so readers never see a partial
+    file."""
+    import json
+    d = desc.contents
+    c = d.config
+    h, kvw = c.hidden_size, c.num_key_value_heads * c.head_dim
+    blobs, index = [], {}
+
+    def add(ptr, nbytes):
+        if not ptr:
+            return None
+        key = (int(ptr), int(nbytes))
+        if key not in index:
+            index[key] = len(blobs)
+            blobs.append(key)
+        return index[key]
+
+    def tens(td):
+        return {"blob": add(td.data, td.nbytes), "rows": int(td.rows), "cols": int(td.cols),
+                "type": int(td.ggml_type)}
+
+    cfg = {k: getattr(c, k) for k, _ in _Config._fields_}
+    meta = {"config": cfg, "embed_tokens": tens(d.embed_tokens), "lm_head": tens(d.lm_head),
+            "final_norm": add(d.final_norm, 4 * h), "layers": []}
+    vec_len = {"input_layernorm": h, "post_attention_layernorm": h, "q_bias": h,
+               "k_bias": kvw, "v_bias": kvw}
+    for i in range(c.num_hidden_layers):
+        L = d.layers[i]
+        ent = {n: tens(getattr(L, n)) for n in _MF_LAYER_TENSORS}
+        for n in _MF_LAYER_VECS:
+            ent[n] = add(getattr(L, n), 4 * vec_len[n])
+        meta["layers"].append(ent)
+    off = 0
+    table = []
+    for ptr, nbytes in blobs:
+        table.append([off, nbytes])
+        off += (nbytes + 63) // 64 * 64
+    meta["blobs"] = table
+    hdr = json.dumps(meta).encode()
+    data_start = (16 + len(hdr) + 63) // 64 * 64
+    tmp = f"{path}.tmp{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(_MF_MAGIC + len(hdr).to_bytes(8, "little") + hdr)
+        f.write(b"\0" * (data_start - 16 - len(hdr)))
+        for (ptr, nbytes), (o, _) in zip(blobs, table):
+            f.seek(data_start + o)
+            f.write((C.c_uint8 * nbytes).from_address(ptr))
+        f.truncate(data_start + off)
+    os.replace(tmp, path)
+
+
+class ModelFile:
+    """A model written by save_model_file, memory-mapped; ``desc()`` has the
+    same shape as SynthModel.desc() and stays valid while this object lives."""
+
+    def __init__(self, path: str):
+        import json
+        with open(path, "rb") as f:
+            head = f.read(16)
+            if head[:8] != _MF_MAGIC:
+                raise LrsError(1, f"{path}: not a model file")
+            n = int.from_bytes(head[8:16], "little")
+            meta = json.loads(f.read(n))
+        data_start = (16 + n + 63) // 64 * 64
+        self._map = np.memmap(path, dtype=np.uint8, mode="r")
+        base = self._map.ctypes.data + data_start
+        blobs = meta["blobs"]
+
+        def ptr(i):
+            return None if i is None else base + blobs[i][0]
+
+        def tens(t):
+            return _TensorDesc(ptr(t["blob"]), blobs[t["blob"]][1], t["rows"], t["cols"], t["type"], 0)
+
+        cfgd = meta["config"]
+        self.config = LlamaConfig(cfgd["hidden_size"], cfgd["intermediate_size"],
+                                  cfgd["num_attention_heads"], cfgd["num_key_value_heads"],
+                                  cfgd["num_hidden_layers"], cfgd["vocab_size"],
+                                  cfgd["rms_norm_eps"], cfgd["rope_theta"],
+                                  cfgd["max_position_embeddings"], cfgd["head_dim"],
+                                  meta["embed_tokens"]["blob"] == meta["lm_head"]["blob"])
+        nl = cfgd["num_hidden_layers"]
+        self._layers = (_LayerDesc * nl)()
+        for i, ent in enumerate(meta["layers"]):
+            L = self._layers[i]
+            for n in _MF_LAYER_TENSORS:
+                setattr(L, n, tens(ent[n]))
+            for n in _MF_LAYER_VECS:
+                setattr(L, n, ptr(ent[n]))
+        self._desc = _ModelDesc()
+        self._desc.config = _Config(*[cfgd[k] for k, _ in _Config._fields_])
+        self._desc.embed_tokens = tens(meta["embed_tokens"])
+        self._desc.lm_head = tens(meta["lm_head"])
+        self._desc.final_norm = ptr(meta["final_norm"])
+        self._desc.layers = C.cast(self._layers, C.POINTER(_LayerDesc))
+
+    def desc(self):
+        return C.pointer(self._desc)
+
+
 class CudaQwen2Model:
     """CausalModel on the CUDA backend (src/architecture.rs:42-78).
 

@@ -118,3 +118,34 @@ def test_synth_model_is_deterministic_and_follows_recipe(lrs):
     assert a.tensor("down_proj", 0).quant_type == lrs.QuantType.Q6_K
     d = a.desc().contents
     assert d.lm_head.data == d.embed_tokens.data  # tied head reuses the quantized embedding
+
+
+def test_model_file_round_trip(lrs, tmp_path):
+    """save_model_file / ModelFile reproduce the synthetic model byte for byte."""
+    for tied in (True, False):
+        cfg = lrs.LlamaConfig(256, 512, 4, 2, 2, 300, 1e-6, 1e6, 4096, 64, tied)
+        sm = lrs.SynthModel(cfg, 7, lrs.LoadQuantization.Q4KM)
+        path = str(tmp_path / f"m{int(tied)}.lrs")
+        lrs.save_model_file(sm.desc(), path)
+        mf = lrs.ModelFile(path)
+        got = mf.config
+        assert abs(got.rms_norm_eps - cfg.rms_norm_eps) < 1e-12
+        got.rms_norm_eps = cfg.rms_norm_eps
+        assert got == cfg
+        for name in ("embed", "lm_head"):
+            a = sm.tensor(name)
+            d = mf.desc().contents
+            td = d.embed_tokens if name == "embed" else d.lm_head
+            b = np.ctypeslib.as_array((ctypes.c_uint8 * td.nbytes).from_address(td.data))
+            assert td.ggml_type == int(a.quant_type) and np.array_equal(a.data, b)
+        for i in range(cfg.num_hidden_layers):
+            for n in ("q_proj", "v_proj", "down_proj"):
+                a = sm.tensor(n, i)
+                td = getattr(mf.desc().contents.layers[i], n)
+                b = np.ctypeslib.as_array((ctypes.c_uint8 * td.nbytes).from_address(td.data))
+                assert np.array_equal(a.data, b)
+            for n, width in (("input_layernorm", 256), ("k_bias", 128)):
+                pa = getattr(sm.desc().contents.layers[i], n)
+                pb = getattr(mf.desc().contents.layers[i], n)
+                assert np.array_equal(np.ctypeslib.as_array((ctypes.c_float * width).from_address(pa)),
+                                      np.ctypeslib.as_array((ctypes.c_float * width).from_address(pb)))
