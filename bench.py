@@ -126,8 +126,9 @@ def launches_per_step(layers, batch):
 
 
 def model_cache_path(wl):
+    layers = f"_L{wl['layers']}" if wl.get("layers") else ""
     return os.path.join(tempfile.gettempdir(),
-                        f"llamars_{wl['cfg']}_s{wl['seed']}_{wl['recipe']}_v1.lrs")
+                        f"llamars_{wl['cfg']}{layers}_s{wl['seed']}_{wl['recipe']}_v1.lrs")
 
 
 def build_model(lrs, wl, threads=0, barrier=None, builder=True):
@@ -137,6 +138,8 @@ def build_model(lrs, wl, threads=0, barrier=None, builder=True):
     path = model_cache_path(wl)
     if builder and not os.path.exists(path):
         cfg = getattr(lrs, wl["cfg"])()
+        if wl.get("layers"):
+            cfg.num_hidden_layers = wl["layers"]
         sm = lrs.SynthModel(cfg, wl["seed"], lrs.LoadQuantization[wl["recipe"]], threads=threads)
         try:
             lrs.save_model_file(sm.desc(), path)
@@ -274,11 +277,14 @@ def run_ours(args, wl):
     torch.cuda.synchronize()
     clocks.start()
     t0, t1 = ev(), ev()
+    torch.cuda.nvtx.range_push("lrs_decode_timed")
     t0.record(ext)
     model.decode_enqueue(firsts, pos, args.steps, seqs)
     t1.record(ext)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clock_info = clocks.stop()
+    step_kernels = model.step_kernels()
     barrier()
     step_ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
     toks = model.read_tokens(B, args.steps)
@@ -301,8 +307,13 @@ def run_ours(args, wl):
     e2e_value = total_seqs / (e2e_ms / 1e3)
 
     # ---- GEMV roofline: one step with per-launch CUDA events ----
-    gemv_ms, gemv_n, prof_step_ms = model.profile_step(firsts, pos, seqs)
+    gemv_ms, gemv_n, prof_step_ms, attn_ms = model.profile_step(firsts, pos, seqs)
     gemv_ms = max_over_ranks(gemv_ms)
+    attn_ms = max_over_ranks(attn_ms)
+    kv_elem = 2 if args.kv_bf16 else 4
+    kvw = cfg.num_key_value_heads * cfg.resolved_head_dim()
+    # K and V rows read by the step (positions 0..pos) plus the row written, all layers
+    kv_bytes = sum(2 * cfg.num_hidden_layers * kvw * kv_elem * (p + 2) for p in pos)
     wbytes = model.weight_bytes()
     hbm, peak_kind = peaks()
     achieved = wbytes / (gemv_ms / 1e3) / 1e9
@@ -318,7 +329,7 @@ def run_ours(args, wl):
         q1.record(ext)
         torch.cuda.synchronize()
         b1_ms = max_over_ranks(q0.elapsed_time(q1)) / args.steps
-        g1, n1, _ = model.profile_step([int(model.read_tokens(1, args.steps)[-1, 0])],
+        g1, n1, _, _ = model.profile_step([int(model.read_tokens(1, args.steps)[-1, 0])],
                                        [pos[0] + 3 + args.steps], [0])
         g1 = max_over_ranks(g1)
         b1 = {"decode_tok_s_per_gpu": 1e3 / b1_ms, "ms_per_step": b1_ms,
@@ -346,6 +357,8 @@ def run_ours(args, wl):
             "data": "synthetic (seeded random weights N(0,0.02), uniform prompt ids)",
             "config": {"workload": f"{wl['model']} {wl['quant']}: {total_seqs} sequences x "
                                    f"({P} prompt + greedy decode), ctx {wl['ctx']}, "
+                                   + (f"{cfg.num_hidden_layers} layers (profiling case), "
+                                      if wl.get("layers") else "") +
                                    f"data-parallel over {world} GPU(s)",
                        "sequences_per_gpu": B, "prompt": P,
                        "kv_cache": "bf16" if args.kv_bf16 else "f32",
@@ -354,15 +367,26 @@ def run_ours(args, wl):
                     "d2h_bytes_per_step": 4 * B + 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None,
-                         "kernel": "gemv_kernel (all GEMV launches of one decode step)",
+                         "kernel": ("gemm_i8_kernel: batched quantized matmul (x split, matmul, "
+                                    "K-split epilogue) of every projection and the LM head"
+                                    if B > 1 else "gemv5_kernel: batch-1 quantized GEMV"),
                          "bytes_per_launch": wbytes / gemv_n, "ms_per_launch": gemv_ms / gemv_n,
-                         "launches": gemv_n, "peak_kind": peak_kind},
+                         "launches": gemv_n, "peak_kind": peak_kind,
+                         "share_of_step": gemv_ms / prof_step_ms},
+            "attention": {"kernel": "rope_store + attn_split + attn_combine, all layers",
+                          "kv_bytes_per_step": kv_bytes, "ms": attn_ms,
+                          "achieved_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
+                          "frac": kv_bytes / (attn_ms / 1e3) / 1e9 / hbm,
+                          "share_of_step": attn_ms / prof_step_ms},
+            "step_hbm": {"bytes_per_step": wbytes + kv_bytes,
+                         "achieved_gbs": (wbytes + kv_bytes) / (step_ms / 1e3) / 1e9,
+                         "frac": (wbytes + kv_bytes) / (step_ms / 1e3) / 1e9 / hbm},
             "weight_stream_gbs": wbytes / (step_ms / 1e3) / 1e9,
             "prefill_tok_s": total_seqs * P / (prefill_ms / 1e3),
             "b1": b1,
             "cpu_baseline": cpu,
             "clocks": clock_info,
-            "gpu_launches": nl * args.steps,
+            "gpu_launches": (step_kernels or nl) * args.steps,
             "model_build_s": build_s,
         }
         print(json.dumps(line), flush=True)
@@ -438,6 +462,9 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="total sequences (default: the config's)")
     ap.add_argument("--prompt", type=int, default=0, help="prompt tokens (default: the config's)")
     ap.add_argument("--kv-bf16", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small profiling cases only)")
+    ap.add_argument("--ctx", type=int, default=0, help="override the context length")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
     ap.add_argument("--gemv-sweep", action="store_true", help="BASELINE config 1 GEMV sweep")
@@ -451,7 +478,11 @@ def main():
     if args.gemv_sweep:
         run_gemv_sweep(args)
         return
-    wl = WORKLOADS[args.config]
+    wl = dict(WORKLOADS[args.config])
+    if args.layers:
+        wl["layers"] = args.layers
+    if args.ctx:
+        wl["ctx"] = args.ctx
     if args.impl == "reference":
         run_reference(args, wl)
     else:

@@ -232,11 +232,16 @@ lrs_status lrs_model_read_tokens(lrs_model* model, size_t n_seqs, size_t n_steps
 /* Measurement hook (no counterpart in the reference): runs ONE greedy step for
  * the given items outside any CUDA graph, with every GEMV launch bracketed by
  * CUDA events on the model's stream.  Reports the summed GEMV time, the number
- * of GEMV launches and the whole step's time (milliseconds).  The step writes
- * the KV cache at `pos` like a normal decode step. */
+ * of GEMV launches, the whole step's time and the summed time of the per-layer
+ * RoPE/KV-store + attention launches (milliseconds; any pointer may be NULL).
+ * The step writes the KV cache at `pos` like a normal decode step. */
 lrs_status lrs_model_profile_step(lrs_model* model, size_t n_seqs, const uint32_t* seqs,
                                   const uint32_t* tokens, const uint32_t* pos, float* gemv_ms,
-                                  uint32_t* gemv_launches, float* step_ms);
+                                  uint32_t* gemv_launches, float* step_ms, float* attn_ms);
+
+/* Kernel launches in one decode step of the most recent decode_enqueue
+ * (kernel nodes of its CUDA graph); 0 before the first graph-captured step. */
+uint32_t lrs_model_step_kernels(const lrs_model* model);
 
 /* Device stream (cudaStream_t) the model and backend queue work on. */
 void* lrs_backend_stream(lrs_backend* backend);

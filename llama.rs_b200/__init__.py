@@ -179,7 +179,8 @@ _sig("lrs_model_decode_greedy", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c
 _sig("lrs_model_decode_enqueue", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c_size_t)
 _sig("lrs_model_read_tokens", C.c_int32, _P, C.c_size_t, C.c_size_t, _U32)
 _sig("lrs_model_weight_bytes", C.c_uint64, _P)
-_sig("lrs_model_profile_step", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, _F, _U32, _F)
+_sig("lrs_model_profile_step", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, _F, _U32, _F, _F)
+_sig("lrs_model_step_kernels", C.c_uint32, _P)
 _sig("lrs_recipe_type", C.c_uint32, C.c_uint32, C.c_char_p, C.c_size_t, C.c_size_t)
 _sig("lrs_quantize_matrix", C.c_int32, C.c_uint32, _F, C.c_size_t, C.c_size_t, _P, C.c_size_t,
      _U32, C.POINTER(C.c_size_t))
@@ -198,7 +199,7 @@ EXPORTED_SYMBOLS = (
     "lrs_model_create",
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
-    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
+    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
 )
 
@@ -677,18 +678,23 @@ class CudaQwen2Model:
         _check(_lib.lrs_model_read_tokens(self._h, n_seqs, n_steps, _uptr(out)))
         return out
 
+    def step_kernels(self) -> int:
+        """Kernel launches per decode step of the last decode_enqueue (graph nodes)."""
+        return int(_lib.lrs_model_step_kernels(self._h))
+
     def profile_step(self, tokens, pos, seqs=None):
-        """One greedy step outside the graph with per-GEMV CUDA events:
-        returns (gemv_ms, gemv_launches, step_ms)."""
+        """One greedy step outside the graph with per-GEMV and per-layer
+        attention CUDA events: returns (gemv_ms, gemv_launches, step_ms, attn_ms)."""
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         p = np.ascontiguousarray(pos, dtype=np.uint32)
         sq = np.ascontiguousarray(seqs if seqs is not None else range(t.size), dtype=np.uint32)
         g = np.zeros(1, np.float32)
         n = np.zeros(1, np.uint32)
         s = np.zeros(1, np.float32)
+        a = np.zeros(1, np.float32)
         _check(_lib.lrs_model_profile_step(self._h, t.size, _uptr(sq), _uptr(t), _uptr(p),
-                                           _fptr(g), _uptr(n), _fptr(s)))
-        return float(g[0]), int(n[0]), float(s[0])
+                                           _fptr(g), _uptr(n), _fptr(s), _fptr(a)))
+        return float(g[0]), int(n[0]), float(s[0]), float(a[0])
 
     def benchmark_tokens(self, prompt: Sequence[int], decode_tokens: int, seq: int = 0):
         """InferenceEngine::benchmark_tokens (src/engine.rs:189-223) on the device:

@@ -334,9 +334,13 @@ struct lrs_model {
   uint32_t* d_tokens_out = nullptr;
   size_t tokens_out_cap = 0;  // in elements
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  std::map<GraphKey, uint32_t> graph_kernels;  // kernel nodes per captured step
+  uint32_t last_step_kernels = 0;
   uint64_t weight_bytes = 0;
   // When set, every GEMV launch of enqueue_step is bracketed by two events.
   std::vector<cudaEvent_t>* prof = nullptr;
+  // When set, each layer's RoPE/KV store + attention launches are bracketed too.
+  std::vector<cudaEvent_t>* prof_attn = nullptr;
 };
 
 namespace {
@@ -442,10 +446,19 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     p.x_ld = h;
     LRS_CUDA(model_gemv(m, p, st, sms));
     // RoPE + KV store (src/model.rs:188-205), attention (:206-231)
+    cudaEvent_t a0 = nullptr, a1 = nullptr;
+    if (m->prof_attn) {
+      cudaEventCreate(&a0);
+      cudaEventCreate(&a1);
+      m->prof_attn->push_back(a0);
+      m->prof_attn->push_back(a1);
+      cudaEventRecord(a0, st);
+    }
     LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
                                L.kpool, L.vpool, kv_bf16, st));
     LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
                               m->att, st));
+    if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
     GemvMat om = mat_of(L.o, m->residual, h);
     if ((rc = gemv_plan(&p, &om, 1, EPI_ADD, B))) return rc;
@@ -792,6 +805,16 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
       cudaError_t e = cudaStreamEndCapture(st, &graph);
       if (rc) return rc;
       if (e != cudaSuccess) return fail(LRS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+      size_t nn = 0;
+      cudaGraphGetNodes(graph, nullptr, &nn);
+      std::vector<cudaGraphNode_t> nodes(nn);
+      uint32_t nk = 0;
+      if (nn && cudaGraphGetNodes(graph, nodes.data(), &nn) == cudaSuccess)
+        for (auto nd : nodes) {
+          cudaGraphNodeType ty;
+          if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) nk++;
+        }
+      m->graph_kernels[key] = nk;
       e = cudaGraphInstantiate(&exec, graph, 0);
       cudaGraphDestroy(graph);
       if (e != cudaSuccess)
@@ -800,6 +823,7 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
     } else {
       exec = it->second;
     }
+    m->last_step_kernels = m->graph_kernels[key];
     for (size_t s = 0; s < n_steps; s++) LRS_CUDA(cudaGraphLaunch(exec, st));
   } else {
     for (size_t s = 0; s < n_steps; s++)
@@ -807,6 +831,8 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
   }
   return LRS_OK;
 }
+
+uint32_t lrs_model_step_kernels(const lrs_model* m) { return m ? m->last_step_kernels : 0; }
 
 lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, uint32_t* out) {
   if (!m || !out) return fail(LRS_ERR_INVALID, "null argument");
@@ -820,7 +846,7 @@ lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, ui
 
 lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
                                   const uint32_t* tokens, const uint32_t* pos, float* gemv_ms,
-                                  uint32_t* gemv_launches, float* step_ms) {
+                                  uint32_t* gemv_launches, float* step_ms, float* attn_ms) {
   if (!m || !seqs || !tokens || !pos) return fail(LRS_ERR_INVALID, "null argument");
   if (n_seqs == 0 || n_seqs > (size_t)m->max_items) return fail(LRS_ERR_INVALID, "n_seqs out of range");
   LRS_CUDA(cudaSetDevice(m->be->device));
@@ -839,14 +865,16 @@ lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* s
   int32_t rc = set_items(m, B, tok.data(), ps.data(), sq.data());
   if (rc) return rc;
   cudaStream_t st = m->be->stream;
-  std::vector<cudaEvent_t> ev;
+  std::vector<cudaEvent_t> ev, aev;
   cudaEvent_t s0, s1;
   cudaEventCreate(&s0);
   cudaEventCreate(&s1);
   cudaEventRecord(s0, st);
   m->prof = &ev;
+  m->prof_attn = &aev;
   rc = enqueue_step(m, B, -1, false, true, 0);
   m->prof = nullptr;
+  m->prof_attn = nullptr;
   cudaEventRecord(s1, st);
   cudaError_t e = cudaStreamSynchronize(st);
   float total = 0.0f, step = 0.0f;
@@ -856,6 +884,14 @@ lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* s
     total += t;
   }
   cudaEventElapsedTime(&step, s0, s1);
+  float atotal = 0.0f;
+  for (size_t i = 0; i + 1 < aev.size(); i += 2) {
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, aev[i], aev[i + 1]);
+    atotal += t;
+  }
+  for (auto x : aev) cudaEventDestroy(x);
+  if (attn_ms) *attn_ms = atotal;
   for (auto x : ev) cudaEventDestroy(x);
   cudaEventDestroy(s0);
   cudaEventDestroy(s1);

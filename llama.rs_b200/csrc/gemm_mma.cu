@@ -1,6 +1,6 @@
-// gemm_i8.cu -- batched quantized matmul (decode batches of 2..64 sequences,
-// prefill chunks) on the integer tensor cores of sm_100a
-// (mma.sync m16n8k32 / m16n8k16, s8 x s8 -> s32).
+// gemm_mma.cu -- batched quantized matmul (decode batches of 2..64 sequences,
+// prefill chunks) on the tensor cores of sm_100a (mma.sync m16n8k16,
+// f16 x f16 -> f32).
 //
 // Replaces B independent CpuBackend::matvec calls (src/backend.rs:143-162)
 // for B >= 2 input vectors: the sequences of a decode batch, or the prompt
@@ -8,43 +8,45 @@
 // runs them one by one).
 //
 // Every quantized GGML type stores integer codes q with a per-group affine
-// map  w = ds * q - dm  (value_at, src/quant.rs:349-456):
-//   Q4_0: ds = d, dm = 8d        Q4_1: ds = d, dm = -m
-//   Q5_0: ds = d, dm = 16d       Q5_1: ds = d, dm = -m
-//   Q8_0: ds = d, dm = 0 (signed codes)
+// map (value_at, src/quant.rs:349-456).  Written as w = ds * (q - z) - dm:
+//   Q4_0: ds = d, z = 8         Q4_1: ds = d, dm = -m
+//   Q5_0: ds = d, z = 16        Q5_1: ds = d, dm = -m
+//   Q8_0: ds = d (signed codes)
 //   Q4_K/Q5_K: ds = d*sc, dm = dmin*m per 32 columns
-//   Q6_K: ds = d*sc, dm = 32*d*sc per 16 columns
-// so that per group  sum_k w_k x_k = ds * sum_k q_k x_k - dm * sum_k x_k.
-// The integer part runs on the tensor cores: x of every item is split per
-// 32-column group into s * (xh + xl/256) with int8 xh, xl (about 15
-// significant bits), and
-//     sum_k q_k x_k = s/256 * (256 * (q.xh) + q.xl)
-// is formed exactly in int32 by two MMAs (the second one accumulates onto the
-// first one's result shifted left by 8).  The A operand is the weight codes,
-// decoded straight from the GGML block bytes into the m16n8k32 fragment
-// layout; B is the split x.  Scales and the offset term are applied in fp32
-// per (row, group); sum_k x_k is the exact f32 sum.  The result matches the
-// reference's f32 dot to about 1e-5 relative.
+//   Q6_K: ds = d*sc per 16 columns, z = 32
+// so per group  sum_k w_k x_k = ds * sum_k (q_k - z) x_k - dm * sum_k x_k.
+// The codes minus their zero point are small integers, exact in f16; they are
+// decoded from the GGML block bytes straight into the A fragments (a code
+// byte or nibble OR 0x6400 is the f16 value 1024 + code, minus 1024 + z).
+// x is scaled by a power of two per item s (exact; max |x/s| in [2^13, 2^14),
+// so the f16 range is never exceeded) and split into xh = f16(x/s) and
+// xl = f16(x/s - xh), together about 22 significant bits.  Per group and 8
+// items the tensor cores form sum (q - z) xh + sum (q - z) xl in f32 (every
+// product exact), and one FMA per element applies ds (plus one for the dm
+// term).  The result matches the reference's f32 dot to about 1e-6 relative.
 //
-// Layout of the split x ("fragment order"): for every 32-column group g and
-// tile j of 8 items, 32 records of 16 bytes, one per lane of the consuming
-// warp: lane (gid, t) gets {xh[4t..4t+3], xh[16+4t..+3], xl[4t..+3],
-// xl[16+4t..+3]} of item 8j + gid -- the B fragments of both MMAs in one
-// 16-byte shared-memory load.  Per (g, j, t) a 32-byte record holds, for
-// items 8j+2t and 8j+2t+1 (the C fragment's columns), {s/256, s/256,
-// X32, X32, Xa, Xa, Xb, Xb} with X32 = sum of x over the group and Xa, Xb
-// over its two 16-column halves (Q6_K).
+// Column order inside a 32-column group: k-step 0 takes columns 0..15, with
+// fragment slots (2t, 2t+1) holding columns (4t, 4t+2) and slots (2t+8, 2t+9)
+// holding (4t+1, 4t+3); k-step 1 the same for columns 16..31.  That is the
+// order in which lane t finds the codes in the 4-byte word it loads, so each
+// A register is one mask and one f16 subtraction.  The split x is stored in
+// the same order ("fragment order"): per group g and tile j of 8 items, 32
+// lane records of 16 bytes for xh then 32 for xl, lane (gid, t) holding
+// {x[4t], x[4t+2]}, {x[4t+1], x[4t+3]}, {x[16+4t], x[16+4t+2]},
+// {x[16+4t+1], x[16+4t+3]} of item 8j + gid; then per (g, j, t) a float2
+// with sum_k x_k / s of items 8j + 2t and 8j + 2t + 1 (the C fragment's
+// columns) for the dm term.
 //
 // Work split: a CTA of 16 warps (8 for a gate/up pair) owns 16 rows per warp
-// of one matrix and a run of K chunks of 512 columns.  The split x of the
-// chunk (16 groups x the item tiles) is copied to shared memory with cp.async,
-// double-buffered so the next chunk lands while this one is multiplied; each
-// warp streams its rows' blocks from HBM exactly once, the next group's codes
-// loaded one group ahead.  When the row CTAs alone fill the GPU the epilogue
-// (bias, residual add, SwiGLU, greedy argmax) runs in the kernel; otherwise K
-// is split across CTAs, the partial sums go to scratch and
-// gemm_epilogue_kernel adds them in a fixed order, so results never depend on
-// scheduling.
+// of one matrix and a run of K chunks of 256 columns.  The split x of the
+// chunk is copied to shared memory with cp.async, double-buffered so the next
+// chunk lands while this one is multiplied; each warp streams its rows'
+// blocks from HBM exactly once, the next group's codes loaded one group
+// ahead.  When the row CTAs alone fill the GPU the epilogue (bias, residual
+// add, SwiGLU, greedy argmax) runs in the kernel; otherwise K is split across
+// CTAs, the partial sums go to scratch and gemm_epilogue_kernel adds them in a
+// fixed order, so results never depend on scheduling.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -56,12 +58,13 @@
 namespace lrs {
 namespace {
 
-constexpr int kGroupsPerChunk = 16;  // 512 columns
+constexpr int kGroupsPerChunk = 8;  // 256 columns
 constexpr int kChunkCols = 32 * kGroupsPerChunk;
-constexpr int kMaxTiles = 8;          // 64 items per launch (larger batches loop)
+constexpr int kMaxTiles = 8;        // 64 items per launch (larger batches loop)
 constexpr int kMaxItems = 8 * kMaxTiles;
-constexpr int kXRec = 512;            // bytes of x records per (group, tile)
-constexpr int kSRec = 128;            // bytes of scale records per (group, tile)
+constexpr int kXRec = 1024;         // bytes of x records per (group, tile): 32 x 16 (xh) + 32 x 16 (xl)
+constexpr int kSRec = 32;           // bytes of sum records per (group, tile): 4 x float2
+constexpr int kAhead = 2;           // K chunks of weight rows prefetched into L2 ahead
 
 template <bool PAIR>
 struct Shape {
@@ -88,17 +91,20 @@ __device__ __forceinline__ uint16_t ldg16(const uint8_t* p) {
   return v;
 }
 // Four bytes at a 2-byte aligned address (blocks of 18, 22, 34, 210 bytes).
+// Branch-free: two aligned words and a funnel shift.
 __device__ __forceinline__ uint32_t ldg32_a2(const uint8_t* p) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  if ((a & 3) == 0) return ldg32(p);
   const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
-  return __funnelshift_r(ldg32(b), ldg32(b + 4), 16);
-}
-// Bit j (j = 0..3) of `nib` to bit 0 of byte j.
-__device__ __forceinline__ uint32_t spread4(uint32_t nib) {
-  return ((nib & 15u) * 0x00204081u) & 0x01010101u;
+  return __funnelshift_r(ldg32(b), ldg32(b + 4), (uint32_t)(a & 3) * 8);
 }
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xffu; }
+
+// f16 pair (1024 + a, 1024 + b) - (1024 + z, 1024 + z) = (a - z, b - z), exact.
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+constexpr uint32_t kF16Base = 0x64006400u;  // f16 pair (1024, 1024)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
@@ -112,75 +118,80 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void mma_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                        uint32_t b1, const int (&c)[4]) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%11,%12,%13};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c[0]), "r"(c[1]),
-        "r"(c[2]), "r"(c[3]));
-}
-__device__ __forceinline__ void mma_k16(int (&d)[4], const uint32_t (&a)[2], uint32_t b0,
-                                        const int (&c)[4]) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
-      "{%7,%8,%9,%10};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(b0), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // ---- x preparation ---------------------------------------------------------
-// One warp per (item, 32-column group); items >= batch (tile padding) get
-// zero records.  xq: [groups][tiles][32] x 16 B; xs: [groups][tiles][4] x 32 B.
+// One CTA per item (items >= batch, the tile padding, get zero records).
+// xq: [groups][tiles][1024 B]; xs: [groups][tiles][4] float2; xscale: [tiles * 8].
 __global__ void __launch_bounds__(256)
     xsplit_kernel(const float* x, int x_ld, int cols, int batch, int tiles, uint8_t* xq,
-                  float* xs) {
-  const int b = blockIdx.y;
-  const int g = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (g * 32 >= cols) return;
-  const float v = b < batch ? x[(size_t)b * x_ld + g * 32 + lane] : 0.0f;
-  float mx = fabsf(v);
+                  float* xs, float* xscale) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* xr = x + (size_t)b * x_ld;
+  __shared__ float red[8];
+  float mx = 0.0f;
+  if (b < batch)
+    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xr[c]));
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float s16 = v;
-  for (int o = 8; o >= 1; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-  const float other = __shfl_xor_sync(0xffffffffu, s16, 16);
-  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
-  const float q = v / sc;
-  const float hf = fminf(fmaxf(rintf(q), -127.0f), 127.0f);
-  const float lf = fminf(fmaxf(rintf((q - hf) * 256.0f), -127.0f), 127.0f);
-  uint32_t h = (uint32_t)(int)hf & 0xffu, l = (uint32_t)(int)lf & 0xffu;
-  // gather 4 consecutive columns into one word (lanes 4k)
-  h |= __shfl_down_sync(0xffffffffu, h, 1) << 8;
-  l |= __shfl_down_sync(0xffffffffu, l, 1) << 8;
-  h |= __shfl_down_sync(0xffffffffu, h, 2) << 16;
-  l |= __shfl_down_sync(0xffffffffu, l, 2) << 16;
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
+  // s = 2^(e - 14) with mx = f * 2^e, f in [0.5, 1): max |x / s| in [2^13, 2^14)
+  int e = 14;
+  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);
+  const float inv = ldexpf(1.0f, 14 - e);
+  if (threadIdx.x == 0) xscale[b] = ldexpf(1.0f, e - 14);
   const int j = b >> 3, gid = b & 7;
-  if ((lane & 3) == 0) {
-    const int t = (lane & 15) >> 2, half = lane >> 4;
-    uint32_t* rec = reinterpret_cast<uint32_t*>(xq + ((size_t)g * tiles + j) * kXRec +
-                                                (gid * 4 + t) * 16);
-    rec[half] = h;
-    rec[2 + half] = l;
-  }
-  float* srec = xs + (((size_t)g * tiles + j) * 4 + (gid >> 1)) * 8 + (gid & 1);
-  if (lane == 0) {
-    srec[0] = sc * (1.0f / 256.0f);
-    srec[2] = s16 + other;
-    srec[4] = s16;
-  } else if (lane == 16) {
-    srec[6] = s16;
+  for (int g = warp; g * 32 < cols; g += 8) {
+    const float v = b < batch ? xr[g * 32 + lane] * inv : 0.0f;
+    const __half h = __float2half_rn(v);
+    const __half l = __float2half_rn(v - __half2float(h));
+    float sum = v;
+    for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    uint32_t hp = __half_as_ushort(h), lp = __half_as_ushort(l);
+    hp |= __shfl_down_sync(0xffffffffu, hp, 2) << 16;  // pair (c, c + 2)
+    lp |= __shfl_down_sync(0xffffffffu, lp, 2) << 16;
+    if ((lane & 2) == 0) {
+      const int ks = lane >> 4, t = (lane & 15) >> 2, bsel = lane & 1;
+      uint8_t* rec = xq + ((size_t)g * tiles + j) * kXRec + (gid * 4 + t) * 16 + ks * 8 + bsel * 4;
+      *reinterpret_cast<uint32_t*>(rec) = hp;
+      *reinterpret_cast<uint32_t*>(rec + 512) = lp;
+    }
+    if (lane == 0) xs[((size_t)g * tiles + j) * 8 + gid] = sum;
   }
 }
 
 // ---- A fragments -------------------------------------------------------------
 // For one row (block bytes at rp), 32-column group gc and thread t of the
-// quad: the code words of columns 4t..4t+3 (w0) and 16+4t..16+4t+3 (w1) and
-// the affine maps of the two 16-column halves (equal except for Q6_K); ndm
-// holds -dm.
+// quad: h[0], h[1] = k-step 0 slot pairs (columns (4t, 4t+2), (4t+1, 4t+3)),
+// h[2], h[3] = k-step 1 (the same + 16), as f16 (q - z); ds0 / ds1 scale the
+// two k-steps (equal except for Q6_K) and ndm = -dm (0 where z holds the offset).
 template <int T>
 struct AFrag {
-  uint32_t w0, w1;
-  float ds0, ndm0, ds1, ndm1;
+  static constexpr bool kAffine = T == LRS_GGML_Q4_1 || T == LRS_GGML_Q5_1 ||
+                                  T == LRS_GGML_Q4_K || T == LRS_GGML_Q5_K;
+  uint32_t h[4];
+  float ds0, ds1, ndm;
+
+  __device__ __forceinline__ void nibbles(uint32_t wa, uint32_t wb) {
+    h[0] = wa & 0x000F000Fu;
+    h[1] = (wa >> 8) & 0x000F000Fu;
+    h[2] = wb & 0x000F000Fu;
+    h[3] = (wb >> 8) & 0x000F000Fu;
+  }
+  __device__ __forceinline__ void finish(uint32_t z) {
+    const uint32_t zz = kF16Base + z * 0x00010001u;
+#pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = h2sub(h[i] | kF16Base, zz);
+  }
 
   __device__ __forceinline__ void load(const uint8_t* rp, int gc, int t) {
     if constexpr (T == LRS_GGML_Q4_K || T == LRS_GGML_Q5_K) {
@@ -190,12 +201,16 @@ struct AFrag {
       constexpr int qs0 = T == LRS_GGML_Q4_K ? 16 : 48;
       const uint8_t* q = u + qs0 + 32 * (g >> 1) + 4 * t;
       const int sh = 4 * (g & 1);
-      w0 = (ldg32(q) >> sh) & 0x0F0F0F0Fu;
-      w1 = (ldg32(q + 16) >> sh) & 0x0F0F0F0Fu;
+      nibbles(ldg32(q) >> sh, ldg32(q + 16) >> sh);
       if constexpr (T == LRS_GGML_Q5_K) {
-        w0 |= ((ldg32(u + 16 + 4 * t) >> g) & 0x01010101u) << 4;
-        w1 |= ((ldg32(u + 32 + 4 * t) >> g) & 0x01010101u) << 4;
+        const uint32_t ha = (ldg32(u + 16 + 4 * t) >> g) & 0x01010101u;
+        const uint32_t hb = (ldg32(u + 32 + 4 * t) >> g) & 0x01010101u;
+        h[0] |= (ha & 0x00010001u) << 4;
+        h[1] |= (ha & 0x01000100u) >> 4;
+        h[2] |= (hb & 0x00010001u) << 4;
+        h[3] |= (hb & 0x01000100u) >> 4;
       }
+      finish(0);
       // header as one 16-byte load; scale_min_k4 (src/quant.rs:338-347) on words
       const uint4 hd = ldg128(u);
       uint32_t sc, mn;
@@ -208,7 +223,7 @@ struct AFrag {
         mn = (byte_of(hd.w, j) >> 4) | ((byte_of(hd.z, j) >> 6) << 4);
       }
       ds0 = ds1 = f16_bits((uint16_t)(hd.x & 0xffffu)) * (float)sc;
-      ndm0 = ndm1 = -f16_bits((uint16_t)(hd.x >> 16)) * (float)mn;
+      ndm = -f16_bits((uint16_t)(hd.x >> 16)) * (float)mn;
     } else if constexpr (T == LRS_GGML_Q6_K) {
       // ql[128], qh[64], scales[16] (i8), d; value_at, src/quant.rs:441-456
       const uint8_t* u = rp + (size_t)(gc >> 3) * 210;
@@ -217,40 +232,49 @@ struct AFrag {
       const uint8_t* ql = u + half * 64 + (quarter & 1) * 32 + 4 * t;
       const uint8_t* qh = u + 128 + half * 32 + 4 * t;
       const int nsh = (quarter >> 1) * 4, hsh = 2 * quarter;
-      w0 = ((ldg32_a2(ql) >> nsh) & 0x0F0F0F0Fu) | (((ldg32_a2(qh) >> hsh) & 0x03030303u) << 4);
-      w1 = ((ldg32_a2(ql + 16) >> nsh) & 0x0F0F0F0Fu) |
-           (((ldg32_a2(qh + 16) >> hsh) & 0x03030303u) << 4);
+      nibbles(ldg32_a2(ql) >> nsh, ldg32_a2(ql + 16) >> nsh);
+      const uint32_t ha = (ldg32_a2(qh) >> hsh) & 0x03030303u;
+      const uint32_t hb = (ldg32_a2(qh + 16) >> hsh) & 0x03030303u;
+      h[0] |= (ha & 0x00030003u) << 4;
+      h[1] |= (ha & 0x03000300u) >> 4;
+      h[2] |= (hb & 0x00030003u) << 4;
+      h[3] |= (hb & 0x03000300u) >> 4;
+      finish(32);
       const float d = f16_bits(ldg16(u + 208));
       const uint16_t sp = ldg16(u + 192 + half * 8 + quarter * 2);
       ds0 = d * (float)(int8_t)(sp & 0xffu);
       ds1 = d * (float)(int8_t)(sp >> 8);
-      ndm0 = -32.0f * ds0;
-      ndm1 = -32.0f * ds1;
+      ndm = 0.0f;
+    } else if constexpr (T == LRS_GGML_Q8_0) {
+      // d, qs[32] (i8); value_at, src/quant.rs:395-400
+      const uint8_t* u = rp + (size_t)gc * 34;
+      const uint32_t wa = ldg32_a2(u + 2 + 4 * t) ^ 0x80808080u;  // i8 -> u8 = q + 128
+      const uint32_t wb = ldg32_a2(u + 18 + 4 * t) ^ 0x80808080u;
+      h[0] = __byte_perm(wa, 0x64646464u, 0x4240);
+      h[1] = __byte_perm(wa, 0x64646464u, 0x4341);
+      h[2] = __byte_perm(wb, 0x64646464u, 0x4240);
+      h[3] = __byte_perm(wb, 0x64646464u, 0x4341);
+      const uint32_t zz = kF16Base + 128u * 0x00010001u;
+#pragma unroll
+      for (int i = 0; i < 4; i++) h[i] = h2sub(h[i], zz);
+      ds0 = ds1 = f16_bits(ldg16(u));
+      ndm = 0.0f;
     } else {
-      // 32-value blocks: d, (m), (qh[4]), qs[16] or Q8_0 d, qs[32]
+      // 32-value blocks d, (m), (qh[4]), qs[16]; value_at, src/quant.rs:361-394
       const uint8_t* u = rp + (size_t)gc * BlockTraits<T>::kBytes;
-      const float d = f16_bits(ldg16(u));
-      ds0 = ds1 = d;
-      if constexpr (T == LRS_GGML_Q8_0) {
-        w0 = ldg32_a2(u + 2 + 4 * t);
-        w1 = ldg32_a2(u + 18 + 4 * t);
-        ndm0 = ndm1 = 0.0f;
-      } else {
-        constexpr int qs = T == LRS_GGML_Q4_0 ? 2 : T == LRS_GGML_Q4_1 ? 4 : T == LRS_GGML_Q5_0 ? 6 : 8;
-        const uint32_t q = ldg32_a2(u + qs + 4 * t);
-        w0 = q & 0x0F0F0F0Fu;
-        w1 = (q >> 4) & 0x0F0F0F0Fu;
-        if constexpr (T == LRS_GGML_Q5_0 || T == LRS_GGML_Q5_1) {
-          const uint32_t qh = ldg32_a2(u + (T == LRS_GGML_Q5_0 ? 2 : 4));
-          w0 |= spread4(qh >> (4 * t)) << 4;
-          w1 |= spread4(qh >> (16 + 4 * t)) << 4;
-        }
-        if constexpr (T == LRS_GGML_Q4_1 || T == LRS_GGML_Q5_1) {
-          ndm0 = ndm1 = f16_bits(ldg16(u + 2));
-        } else {
-          ndm0 = ndm1 = (T == LRS_GGML_Q4_0 ? -8.0f : -16.0f) * d;
-        }
+      constexpr int qs = T == LRS_GGML_Q4_0 ? 2 : T == LRS_GGML_Q4_1 ? 4 : T == LRS_GGML_Q5_0 ? 6 : 8;
+      const uint32_t w = ldg32_a2(u + qs + 4 * t);
+      nibbles(w, w >> 4);  // low nibbles: columns 4t..4t+3; high: 16+4t..16+4t+3
+      if constexpr (T == LRS_GGML_Q5_0 || T == LRS_GGML_Q5_1) {
+        const uint32_t v = ldg32_a2(u + (T == LRS_GGML_Q5_0 ? 2 : 4)) >> (4 * t);
+        h[0] |= ((v & 1u) << 4) | ((v & 4u) << 18);
+        h[1] |= ((v & 2u) << 3) | ((v & 8u) << 17);
+        h[2] |= ((v >> 12) & 0x10u) | ((v & 0x40000u) << 2);
+        h[3] |= ((v >> 13) & 0x10u) | ((v & 0x80000u) << 1);
       }
+      finish(T == LRS_GGML_Q4_0 ? 8 : T == LRS_GGML_Q5_0 ? 16 : 0);
+      ds0 = ds1 = f16_bits(ldg16(u));
+      ndm = kAffine ? f16_bits(ldg16(u + 2)) : 0.0f;
     }
   }
 };
@@ -259,56 +283,68 @@ struct GemmArgs {
   GemvSeg seg[kGemvMaxSeg];
   int cta0[kGemvMaxSeg + 1];  // first row-CTA of each segment
   int nseg, cols, batch, epi, kgroups, tiles;  // tiles: item tiles of the x layout
-  const uint8_t* xq;  // records of tile 0 of this launch's items
+  const uint8_t* xq;     // records of tile 0 of this launch's items
   const float* xs;
+  const float* xscale;   // [batch] power-of-two item scales
   float* part[kGemvMaxSeg];  // [pair][kgroups][batch][rows], kgroups > 1
   unsigned long long* keys;  // [batch], EPI_ARGMAX
 };
 
-// Adds one 32-column group of 16 rows x 8*NT items into acc.
+// Adds one 32-column group of 16 rows x 8*NT items into acc.  Tiles go in
+// pairs so that consecutive MMAs are independent.
 template <int T, int NT>
 __device__ __forceinline__ void group_mma(float (&acc)[NT][4], const AFrag<T>& fa,
                                           const AFrag<T>& fb, const uint4* xr,
-                                          const float4* sr) {
+                                          const float2* sr) {
+  constexpr int JB = NT < 2 ? NT : 2;
 #pragma unroll
-  for (int j = 0; j < NT; j++) {
-    const uint4 xv = xr[j * 32];
-    const float4 sv = sr[j * 8];  // {s0, s1, X0, X1}
-    const int z[4] = {0, 0, 0, 0};
-    if constexpr (T != LRS_GGML_Q6_K) {
-      const uint32_t A[4] = {fa.w0, fb.w0, fa.w1, fb.w1};
-      int d[4], e[4];
-      mma_k32(d, A, xv.x, xv.y, z);
-      const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-      mma_k32(e, A, xv.z, xv.w, c);
-      // e[0], e[1]: row gid, items 2t, 2t+1; e[2], e[3]: row gid+8
-      acc[j][0] = fmaf(fa.ds0, sv.x * (float)e[0], fmaf(fa.ndm0, sv.z, acc[j][0]));
-      acc[j][1] = fmaf(fa.ds0, sv.y * (float)e[1], fmaf(fa.ndm0, sv.w, acc[j][1]));
-      acc[j][2] = fmaf(fb.ds0, sv.x * (float)e[2], fmaf(fb.ndm0, sv.z, acc[j][2]));
-      acc[j][3] = fmaf(fb.ds0, sv.y * (float)e[3], fmaf(fb.ndm0, sv.w, acc[j][3]));
-    } else {
-      const float4 hv = sr[j * 8 + 1];  // {Xa0, Xa1, Xb0, Xb1}
-      {
-        const uint32_t A[2] = {fa.w0, fb.w0};
-        int d[4], e[4];
-        mma_k16(d, A, xv.x, z);
-        const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-        mma_k16(e, A, xv.z, c);
-        acc[j][0] = fmaf(fa.ds0, sv.x * (float)e[0], fmaf(fa.ndm0, hv.x, acc[j][0]));
-        acc[j][1] = fmaf(fa.ds0, sv.y * (float)e[1], fmaf(fa.ndm0, hv.y, acc[j][1]));
-        acc[j][2] = fmaf(fb.ds0, sv.x * (float)e[2], fmaf(fb.ndm0, hv.x, acc[j][2]));
-        acc[j][3] = fmaf(fb.ds0, sv.y * (float)e[3], fmaf(fb.ndm0, hv.y, acc[j][3]));
+  for (int j0 = 0; j0 < NT; j0 += JB) {
+    float c[JB][4];
+    uint4 xh[JB], xl[JB];
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++) {
+      xh[jj] = xr[(j0 + jj) * 64];
+      xl[jj] = xr[(j0 + jj) * 64 + 32];
+      c[jj][0] = c[jj][1] = c[jj][2] = c[jj][3] = 0.0f;
+    }
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++)
+      mma_f16(c[jj], fa.h[0], fb.h[0], fa.h[1], fb.h[1], xh[jj].x, xh[jj].y);
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++)
+      mma_f16(c[jj], fa.h[0], fb.h[0], fa.h[1], fb.h[1], xl[jj].x, xl[jj].y);
+    if constexpr (T == LRS_GGML_Q6_K) {
+#pragma unroll
+      for (int jj = 0; jj < JB; jj++) {
+        float* A = acc[j0 + jj];
+        A[0] = fmaf(fa.ds0, c[jj][0], A[0]);
+        A[1] = fmaf(fa.ds0, c[jj][1], A[1]);
+        A[2] = fmaf(fb.ds0, c[jj][2], A[2]);
+        A[3] = fmaf(fb.ds0, c[jj][3], A[3]);
+        c[jj][0] = c[jj][1] = c[jj][2] = c[jj][3] = 0.0f;
       }
-      {
-        const uint32_t A[2] = {fa.w1, fb.w1};
-        int d[4], e[4];
-        mma_k16(d, A, xv.y, z);
-        const int c[4] = {d[0] << 8, d[1] << 8, d[2] << 8, d[3] << 8};
-        mma_k16(e, A, xv.w, c);
-        acc[j][0] = fmaf(fa.ds1, sv.x * (float)e[0], fmaf(fa.ndm1, hv.z, acc[j][0]));
-        acc[j][1] = fmaf(fa.ds1, sv.y * (float)e[1], fmaf(fa.ndm1, hv.w, acc[j][1]));
-        acc[j][2] = fmaf(fb.ds1, sv.x * (float)e[2], fmaf(fb.ndm1, hv.z, acc[j][2]));
-        acc[j][3] = fmaf(fb.ds1, sv.y * (float)e[3], fmaf(fb.ndm1, hv.w, acc[j][3]));
+    }
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++)
+      mma_f16(c[jj], fa.h[2], fb.h[2], fa.h[3], fb.h[3], xh[jj].z, xh[jj].w);
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++)
+      mma_f16(c[jj], fa.h[2], fb.h[2], fa.h[3], fb.h[3], xl[jj].z, xl[jj].w);
+    // c[0], c[1]: row gid, items 2t, 2t+1; c[2], c[3]: row gid+8
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++) {
+      float* A = acc[j0 + jj];
+      if constexpr (AFrag<T>::kAffine) {
+        const float2 X = sr[(j0 + jj) * 4];
+        A[0] = fmaf(fa.ds1, c[jj][0], fmaf(fa.ndm, X.x, A[0]));
+        A[1] = fmaf(fa.ds1, c[jj][1], fmaf(fa.ndm, X.y, A[1]));
+        A[2] = fmaf(fb.ds1, c[jj][2], fmaf(fb.ndm, X.x, A[2]));
+        A[3] = fmaf(fb.ds1, c[jj][3], fmaf(fb.ndm, X.y, A[3]));
+      } else {
+        A[0] = fmaf(fa.ds1, c[jj][0], A[0]);
+        A[1] = fmaf(fa.ds1, c[jj][1], A[1]);
+        A[2] = fmaf(fb.ds1, c[jj][2], A[2]);
+        A[3] = fmaf(fb.ds1, c[jj][3], A[3]);
       }
     }
   }
@@ -337,7 +373,7 @@ __device__ __forceinline__ void stage_chunk(const GemmArgs& a, int kc, uint8_t* 
 
 template <int T, bool PAIR, int NT>
 __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
-    gemm_i8_kernel(const __grid_constant__ GemmArgs a) {
+    gemm_mma_kernel(const __grid_constant__ GemmArgs a) {
   using S = Shape<PAIR>;
   constexpr int kBuf = kGroupsPerChunk * NT * (kXRec + kSRec);
   extern __shared__ __align__(16) uint8_t smem[];
@@ -377,6 +413,24 @@ __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
   stage_chunk<NT, S::kThreads>(a, k0, smem);
   cp_async_commit();
 
+  // L2 prefetch of this warp's rows, chunks k0 .. k0 + kAhead - 1 now and
+  // chunk kc + kAhead when chunk kc starts: the code loads then hit L2.
+  // bytes of one row per 256-column chunk (the last chunk may be shorter)
+  constexpr int rbc = BlockTraits<T>::kBytes * (kChunkCols / BlockTraits<T>::kValues);
+  auto prefetch_rows = [&](int kc) {
+    if (!active || kc >= k1) return;
+    const int nbytes = kc + 1 < kch ? rbc : rb - kc * rbc;
+    const int lines = (nbytes + 127) / 128 + 1;
+    for (int i = lane; i < 16 * lines * (PAIR ? 2 : 1); i += 32) {
+      const int r = i % 16, l = (i / 16) % lines, m = i / (16 * lines);
+      const int row = min(rbase + r, rows - 1);
+      const uint8_t* base = (m ? W2 : W) + (size_t)row * rb + (size_t)kc * rbc;
+      const uint8_t* line = base + min(l * 128, nbytes - 1);
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+    }
+  };
+  for (int k = 0; k < kAhead; k++) prefetch_rows(k0 + k);
+
   AFrag<T> fa, fb, ua, ub;
   int gc = k0 * kGroupsPerChunk;
   if (active) {
@@ -397,11 +451,14 @@ __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
       cp_async_wait<0>();
     }
     __syncthreads();
+    prefetch_rows(kc + kAhead);
     const int ng = min(kGroupsPerChunk, a.cols / 32 - kc * kGroupsPerChunk);
     if (active) {
       const uint4* xr = reinterpret_cast<const uint4*>(buf) + lane;
-      const float4* sr = reinterpret_cast<const float4*>(buf + kGroupsPerChunk * NT * kXRec) + t * 2;
-      for (int g = 0; g < ng; g++, gc++) {
+      const float2* sr = reinterpret_cast<const float2*>(buf + kGroupsPerChunk * NT * kXRec) + t;
+#pragma unroll
+      for (int g = 0; g < kGroupsPerChunk; g++, gc++) {
+        if (g >= ng) break;
         AFrag<T> na, nb, nua, nub;
         const int gn = gc + 1 < gend ? gc + 1 : gc;  // next group's codes, one group ahead
         na.load(rpa, gn, t);
@@ -410,8 +467,8 @@ __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
           nua.load(upa, gn, t);
           nub.load(upb, gn, t);
         }
-        group_mma<T, NT>(acc, fa, fb, xr + g * NT * 32, sr + g * NT * 8);
-        if constexpr (PAIR) group_mma<T, NT>(acc2, ua, ub, xr + g * NT * 32, sr + g * NT * 8);
+        group_mma<T, NT>(acc, fa, fb, xr + g * NT * 64, sr + g * NT * 4);
+        if constexpr (PAIR) group_mma<T, NT>(acc2, ua, ub, xr + g * NT * 64, sr + g * NT * 4);
         fa = na;
         fb = nb;
         if constexpr (PAIR) {
@@ -421,6 +478,17 @@ __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
       }
     }
     __syncthreads();  // buffer kc is refilled by iteration kc + 1's stage of kc + 2
+  }
+
+  // undo the item scales (powers of two: exact)
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const float2 sc = *reinterpret_cast<const float2*>(a.xscale + 8 * j + 2 * t);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      acc[j][c] *= (c & 1) ? sc.y : sc.x;
+      if constexpr (PAIR) acc2[PAIR ? j : 0][c] *= (c & 1) ? sc.y : sc.x;
+    }
   }
 
   // ---- output ----
@@ -541,13 +609,13 @@ template <int T, bool PAIR, int NT>
 cudaError_t launch_t(const GemmArgs& a, dim3 grid, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<T, PAIR, NT>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_mma_kernel<T, PAIR, NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem_for<NT>());
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gemm_i8_kernel<T, PAIR, NT><<<grid, Shape<PAIR>::kThreads, smem_for<NT>(), st>>>(a);
+  gemm_mma_kernel<T, PAIR, NT><<<grid, Shape<PAIR>::kThreads, smem_for<NT>(), st>>>(a);
   return cudaGetLastError();
 }
 
@@ -608,7 +676,7 @@ bool gemm_supported(const GemvParams& p) {
 
 size_t gemm_scratch_bytes(int batch, int max_cols, int sms) {
   const size_t tiles = layout_tiles(std::max(batch, 1));
-  const size_t xq = (size_t)(max_cols / 32) * tiles * (kXRec + kSRec) + 1024;
+  const size_t xq = (size_t)(max_cols / 32) * tiles * (kXRec + kSRec) + tiles * 32 + 1024;
   // kgroups > 1 only when the row CTAs do not fill the SMs; then kgroups *
   // rows <= 2 * sms * 256 for a launch (a pair has half the rows of a CTA).
   const size_t parts = (size_t)(2 * sms) * 256 * std::min(batch, kMaxItems) * 4 + 1024;
@@ -625,10 +693,10 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
   };
   uint8_t* xq = align(scratch);
   float* xs = reinterpret_cast<float*>(xq + (size_t)(cols / 32) * tiles * kXRec);
-  float* part = reinterpret_cast<float*>(
+  float* xscale = reinterpret_cast<float*>(
       align(reinterpret_cast<uint8_t*>(xs) + (size_t)(cols / 32) * tiles * kSRec));
-  xsplit_kernel<<<dim3((cols / 32 + 7) / 8, tiles * 8), 256, 0, st>>>(p.x, p.x_ld, cols, Ball,
-                                                                       tiles, xq, xs);
+  float* part = reinterpret_cast<float*>(align(xscale + tiles * 8));
+  xsplit_kernel<<<tiles * 8, 256, 0, st>>>(p.x, p.x_ld, cols, Ball, tiles, xq, xs, xscale);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows_cta = pair ? Shape<true>::kRows : Shape<false>::kRows;
@@ -648,6 +716,7 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
       a.tiles = tiles;
       a.xq = xq + (size_t)(b0 / 8) * kXRec;
       a.xs = xs + (size_t)(b0 / 8) * (kSRec / 4);
+      a.xscale = xscale + b0;
       a.keys = p.argmax_keys ? p.argmax_keys + b0 : nullptr;
       int ctas = 0;
       for (int k = 0; k < a.nseg; k++) {
