@@ -389,9 +389,12 @@ int32_t upload_mat(const lrs_tensor_desc& d, size_t rows, size_t cols, const cha
   return upload(d.data, d.nbytes, rows, cols, d.ggml_type, out);
 }
 
+// Splits of each sequence's context: as many as fit in one wave of resident
+// attention CTAs (batch * kv heads * splits CTAs), so no tail wave.
 int nsplit_for(const lrs_model* m, int batch) {
-  int want = (4 * m->be->sms + batch * (int)m->c.num_key_value_heads - 1) /
-             (batch * (int)m->c.num_key_value_heads);
+  const int slots = m->be->sms * attention_ctas_per_sm((int)m->c.head_dim,
+                                                       m->opt.kv_dtype == LRS_KV_BF16);
+  int want = slots / (batch * (int)m->c.num_key_value_heads);
   int maxs = std::max(1, (int)((m->opt.max_seq_len + 31) / 32));
   return std::max(1, std::min({want, m->max_split, maxs}));
 }

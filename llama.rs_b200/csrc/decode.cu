@@ -380,6 +380,17 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
   return cudaGetLastError();
 }
 
+int attention_ctas_per_sm(int hd, int kv_bf16) {
+  int n = 1;
+  const void* k = hd == 128 ? (kv_bf16 ? (const void*)attn_split_kernel<128, true>
+                                       : (const void*)attn_split_kernel<128, false>)
+                            : (kv_bf16 ? (const void*)attn_split_kernel<64, true>
+                                       : (const void*)attn_split_kernel<64, false>);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kAttnWarps * 32, 0) != cudaSuccess)
+    return 1;
+  return n < 1 ? 1 : n;
+}
+
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
                              const void* kpool, const void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, cudaStream_t st) {

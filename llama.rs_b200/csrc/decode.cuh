@@ -35,6 +35,8 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
                               void* kpool, void* vpool, int kv_bf16, cudaStream_t st);
 // Split-K GQA decode attention over the paged cache (src/model.rs:206-231 with
 // softmax_inplace :298-313), then the cross-split combine into att[b][nh*hd].
+// Resident attention CTAs per SM (occupancy of the split kernel).
+int attention_ctas_per_sm(int hd, int kv_bf16);
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
                              const void* kpool, const void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, cudaStream_t st);
