@@ -191,6 +191,23 @@ typedef struct lrs_model lrs_model;
  * activation buffers (InferenceBuffers::new, src/cache.rs:79-101). */
 lrs_status lrs_model_create(lrs_backend* backend, const lrs_model_desc* desc,
                             const lrs_model_options* options, lrs_model** out);
+/* ---- tensor parallelism (c4) ---------------------------------------------
+ * No counterpart in the reference (one CPU process): the model is split over
+ * `world` processes, one GPU each.  q/k/v/gate/up and the LM head are split by
+ * rows (heads, MLP width, vocabulary), o and down by columns; after o and
+ * after down one NCCL sum all-reduce rebuilds the residual on every rank, and
+ * the greedy argmax is a MAX all-reduce of the packed (value, index) keys.
+ * Every rank passes the FULL model description and makes the same calls in
+ * the same order.  world must divide the KV heads, the MLP width and the
+ * vocabulary, and the column splits must fall on block boundaries. */
+#define LRS_TP_ID_BYTES 128
+/* Rank 0 makes the id and shares it with the other ranks out of band. */
+lrs_status lrs_tp_unique_id(uint8_t* id_out /* LRS_TP_ID_BYTES */);
+lrs_status lrs_model_create_tp(lrs_backend* backend, const lrs_model_desc* desc,
+                               const lrs_model_options* options, uint32_t rank, uint32_t world,
+                               const uint8_t* id /* LRS_TP_ID_BYTES */, lrs_model** out);
+uint32_t lrs_model_tp_world(const lrs_model* model);
+
 void lrs_model_destroy(lrs_model* model);
 
 /* Forgets the contents of a sequence slot (KVCache::reset, src/cache.rs:55-57). */

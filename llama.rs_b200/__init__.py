@@ -168,6 +168,10 @@ _sig("lrs_matvec", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_batched", C.c_int32, _P, _P, _F, C.c_size_t, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_noalloc", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_device", C.c_int32, _P, _P, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+_sig("lrs_tp_unique_id", C.c_int32, C.c_char_p)
+_sig("lrs_model_create_tp", C.c_int32, _P, C.POINTER(_ModelDesc), C.POINTER(_ModelOptions),
+     C.c_uint32, C.c_uint32, C.c_char_p, C.POINTER(_P))
+_sig("lrs_model_tp_world", C.c_uint32, _P)
 _sig("lrs_model_create", C.c_int32, _P, C.POINTER(_ModelDesc), C.POINTER(_ModelOptions),
      C.POINTER(_P))
 _sig("lrs_model_destroy", None, _P)
@@ -199,7 +203,8 @@ EXPORTED_SYMBOLS = (
     "lrs_model_create",
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
-    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
+    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels",
+    "lrs_tp_unique_id", "lrs_model_create_tp", "lrs_model_tp_world", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
 )
 
@@ -601,11 +606,20 @@ class CudaQwen2Model:
 
     def __init__(self, backend: CudaBackend, desc, max_seq_len: int = 4096,
                  max_sequences: int = 1, kv_bf16: bool = False, use_graph: bool = True,
-                 keepalive=None):
+                 keepalive=None, tp_rank: int = 0, tp_world: int = 1, tp_id: bytes = b""):
+        """tp_world > 1 makes this process shard tp_rank of a tensor-parallel
+        model (every rank passes the full desc and the same tp_id, made once by
+        tp_unique_id() and shared out of band)."""
         opts = _ModelOptions(max_seq_len, max_sequences, 1 if kv_bf16 else 0,
                              1 if use_graph else 0)
         h = _P()
-        _check(_lib.lrs_model_create(backend.handle, desc, C.byref(opts), C.byref(h)))
+        if tp_world > 1:
+            if len(tp_id) != 128:
+                raise LrsError(1, "tp_id must be the 128 bytes of tp_unique_id()")
+            _check(_lib.lrs_model_create_tp(backend.handle, desc, C.byref(opts), tp_rank,
+                                            tp_world, tp_id, C.byref(h)))
+        else:
+            _check(_lib.lrs_model_create(backend.handle, desc, C.byref(opts), C.byref(h)))
         self._h = h
         self.backend = backend
         self.keepalive = keepalive
@@ -707,6 +721,13 @@ class CudaQwen2Model:
 
 
 # ------------------------------------------------------ benchmark configs --
+def tp_unique_id() -> bytes:
+    """The 128-byte NCCL id for lrs_model_create_tp (rank 0 makes it)."""
+    buf = C.create_string_buffer(128)
+    _check(_lib.lrs_tp_unique_id(buf))
+    return buf.raw
+
+
 def config_c0() -> LlamaConfig:
     """Qwen2.5-0.5B shape."""
     return LlamaConfig(896, 4864, 14, 2, 24, 151936, 1e-6, 1e6, 32768, 64, True)

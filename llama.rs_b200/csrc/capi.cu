@@ -6,6 +6,8 @@
 // weights, the paged KV cache and the activation buffers, and replays the
 // per-token decode step as one CUDA graph.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -40,6 +42,53 @@ using namespace lrs;
   } while (0)
 
 namespace {
+
+// NCCL, resolved at run time from the process (or libnccl.so.2) the first time
+// a tensor-parallel model is made, so the library loads without NCCL.
+struct NcclApi {
+  bool ok = false;
+  std::string err;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      a.err = std::string("NCCL not found: ") + dlerror();
+      return a;
+    }
+#define LRS_NCCL_SYM(f) a.f = reinterpret_cast<decltype(a.f)>(dlsym(h, "nccl" #f))
+    LRS_NCCL_SYM(GetUniqueId);
+    LRS_NCCL_SYM(CommInitRank);
+    LRS_NCCL_SYM(AllReduce);
+    LRS_NCCL_SYM(AllGather);
+    LRS_NCCL_SYM(CommDestroy);
+    LRS_NCCL_SYM(GetErrorString);
+#undef LRS_NCCL_SYM
+    a.ok = a.GetUniqueId && a.CommInitRank && a.AllReduce && a.AllGather && a.CommDestroy &&
+           a.GetErrorString;
+    if (!a.ok) a.err = "NCCL is missing required symbols";
+    return a;
+  }();
+  return api;
+}
+
+#define LRS_NCCL(call)                                                                      \
+  do {                                                                                      \
+    ncclResult_t r_ = (call);                                                               \
+    if (r_ != ncclSuccess)                                                                  \
+      return fail(LRS_ERR_CUDA, std::string("NCCL: ") + nccl().GetErrorString(r_));        \
+  } while (0)
 
 int32_t check_device_error(lrs_backend* be) {
   int h = 0;
@@ -327,6 +376,12 @@ struct lrs_model {
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
   void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
+  // tensor parallelism: this process holds shard tp_rank of tp_world
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
+  uint32_t vocab_full = 0;  // the model's vocabulary (c.vocab_size is this shard's head rows)
+  int vocab0 = 0;           // first LM-head row of this shard
+  float* logits_full = nullptr;
   size_t gemm_scratch_bytes = 0;
   unsigned long long* keys = nullptr;
   int *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_step = nullptr;
@@ -423,8 +478,19 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   const lrs_config& c = m->c;
   cudaStream_t st = m->be->stream;
   const int h = c.hidden_size, I = c.intermediate_size, nh = c.num_attention_heads,
-            nkv = c.num_key_value_heads, hd = c.head_dim, kvw = nkv * hd;
+            nkv = c.num_key_value_heads, hd = c.head_dim, kvw = nkv * hd, qw = nh * hd;
   const int sms = m->be->sms;
+  const bool tp = m->tp_world > 1;
+  // Row-split projections (o, down): every rank adds its partial sum of the
+  // residual update; rank 0 adds onto the residual, the others overwrite their
+  // copy with the partial, and one sum all-reduce rebuilds the residual.
+  const int res_epi = tp && m->tp_rank != 0 ? EPI_STORE : EPI_ADD;
+  auto allreduce_residual = [&]() -> int32_t {
+    if (tp)
+      LRS_NCCL(nccl().AllReduce(m->residual, m->residual, (size_t)B * h, ncclFloat32, ncclSum,
+                                m->comm, st));
+    return LRS_OK;
+  };
   StepIO io{m->d_tok, m->d_pos, m->d_seq, m->d_pages, m->pages_per_seq};
   const int kv_bf16 = m->opt.kv_dtype == LRS_KV_BF16;
   const int nsplit = nsplit_for(m, B);
@@ -434,7 +500,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     Layer& L = m->layers[li];
     GemvParams p;
     // input_layernorm + q/k/v projections with bias (src/model.rs:175-186)
-    GemvMat qkv[3] = {mat_of(L.q, m->q, h, L.qb), mat_of(L.k, m->k, kvw, L.kb),
+    GemvMat qkv[3] = {mat_of(L.q, m->q, qw, L.qb), mat_of(L.k, m->k, kvw, L.kb),
                       mat_of(L.v, m->v, kvw, L.vb)};
     if ((rc = gemv_plan(&p, qkv, 3, EPI_STORE, B))) return rc;
     p.error_flag = m->be->d_err;
@@ -464,11 +530,12 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
     GemvMat om = mat_of(L.o, m->residual, h);
-    if ((rc = gemv_plan(&p, &om, 1, EPI_ADD, B))) return rc;
+    if ((rc = gemv_plan(&p, &om, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->att;
-    p.x_ld = h;
+    p.x_ld = qw;
     LRS_CUDA(model_gemv(m, p, st, sms));
+    if ((rc = allreduce_residual())) return rc;
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
     GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
     if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B))) return rc;
@@ -485,11 +552,12 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     LRS_CUDA(model_gemv(m, p, st, sms));
     // down_proj + residual (src/model.rs:255-260)
     GemvMat dm = mat_of(L.down, m->residual, h);
-    if ((rc = gemv_plan(&p, &dm, 1, EPI_ADD, B))) return rc;
+    if ((rc = gemv_plan(&p, &dm, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->act;
     p.x_ld = I;
     LRS_CUDA(model_gemv(m, p, st, sms));
+    if ((rc = allreduce_residual())) return rc;
   }
   if (lm_item == -2) return LRS_OK;
   // final norm + lm_head (src/model.rs:263-268) fused with the greedy argmax
@@ -500,6 +568,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   if ((rc = gemv_plan(&p, &lmm, 1, EPI_ARGMAX, nb))) return rc;
   p.error_flag = m->be->d_err;
   p.argmax_keys = m->keys + (lm_item >= 0 ? lm_item : 0);
+  p.argmax_base = m->vocab0;
   if (nb == 1) {
     p.x = xin;
     p.norm_w = m->final_norm;
@@ -510,6 +579,14 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   }
   p.x_ld = h;
   LRS_CUDA(model_gemv(m, p, st, sms));
+  if (tp) {
+    // the shard argmaxes meet in one MAX all-reduce of the packed keys
+    LRS_NCCL(nccl().AllReduce(p.argmax_keys, p.argmax_keys, (size_t)nb, ncclUint64, ncclMax,
+                              m->comm, st));
+    if (want_logits)
+      LRS_NCCL(nccl().AllGather(m->logits, m->logits_full, (size_t)c.vocab_size, ncclFloat32,
+                                m->comm, st));
+  }
   if (greedy_advance)
     LRS_CUDA(launch_advance(m->keys, m->d_tok, m->d_pos, B, m->d_step, n_steps_cap,
                             m->d_tokens_out, m->d_last, st));
@@ -537,8 +614,52 @@ int32_t read_argmax(lrs_model* m, int item, uint32_t* out) {
 
 extern "C" {
 
-lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
-                            const lrs_model_options* options, lrs_model** out) {
+}  // extern "C"
+
+namespace {
+
+// Row window [r0, r0 + n) of a tensor (rows are contiguous: no copy).
+lrs_tensor_desc rows_of(const lrs_tensor_desc& d, size_t r0, size_t n) {
+  lrs_tensor_desc o = d;
+  const size_t rb = d.rows ? d.nbytes / d.rows : 0;
+  o.data = static_cast<const uint8_t*>(d.data) + r0 * rb;
+  o.rows = n;
+  o.nbytes = n * rb;
+  return o;
+}
+
+// Column window [c0, c0 + n) of a tensor, copied into `buf` (whole blocks).
+int32_t cols_of(const lrs_tensor_desc& d, size_t c0, size_t n, const char* what,
+                std::vector<uint8_t>* buf, lrs_tensor_desc* out) {
+  uint32_t bv = 0, bb = 0;
+  if (!type_geometry(d.ggml_type, &bv, &bb)) return fail(LRS_ERR_UNSUPPORTED, "unknown ggml type");
+  if (c0 % bv || n % bv)
+    return fail(LRS_ERR_UNSUPPORTED, std::string("tensor-parallel split of ") + what +
+                                         " at column " + std::to_string(c0) +
+                                         " is not aligned to its " + std::to_string(bv) +
+                                         "-value blocks");
+  const size_t rb = d.rows ? d.nbytes / d.rows : 0, off = c0 / bv * bb, len = n / bv * bb;
+  buf->resize(d.rows * len);
+  for (size_t r = 0; r < d.rows; r++)
+    memcpy(buf->data() + r * len, static_cast<const uint8_t*>(d.data) + r * rb + off, len);
+  *out = d;
+  out->data = buf->data();
+  out->cols = n;
+  out->nbytes = buf->size();
+  return LRS_OK;
+}
+
+int32_t check_shape(const lrs_tensor_desc& d, size_t rows, size_t cols, const char* what) {
+  if (d.rows != rows || d.cols != cols)
+    return fail(LRS_ERR_INVALID, std::string("tensor ") + what + " has shape [" +
+                                     std::to_string(d.rows) + ", " + std::to_string(d.cols) +
+                                     "], expected [" + std::to_string(rows) + ", " +
+                                     std::to_string(cols) + "]");
+  return validate_tensor(d.nbytes, d.rows, d.cols, d.ggml_type);
+}
+
+int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_options* options,
+                     int rank, int world, ncclComm_t comm, lrs_model** out) {
   if (!be || !d || !out) return fail(LRS_ERR_INVALID, "null argument");
   const lrs_config& c = d->config;
   // LlamaConfig::validate, src/config.rs:57-89
@@ -571,46 +692,80 @@ lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
   if (opt.max_sequences == 0) opt.max_sequences = 1;
   LRS_CUDA(cudaSetDevice(be->device));
 
+  // Tensor parallelism (world > 1): heads, the MLP width and the LM-head rows
+  // are split evenly; q/k/v/gate/up/lm_head by rows, o/down by columns.
+  if (world > 1 && (c.num_key_value_heads % world || c.intermediate_size % world ||
+                    c.vocab_size % world))
+    return fail(LRS_ERR_UNSUPPORTED, "tensor-parallel degree " + std::to_string(world) +
+                                         " does not divide the KV heads, the MLP width and the vocabulary");
+  lrs_config cl = c;
+  cl.num_attention_heads /= world;
+  cl.num_key_value_heads /= world;
+  cl.intermediate_size /= world;
+  cl.vocab_size /= world;
+
   auto m = std::make_unique<lrs_model>();
   m->be = be;
-  m->c = c;
+  m->c = cl;
   m->opt = opt;
-  const size_t h = c.hidden_size, I = c.intermediate_size, kvw = (size_t)c.num_key_value_heads * c.head_dim;
+  m->tp_rank = rank;
+  m->tp_world = world;
+  m->comm = comm;
+  m->vocab_full = c.vocab_size;
+  m->vocab0 = rank * (int)cl.vocab_size;
+  const size_t h = c.hidden_size, I = cl.intermediate_size, kvw = (size_t)cl.num_key_value_heads * c.head_dim,
+               qw = (size_t)cl.num_attention_heads * c.head_dim, V = cl.vocab_size;
+  const size_t kvw_full = (size_t)c.num_key_value_heads * c.head_dim;
   int32_t rc;
   auto cleanup = [&](int32_t code) {
+    if (m->comm == comm) m->comm = nullptr;  // the caller owns a communicator it passed in
     lrs_model_destroy(m.release());
     return code;
   };
   if ((rc = upload_mat(d->embed_tokens, c.vocab_size, h, "model.embed_tokens.weight", &m->embed)))
     return cleanup(rc);
-  if (d->lm_head.data == d->embed_tokens.data) {
+  if (d->lm_head.data == d->embed_tokens.data && world == 1) {
     m->tied = true;
     m->lm = m->embed;
-  } else if ((rc = upload_mat(d->lm_head, c.vocab_size, h, "lm_head.weight", &m->lm))) {
+  } else if ((rc = check_shape(d->lm_head, c.vocab_size, h, "lm_head.weight")) ||
+             (rc = upload_mat(rows_of(d->lm_head, m->vocab0, V), V, h, "lm_head.weight", &m->lm))) {
     return cleanup(rc);
   }
   if ((rc = upload_vec(m.get(), d->final_norm, h, &m->final_norm))) return cleanup(rc);
   if (!m->final_norm) return cleanup(fail(LRS_ERR_INVALID, "missing model.norm.weight"));
   m->weight_bytes = m->lm.nbytes + m->embed.nbytes / c.vocab_size;
   m->layers.resize(c.num_hidden_layers);
+  std::vector<uint8_t> obuf, dbuf;
   for (uint32_t i = 0; i < c.num_hidden_layers; i++) {
     const lrs_layer_desc& s = d->layers[i];
     Layer& L = m->layers[i];
-    if ((rc = upload_mat(s.q_proj, h, h, "q_proj", &L.q)) ||
-        (rc = upload_mat(s.k_proj, kvw, h, "k_proj", &L.k)) ||
-        (rc = upload_mat(s.v_proj, kvw, h, "v_proj", &L.v)) ||
-        (rc = upload_mat(s.o_proj, h, h, "o_proj", &L.o)) ||
-        (rc = upload_mat(s.gate_proj, I, h, "gate_proj", &L.gate)) ||
-        (rc = upload_mat(s.up_proj, I, h, "up_proj", &L.up)) ||
-        (rc = upload_mat(s.down_proj, h, I, "down_proj", &L.down)))
+    lrs_tensor_desc o_loc = s.o_proj, d_loc = s.down_proj;
+    if ((rc = check_shape(s.q_proj, h, h, "q_proj")) ||
+        (rc = check_shape(s.k_proj, kvw_full, h, "k_proj")) ||
+        (rc = check_shape(s.v_proj, kvw_full, h, "v_proj")) ||
+        (rc = check_shape(s.o_proj, h, h, "o_proj")) ||
+        (rc = check_shape(s.gate_proj, (size_t)c.intermediate_size, h, "gate_proj")) ||
+        (rc = check_shape(s.up_proj, (size_t)c.intermediate_size, h, "up_proj")) ||
+        (rc = check_shape(s.down_proj, h, (size_t)c.intermediate_size, "down_proj")))
+      return cleanup(rc);
+    if (world > 1 && ((rc = cols_of(s.o_proj, rank * qw, qw, "o_proj", &obuf, &o_loc)) ||
+                      (rc = cols_of(s.down_proj, rank * I, I, "down_proj", &dbuf, &d_loc))))
+      return cleanup(rc);
+    if ((rc = upload_mat(rows_of(s.q_proj, rank * qw, qw), qw, h, "q_proj", &L.q)) ||
+        (rc = upload_mat(rows_of(s.k_proj, rank * kvw, kvw), kvw, h, "k_proj", &L.k)) ||
+        (rc = upload_mat(rows_of(s.v_proj, rank * kvw, kvw), kvw, h, "v_proj", &L.v)) ||
+        (rc = upload_mat(o_loc, h, qw, "o_proj", &L.o)) ||
+        (rc = upload_mat(rows_of(s.gate_proj, rank * I, I), I, h, "gate_proj", &L.gate)) ||
+        (rc = upload_mat(rows_of(s.up_proj, rank * I, I), I, h, "up_proj", &L.up)) ||
+        (rc = upload_mat(d_loc, h, I, "down_proj", &L.down)))
       return cleanup(rc);
     if (L.gate.type != L.up.type)
       return cleanup(fail(LRS_ERR_UNSUPPORTED, "gate_proj and up_proj must share a GGML type"));
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
-        (rc = upload_vec(m.get(), s.q_bias, h, &L.qb)) ||
-        (rc = upload_vec(m.get(), s.k_bias, kvw, &L.kb)) ||
-        (rc = upload_vec(m.get(), s.v_bias, kvw, &L.vb)))
+        (rc = upload_vec(m.get(), s.q_bias ? s.q_bias + rank * qw : nullptr, qw, &L.qb)) ||
+        (rc = upload_vec(m.get(), s.k_bias ? s.k_bias + rank * kvw : nullptr, kvw, &L.kb)) ||
+        (rc = upload_vec(m.get(), s.v_bias ? s.v_bias + rank * kvw : nullptr, kvw, &L.vb)))
       return cleanup(rc);
     if (!L.in_norm || !L.post_norm) return cleanup(fail(LRS_ERR_INVALID, "missing layer norm weight"));
     m->weight_bytes += L.q.nbytes + L.k.nbytes + L.v.nbytes + L.o.nbytes + L.gate.nbytes +
@@ -636,7 +791,7 @@ lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
   m->kv_elem = opt.kv_dtype == LRS_KV_BF16 ? 2 : 4;
   m->pages_per_seq = (int)((opt.max_seq_len + kPageSize - 1) / kPageSize);
   m->total_pages = m->pages_per_seq * (int)opt.max_sequences;
-  const size_t page_elems = (size_t)c.num_key_value_heads * kPageSize * c.head_dim;
+  const size_t page_elems = (size_t)cl.num_key_value_heads * kPageSize * c.head_dim;
   for (auto& L : m->layers) {
     if ((rc = model_alloc(m.get(), &L.kpool, (size_t)m->total_pages * page_elems * m->kv_elem)) ||
         (rc = model_alloc(m.get(), &L.vpool, (size_t)m->total_pages * page_elems * m->kv_elem)))
@@ -670,10 +825,53 @@ lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
     return cleanup(rc);
   m->gemm_scratch_bytes = gemm_scratch_bytes((int)B, std::max(h, I), m->be->sms);
   if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
+  if (world > 1 &&
+      (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))
+    return cleanup(rc);
   LRS_CUDA(cudaDeviceSynchronize());
   *out = m.release();
   return LRS_OK;
 }
+
+}  // namespace
+
+extern "C" {
+
+lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
+                            const lrs_model_options* options, lrs_model** out) {
+  return create_model(be, d, options, 0, 1, nullptr, out);
+}
+
+lrs_status lrs_tp_unique_id(uint8_t* id_out) {
+  if (!id_out) return fail(LRS_ERR_INVALID, "null argument");
+  const NcclApi& n = nccl();
+  if (!n.ok) return fail(LRS_ERR_UNSUPPORTED, n.err);
+  static_assert(sizeof(ncclUniqueId) == LRS_TP_ID_BYTES, "NCCL unique id size");
+  ncclUniqueId id;
+  LRS_NCCL(n.GetUniqueId(&id));
+  memcpy(id_out, &id, sizeof id);
+  return LRS_OK;
+}
+
+lrs_status lrs_model_create_tp(lrs_backend* be, const lrs_model_desc* d,
+                               const lrs_model_options* options, uint32_t rank, uint32_t world,
+                               const uint8_t* id, lrs_model** out) {
+  if (!be || !d || !id || !out) return fail(LRS_ERR_INVALID, "null argument");
+  if (world < 1 || rank >= world) return fail(LRS_ERR_INVALID, "tensor-parallel rank out of range");
+  if (world == 1) return create_model(be, d, options, 0, 1, nullptr, out);
+  const NcclApi& n = nccl();
+  if (!n.ok) return fail(LRS_ERR_UNSUPPORTED, n.err);
+  LRS_CUDA(cudaSetDevice(be->device));
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof uid);
+  ncclComm_t comm = nullptr;
+  LRS_NCCL(n.CommInitRank(&comm, (int)world, uid, (int)rank));
+  int32_t rc = create_model(be, d, options, (int)rank, (int)world, comm, out);
+  if (rc) n.CommDestroy(comm);
+  return rc;
+}
+
+uint32_t lrs_model_tp_world(const lrs_model* m) { return m ? (uint32_t)m->tp_world : 0; }
 
 void lrs_model_destroy(lrs_model* m) {
   if (!m) return;
@@ -693,6 +891,7 @@ void lrs_model_destroy(lrs_model* m) {
   if (!m->tied) cudaFree(m->lm.d);
   for (void* p : m->allocs) cudaFree(p);
   cudaFree(m->d_tokens_out);
+  if (m->comm) nccl().CommDestroy(m->comm);
   delete m;
 }
 
@@ -724,7 +923,7 @@ lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens,
     return fail(LRS_ERR_INVALID, "position " + std::to_string(start_pos + n - 1) +
                                      " exceeds configured context " + std::to_string(m->opt.max_seq_len));
   for (size_t i = 0; i < n; i++)
-    if (tokens[i] >= m->c.vocab_size)
+    if (tokens[i] >= m->vocab_full)
       return fail(LRS_ERR_INVALID, "token id " + std::to_string(tokens[i]) + " is outside vocabulary");
   LRS_CUDA(cudaSetDevice(m->be->device));
   int32_t rc = ensure_pages(m, (int)seq, start_pos + (uint32_t)n - 1);
@@ -744,7 +943,8 @@ lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens,
     if (rc) return rc;
   }
   if (logits_out)
-    LRS_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->c.vocab_size * 4,
+    LRS_CUDA(cudaMemcpyAsync(logits_out, m->tp_world > 1 ? m->logits_full : m->logits,
+                             (size_t)m->vocab_full * 4,
                              cudaMemcpyDeviceToHost, m->be->stream));
   LRS_CUDA(cudaStreamSynchronize(m->be->stream));
   if ((rc = check_device_error(m->be))) return rc;
@@ -767,7 +967,7 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
   std::vector<int> tok(B), pos(B), sq(B);
   for (int i = 0; i < B; i++) {
     if (seqs[i] >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
-    if (first_tokens[i] >= m->c.vocab_size) return fail(LRS_ERR_INVALID, "token id is outside vocabulary");
+    if (first_tokens[i] >= m->vocab_full) return fail(LRS_ERR_INVALID, "token id is outside vocabulary");
     if ((size_t)start_pos[i] + n_steps > m->opt.max_seq_len)
       return fail(LRS_ERR_INVALID, "decode steps exceed configured context");
     for (int j = 0; j < i; j++)
@@ -856,7 +1056,7 @@ lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* s
   const int B = (int)n_seqs;
   std::vector<int> tok(B), ps(B), sq(B);
   for (int i = 0; i < B; i++) {
-    if (seqs[i] >= m->opt.max_sequences || tokens[i] >= m->c.vocab_size ||
+    if (seqs[i] >= m->opt.max_sequences || tokens[i] >= m->vocab_full ||
         pos[i] >= m->opt.max_seq_len)
       return fail(LRS_ERR_INVALID, "profile_step: item out of range");
     tok[i] = (int)tokens[i];

@@ -288,6 +288,7 @@ struct GemmArgs {
   const float* xscale;   // [batch] power-of-two item scales
   float* part[kGemvMaxSeg];  // [pair][kgroups][batch][rows], kgroups > 1
   unsigned long long* keys;  // [batch], EPI_ARGMAX
+  int argmax_base;
 };
 
 // Adds one 32-column group of 16 rows x 8*NT items into acc.  Tiles go in
@@ -530,7 +531,7 @@ __global__ void __launch_bounds__(Shape<PAIR>::kThreads)
           if constexpr (PAIR) *o = (y / (1.0f + expf(-y))) * acc2[PAIR ? j : 0][c];
         } else {
           if (o) *o = y;
-          const unsigned long long k = argmax_pack(y, (uint32_t)r);
+          const unsigned long long k = argmax_pack(y, (uint32_t)(r + a.argmax_base));
           key[c & 1] = k > key[c & 1] ? k : key[c & 1];
         }
       }
@@ -559,7 +560,7 @@ struct EpiArgs {
   GemvSeg seg[kGemvMaxSeg];
   const float* part[kGemvMaxSeg];
   int row0[kGemvMaxSeg + 1];
-  int nseg, kgroups, batch, epi;
+  int nseg, kgroups, batch, epi, argmax_base;
   unsigned long long* keys;
 };
 
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(256) gemm_epilogue_kernel(const __grid_constan
       *o = (y / (1.0f + expf(-y))) * y2;
     } else {
       if (o) *o = y;
-      key = argmax_pack(y, (uint32_t)r);
+      key = argmax_pack(y, (uint32_t)(r + e.argmax_base));
     }
   }
   if (e.epi == EPI_ARGMAX) {
@@ -718,6 +719,7 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
       a.xs = xs + (size_t)(b0 / 8) * (kSRec / 4);
       a.xscale = xscale + b0;
       a.keys = p.argmax_keys ? p.argmax_keys + b0 : nullptr;
+      a.argmax_base = p.argmax_base;
       int ctas = 0;
       for (int k = 0; k < a.nseg; k++) {
         a.seg[k] = p.seg[i + k];
@@ -746,6 +748,7 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
         ea.batch = B;
         ea.epi = p.epi;
         ea.keys = a.keys;
+        ea.argmax_base = p.argmax_base;
       }
       const dim3 grid(ctas, a.kgroups);
       e = pair ? launch_type<true>(a.seg[0].type, nt, a, grid, st)
