@@ -54,6 +54,8 @@ WORKLOADS = {
                model="Qwen2.5-7B-shape", quant="q4km"),
     "c2": dict(cfg="config_c2", seed=1, recipe="Q4K", seqs=1, prompt=512, decode=128, ctx=4096,
                model="Qwen2.5-1.5B-shape", quant="q4k"),
+    "c4": dict(cfg="config_c4", seed=3, recipe="Q4K", seqs=16, prompt=2048, decode=256, ctx=8192,
+               model="Qwen2.5-32B-shape", quant="q4k"),
     "c0": dict(cfg="config_c0", seed=0, recipe="Q4KM", seqs=1, prompt=128, decode=32, ctx=4096,
                model="Qwen2.5-0.5B-shape", quant="q4km"),
 }
@@ -232,9 +234,10 @@ def run_ours(args, wl):
         return float(t.item())
 
     total_seqs = args.seqs or wl["seqs"]
-    if total_seqs % world:
+    tp = args.tp and world > 1
+    if not tp and total_seqs % world:
         raise SystemExit("sequences must divide evenly over the GPUs")
-    B = total_seqs // world
+    B = total_seqs if tp else total_seqs // world
     P = args.prompt or wl["prompt"]
     ncpu = os.cpu_count() or 1
 
@@ -242,15 +245,22 @@ def run_ours(args, wl):
     cfg, sm = build_model(lrs, wl, ncpu, barrier if world > 1 else None, builder=local == 0)
     build_s = time.perf_counter() - t_build
     be = lrs.CudaBackend(local)
+    tp_kw = {}
+    if tp:
+        # one tensor-parallel model over the ranks; rank 0 makes the NCCL id
+        obj = [lrs.tp_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(obj, src=0)
+        tp_kw = dict(tp_rank=rank, tp_world=world, tp_id=obj[0])
     model = lrs.CudaQwen2Model(be, sm.desc(), max_seq_len=wl["ctx"], max_sequences=B,
-                               kv_bf16=args.kv_bf16)
+                               kv_bf16=args.kv_bf16, **tp_kw)
     ext = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local))
 
     def ev():
         return torch.cuda.Event(enable_timing=True)
 
     # ---- prefill every local sequence (prompt of P uniform ids) ----
-    prompts = [lrs.prompt_tokens(wl["seed"], P, cfg.vocab_size, rank * B + s) for s in range(B)]
+    first_seq = 0 if tp else rank * B
+    prompts = [lrs.prompt_tokens(wl["seed"], P, cfg.vocab_size, first_seq + s) for s in range(B)]
     firsts = []
     p0, p1 = ev(), ev()
     p0.record(ext)
@@ -359,7 +369,9 @@ def run_ours(args, wl):
                                    f"({P} prompt + greedy decode), ctx {wl['ctx']}, "
                                    + (f"{cfg.num_hidden_layers} layers (profiling case), "
                                       if wl.get("layers") else "") +
-                                   f"data-parallel over {world} GPU(s)",
+                                   (f"tensor-parallel over {world} GPUs" if tp else
+                                      f"data-parallel over {world} GPU(s)"),
+                       "parallelism": f"tp{world}" if tp else f"dp{world}",
                        "sequences_per_gpu": B, "prompt": P,
                        "kv_cache": "bf16" if args.kv_bf16 else "f32",
                        "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights streamed per step"},
@@ -465,6 +477,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small profiling cases only)")
     ap.add_argument("--ctx", type=int, default=0, help="override the context length")
+    ap.add_argument("--tp", action="store_true",
+                    help="one tensor-parallel model over the ranks instead of data parallel")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
     ap.add_argument("--gemv-sweep", action="store_true", help="BASELINE config 1 GEMV sweep")

@@ -824,6 +824,22 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
     return cleanup(rc);
   m->gemm_scratch_bytes = gemm_scratch_bytes((int)B, std::max(h, I), m->be->sms);
+  {
+    // the tcgen05 path keeps all K-group partials of a launch: size for the
+    // largest one at 64 items (q/k/v, o, gate+up, down, LM head)
+    const Layer& L0 = m->layers[0];
+    GemvMat mats[][3] = {{mat_of(L0.q, nullptr, 1), mat_of(L0.k, nullptr, 1), mat_of(L0.v, nullptr, 1)},
+                         {mat_of(L0.o, nullptr, 1)},
+                         {mat_of(L0.gate, nullptr, 1, nullptr, &L0.up)},
+                         {mat_of(L0.down, nullptr, 1)},
+                         {mat_of(m->lm, nullptr, 1)}};
+    const int nm[] = {3, 1, 1, 1, 1}, epis[] = {EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_ADD, EPI_ARGMAX};
+    for (int i = 0; i < 5; i++) {
+      GemvParams p;
+      if (gemv_plan(&p, mats[i], nm[i], epis[i], (int)std::min<size_t>(B, 64)) == LRS_OK)
+        m->gemm_scratch_bytes = std::max(m->gemm_scratch_bytes, gemm_tc_scratch_bytes(p, m->be->sms));
+    }
+  }
   if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
   if (world > 1 &&
       (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))

@@ -684,6 +684,27 @@ size_t gemm_scratch_bytes(int batch, int max_cols, int sms) {
   return xq + parts;
 }
 
+cudaError_t gemm_partials_epilogue(const GemvParams& p, const float* const* parts, int kgroups,
+                                   cudaStream_t st) {
+  EpiArgs ea = {};
+  int row0 = 0;
+  for (int k = 0; k < p.nseg; k++) {
+    ea.seg[k] = p.seg[k];
+    ea.part[k] = parts[k];
+    ea.row0[k] = row0;
+    row0 += p.seg[k].rows;
+  }
+  ea.row0[p.nseg] = row0;
+  ea.nseg = p.nseg;
+  ea.kgroups = kgroups;
+  ea.batch = p.batch;
+  ea.epi = p.epi;
+  ea.keys = p.argmax_keys;
+  ea.argmax_base = p.argmax_base;
+  gemm_epilogue_kernel<<<dim3((row0 + 255) / 256, p.batch), 256, 0, st>>>(ea);
+  return cudaGetLastError();
+}
+
 cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t st) {
   const int Ball = p.batch, cols = p.cols;
   const bool pair = p.epi == EPI_SWIGLU;

@@ -1,0 +1,465 @@
+// gemm_tc.cu -- batched Q4_K matmul (33..64 items: decode batches and prefill
+// chunks) on the 5th-generation tensor cores: tcgen05.mma with the
+// accumulators in tensor memory (TMEM).
+//
+// Replaces B independent CpuBackend::matvec calls (src/backend.rs:143-162)
+// for Q4_K weights, the bulk of the q4k/q4km models (q, k, o, gate, up).
+//
+// Arithmetic.  A Q4_K super-block row is w_k = d*sc_g*q_k - dmin*m_g
+// (value_at, src/quant.rs:404-440) with 6-bit sc_g, m_g per 32-column group g.
+// sc_g*q_k <= 63*15 = 945 is an exact f16 integer, so the A tile holds
+// f16(sc_g*q_k) and the whole 256-column super-block accumulates in one TMEM
+// accumulator; per super-block and element the epilogue adds
+//     d * T - dmin * M,   T = sum_k sc q_k x_k,   M = sum_g m_g sum_{k in g} x_k
+// where M comes from a second, K = 16 MMA of A_min = 32*m_g (exact f16) with
+// B_min = (group sums of x)/32.  x is scaled per item by a power of two (max
+// |x/s| in [2^13, 2^14)) and split into f16 hi + lo; the B tile stacks the
+// two as rows 2i and 2i+1 (N = 128 for 64 items), so one MMA covers both and
+// the epilogue adds the pair.  Every product is exact and accumulates in f32.
+//
+// Layout.  A, B, A_min and B_min are K-major, no swizzle: 8x8 f16 core
+// matrices (8 rows of 16 contiguous bytes), K-adjacent core matrices 128 B
+// apart (LBO), 8-row groups 16 core matrices apart (SBO = 2048 B for a
+// 128-column K chunk).  Inside every 4 columns the order is (0, 2, 1, 3): the
+// order in which a nibble mask of a 4-byte word yields f16 pairs.  The split x
+// is written by xsplit_tc_kernel in exactly the shared-memory image, so it is
+// staged with one cp.async.bulk per 128-column chunk.
+//
+// Pipeline (256 threads, one CTA per SM):
+//   warps 0-3 (one weight row per thread) decode each half super-block into
+//     the A tile (double-buffered), thread 0 also issues the bulk copy of the
+//     x tile and, once the 128 rows are written, the MMAs (8 x K=16 per half,
+//     plus the A_min MMA) and tcgen05.commit;
+//   warps 4-7 (TMEM lanes 32*(w-4)...) read the finished super-block's
+//     accumulators with tcgen05.ld and update 64 per-item f32 sums;
+//   TMEM holds two super-blocks (2 x (128 + 128) columns) so the epilogue of
+//   super-block s overlaps the MMAs of s+1.
+// Results are partial sums per K group (grid.y), reduced with the epilogue of
+// gemm_mma.cu (fixed order).  Every mbarrier wait is bounded; a timeout sets
+// the error word, the kernel stops issuing work, frees its TMEM and returns.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.h"
+#include "device_common.cuh"
+#include "gemv.cuh"
+
+namespace lrs {
+namespace {
+
+constexpr int kItems = 64;
+constexpr int kN = 2 * kItems;       // B rows: (item, hi/lo)
+constexpr int kRows = 128;           // weight rows per CTA = TMEM lanes
+constexpr int kKC = 128;             // columns per A/B tile (half a super-block)
+constexpr int kTileA = kRows * kKC * 2;  // 32 KB
+constexpr int kTileB = kN * kKC * 2;     // 32 KB
+constexpr int kTileMin = 128 * 16 * 2;   // 4 KB (A_min or B_min)
+constexpr int kSBO = (kKC / 8) * 128;    // 2048
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+
+// smem: A[2] | B[2] | Amin[2] | Bmin[2] | barriers
+constexpr int kOffA = 0, kOffB = 2 * kTileA, kOffAmin = kOffB + 2 * kTileB,
+              kOffBmin = kOffAmin + 2 * kTileMin, kOffBar = kOffBmin + 2 * kTileMin;
+constexpr int kSmem = kOffBar + 128;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, no swizzle, version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor, kind::f16: f16 A and B, f32 D, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+  __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b),
+                      *reinterpret_cast<const __half2*>(&c));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2u(float a, float b) {
+  __half2 r = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint4 ldg128(const uint8_t* p) {
+  uint4 v;
+  asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xffu; }
+
+// Byte offset of element (row n, position k) of a K-major no-swizzle tile with
+// 16 k-groups per row group; the column order inside 4 columns is (0, 2, 1, 3).
+__device__ __forceinline__ int tile_off(int n, int k, int sbo) {
+  const int c4 = k & 3, pos = (k & ~3) | (c4 == 1 ? 2 : c4 == 2 ? 1 : c4);
+  return (n >> 3) * sbo + (pos >> 3) * 128 + (n & 7) * 16 + (pos & 7) * 2;
+}
+
+// ---- x preparation: one CTA per item slot (64, zero-padded) -------------------
+// xt: [cols/128][N x 128] f16 tiles; xm: [cols/256][N x 16] group-sum tiles;
+// xscale: [64] item scales.
+__global__ void __launch_bounds__(256)
+    xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, uint8_t* xt, uint8_t* xm,
+                     float* xscale) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* xr = x + (size_t)b * x_ld;
+  __shared__ float red[8];
+  float mx = 0.0f;
+  if (b < batch)
+    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xr[c]));
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
+  int e = 14;
+  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);
+  const float inv = ldexpf(1.0f, 14 - e);
+  if (threadIdx.x == 0) xscale[b] = ldexpf(1.0f, e - 14);
+  for (int g = warp; g * 32 < cols; g += 8) {
+    const int k = g * 32 + lane;
+    const float v = b < batch ? xr[k] * inv : 0.0f;
+    const __half h = __float2half_rn(v);
+    const __half l = __float2half_rn(v - __half2float(h));
+    uint8_t* tile = xt + (size_t)(k / kKC) * kTileB;
+    *reinterpret_cast<__half*>(tile + tile_off(2 * b, k % kKC, kSBO)) = h;
+    *reinterpret_cast<__half*>(tile + tile_off(2 * b + 1, k % kKC, kSBO)) = l;
+    float sum = v;
+    for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // group sums / 32 (exact), hi/lo, at position g % 8 of the super-block's B_min
+    uint8_t* mt = xm + (size_t)(g / 8) * kTileMin;
+    if (lane < 2) {
+      const float s = sum * (1.0f / 32.0f);
+      const __half sh = __float2half_rn(s);
+      const __half val = lane == 0 ? sh : __float2half_rn(s - __half2float(sh));
+      const int n = 2 * b + lane, pos = g % 8;
+      *reinterpret_cast<__half*>(mt + (n >> 3) * 256 + (n & 7) * 16 + pos * 2) = val;
+      // positions 8..15 (second core matrix) stay zero
+      if ((g % 8) == 0)
+        *reinterpret_cast<uint4*>(mt + (n >> 3) * 256 + 128 + (n & 7) * 16) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+struct TcArgs {
+  const uint8_t* w;  // Q4_K rows
+  int rows, rb, cols, batch, kgroups;
+  const uint8_t* xt;
+  const uint8_t* xm;
+  const float* xscale;
+  float* part;  // [kgroups][batch][rows]
+  int* error_flag;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_constant__ TcArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t tmem_base_sh;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full_b = bars;        // [2] x tile landed
+  uint64_t* mma_done = bars + 2;  // [2] MMAs of a half step finished (A/B buffer free)
+  uint64_t* acc_full = bars + 4;  // [2] super-block accumulator ready
+  uint64_t* acc_empty = bars + 6; // [2] epilogue finished reading it
+  uint64_t* a_full = bars + 8;    // [2] the 128 producer rows of an A tile are written
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&full_b[i], 1);
+      mbar_init(&mma_done[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+      mbar_init(&a_full[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_sh)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  const int nsb_all = a.cols / 256;
+  const int s0 = (int)((long long)blockIdx.y * nsb_all / a.kgroups);
+  const int s1 = (int)((long long)(blockIdx.y + 1) * nsb_all / a.kgroups);
+  const int nsb = s1 - s0;
+  const int row0 = blockIdx.x * kRows;
+  bool ok = true;
+
+  if (warp < 4) {
+    // ---------------- producers: decode A, issue copies and MMAs ----------------
+    const int r = tid;
+    const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
+    const uint64_t pol = evict_first_policy();
+    constexpr uint32_t idesc = idesc_f16(kRows, kN);
+    for (int hs = 0; hs < 2 * nsb && ok; hs++) {
+      const int sb = hs >> 1, half = hs & 1, buf = hs & 1, tb = sb & 1;
+      const int sbg = s0 + sb;
+      if (hs >= 2) ok = mbar_wait_bounded(&mma_done[buf], ((hs - 2) >> 1) & 1);
+      if (!ok) break;
+      uint8_t* A = smem + kOffA + buf * kTileA;
+      if (tid == 0) {
+        const uint32_t bytes = kTileB + (half == 0 ? kTileMin : 0);
+        mbar_expect_tx(&full_b[buf], bytes);
+        tma_load_1d(smem + kOffB + buf * kTileB, a.xt + (size_t)(2 * sbg + half) * kTileB, kTileB,
+                    &full_b[buf], pol);
+        if (half == 0)
+          tma_load_1d(smem + kOffBmin + tb * kTileMin, a.xm + (size_t)sbg * kTileMin, kTileMin,
+                      &full_b[buf], pol);
+      }
+      // decode: row r, columns [128*half, 128*half + 128) of super-block sbg
+      const uint8_t* u = rp + (size_t)sbg * 144;
+      const uint4 hd = ldg128(u);
+      uint4 q[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) q[i] = ldg128(u + 16 + 64 * half + 16 * i);
+#pragma unroll
+      for (int gl = 0; gl < 4; gl++) {
+        const int g = 4 * half + gl;
+        uint32_t sc;
+        if (g < 4) {
+          sc = byte_of(hd.y, g) & 63u;
+        } else {
+          sc = (byte_of(hd.w, g - 4) & 15u) | ((byte_of(hd.y, g - 4) >> 6) << 4);
+        }
+        const uint32_t sc2 = h2u((float)sc, (float)sc);
+        const uint32_t nb2 = h2u(-1024.0f * (float)sc, -1024.0f * (float)sc);
+        // group g uses pair p = g/2 (bytes 32*(p - 2*half) .. of this half's 64 bytes),
+        // low nibbles for even g, high for odd
+        const int sh = 4 * (g & 1);
+        const uint32_t* wq = reinterpret_cast<const uint32_t*>(q) + 8 * (gl >> 1);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const uint32_t w0 = wq[2 * e] >> sh, w1 = wq[2 * e + 1] >> sh;
+          uint4 v;
+          v.x = hfma2u((w0 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+          v.y = hfma2u(((w0 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+          v.z = hfma2u((w1 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+          v.w = hfma2u(((w1 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+          const int j = gl * 4 + e;  // k-group within the 128-column tile
+          *reinterpret_cast<uint4*>(A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16) = v;
+        }
+      }
+      if (half == 0) {
+        // A_min row: 32*m_g for the 8 groups, then 8 zeros
+        uint32_t mw[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          float m2[2];
+#pragma unroll
+          for (int k = 0; k < 2; k++) {
+            const int g = 2 * i + k;
+            const uint32_t mn = g < 4 ? (byte_of(hd.z, g) & 63u)
+                                      : ((byte_of(hd.w, g - 4) >> 4) | ((byte_of(hd.z, g - 4) >> 6) << 4));
+            m2[k] = 32.0f * (float)mn;
+          }
+          mw[i] = h2u(m2[0], m2[1]);
+        }
+        uint8_t* Am = smem + kOffAmin + tb * kTileMin;
+        *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + (r & 7) * 16) =
+            make_uint4(mw[0], mw[1], mw[2], mw[3]);
+        *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async();
+      mbar_arrive(&a_full[buf]);
+      if (tid == 0) {
+        ok = mbar_wait_bounded(&a_full[buf], (hs >> 1) & 1) &&
+             mbar_wait_bounded(&full_b[buf], (hs >> 1) & 1);
+        if (ok && half == 0 && sb >= 2) ok = mbar_wait_bounded(&acc_empty[tb], ((sb - 2) >> 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t d_main = tmem + tb * 256, d_min = d_main + kN;
+          const uint32_t a0 = sbase + kOffA + buf * kTileA, b0 = sbase + kOffB + buf * kTileB;
+#pragma unroll
+          for (int t = 0; t < kKC / 16; t++)
+            tc_mma(d_main, smem_desc(a0 + t * 256, 128, kSBO), smem_desc(b0 + t * 256, 128, kSBO),
+                   idesc, (half | t) != 0);
+          if (half == 0)
+            tc_mma(d_min, smem_desc(sbase + kOffAmin + tb * kTileMin, 128, 256),
+                   smem_desc(sbase + kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
+          tc_commit(&mma_done[buf]);
+          if (half == 1) tc_commit(&acc_full[tb]);
+        } else if (a.error_flag) {
+          atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+        }
+      }
+      // the other producers learn of a failed wait at their next bounded wait
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> per-item sums ----------------
+    const int r = tid - 128;  // TMEM lane / row
+    const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+    const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
+    float acc[kItems];
+#pragma unroll
+    for (int i = 0; i < kItems; i++) acc[i] = 0.0f;
+    for (int sb = 0; sb < nsb && ok; sb++) {
+      const int tb = sb & 1;
+      const uint32_t hx = *reinterpret_cast<const uint32_t*>(rp + (size_t)(s0 + sb) * 144);
+      const float d = f16_bits((uint16_t)(hx & 0xffffu)), dmin = f16_bits((uint16_t)(hx >> 16));
+      ok = mbar_wait_bounded(&acc_full[tb], (sb >> 1) & 1);
+      if (!ok) {
+        if (a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kN / 32; c++) {
+        float T[32], M[32];
+        tc_ld32(tmem + lane_off + tb * 256 + 32 * c, T);
+        tc_ld32(tmem + lane_off + tb * 256 + kN + 32 * c, M);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int item = 16 * c + i;
+          acc[item] = fmaf(d, T[2 * i] + T[2 * i + 1], fmaf(-dmin, M[2 * i] + M[2 * i + 1], acc[item]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[tb]);
+    }
+    // partial sums, in units of the true x (item scales are powers of two)
+    const int row = row0 + r;
+    if (ok && row < a.rows) {
+      float* pp = a.part + (size_t)blockIdx.y * a.batch * a.rows + row;
+#pragma unroll
+      for (int i = 0; i < kItems; i++)
+        if (i < a.batch) pp[(size_t)i * a.rows] = acc[i] * a.xscale[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const GemvParams& p) {
+  if (p.batch <= 32 || p.batch > kItems || p.cols % 256 || p.norm_w) return false;
+  for (int i = 0; i < p.nseg; i++)
+    if (p.seg[i].type != LRS_GGML_Q4_K) return false;
+  return true;
+}
+
+namespace {
+int tc_kgroups(const GemvParams& p, int sms) {
+  int ctas = 0;
+  for (int i = 0; i < p.nseg; i++) ctas += (p.seg[i].rows + kRows - 1) / kRows;
+  const int nsb = p.cols / 256;
+  return ctas >= sms ? 1 : std::max(1, std::min(nsb, sms / ctas));
+}
+}  // namespace
+
+size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms) {
+  const int kg = tc_kgroups(p, sms);
+  size_t rows = 0;
+  for (int i = 0; i < p.nseg; i++) rows += p.seg[i].rows;
+  return (size_t)(p.cols / kKC) * kTileB + (size_t)(p.cols / 256) * kTileMin + kItems * 4 +
+         (size_t)kg * p.batch * rows * 4 * (p.epi == EPI_SWIGLU ? 2 : 1) + 1024;
+}
+
+// Partial sums for every segment (and the pair's second matrix), then the
+// fixed-order epilogue shared with gemm_mma.cu.
+cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_q4k_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int cols = p.cols, B = p.batch;
+  const bool pair = p.epi == EPI_SWIGLU;
+  auto align = [](void* q) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255));
+  };
+  uint8_t* xt = align(scratch);
+  uint8_t* xm = xt + (size_t)(cols / kKC) * kTileB;
+  float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * kTileMin);
+  float* part = xscale + kItems;
+  xsplit_tc_kernel<<<kItems, 256, 0, st>>>(p.x, p.x_ld, cols, B, xt, xm, xscale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int kgroups = tc_kgroups(p, sms);
+  const float* parts[kGemvMaxSeg];
+  float* cur = part;
+  for (int i = 0; i < p.nseg; i++) {
+    parts[i] = cur;
+    for (int m = 0; m < (pair ? 2 : 1); m++) {
+      TcArgs a{};
+      a.w = m ? p.seg[i].w2 : p.seg[i].w;
+      a.rows = p.seg[i].rows;
+      a.rb = p.seg[i].rb;
+      a.cols = cols;
+      a.batch = B;
+      a.kgroups = kgroups;
+      a.xt = xt;
+      a.xm = xm;
+      a.xscale = xscale;
+      a.part = cur;
+      a.error_flag = p.error_flag;
+      cur += (size_t)kgroups * B * a.rows;
+      gemm_tc_q4k_kernel<<<dim3((a.rows + kRows - 1) / kRows, kgroups), kThreads, kSmem, st>>>(a);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+  }
+  return gemm_partials_epilogue(p, parts, kgroups, st);
+}
+
+}  // namespace lrs

@@ -725,6 +725,11 @@ cudaError_t launch_cfg(const void* kernel, size_t smem, int grid, int threads,
 
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
   const bool pair = p.epi == EPI_SWIGLU;
+  // LRS_NO_TCGEN05=1 keeps Q4_K batches on the mma.sync kernel (comparison runs)
+  static const bool tc_off = getenv("LRS_NO_TCGEN05") != nullptr;
+  if (!tc_off && p.scratch && gemm_tc_supported(p) &&
+      p.scratch_bytes >= gemm_tc_scratch_bytes(p, num_sms))
+    return gemm_tc_launch(p, p.scratch, num_sms, stream);
   if (p.batch >= 2 && p.scratch && gemm_supported(p) &&
       p.scratch_bytes >= gemm_scratch_bytes(p.batch, p.cols, num_sms))
     return gemm_launch(p, p.scratch, num_sms, stream);

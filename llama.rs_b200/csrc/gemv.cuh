@@ -63,5 +63,13 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
 bool gemm_supported(const GemvParams& p);
 size_t gemm_scratch_bytes(int batch, int max_cols, int sms);
 cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
+// Fixed-order sum of K-group partials [segment][pair][kgroups][batch][rows] + epilogue.
+cudaError_t gemm_partials_epilogue(const GemvParams& p, const float* const* parts, int kgroups,
+                                   cudaStream_t stream);
+
+// Batched Q4_K matmul on tcgen05 (gemm_tc.cu), 33..64 items.
+bool gemm_tc_supported(const GemvParams& p);
+size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms);
+cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
 
 }  // namespace lrs

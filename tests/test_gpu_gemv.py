@@ -128,3 +128,20 @@ def test_sweep_shapes_every_row(lrs, orc, backend, qt, shape):
         ref = orc.matvec(orc.SCALAR, t.data, int(t.quant_type), rows, cols, x[b])
         _check_rows(got[b], ref)
     backend.release(t)
+
+
+@pytest.mark.parametrize("shape", [(1000, 512), (300, 3584), (4864, 896 * 2)], ids=str)
+@pytest.mark.parametrize("batch", [33, 64])
+def test_tcgen05_q4k_batches(lrs, orc, backend, shape, batch):
+    """Q4_K batches of 33..64 run on the tcgen05 kernel (TMEM accumulators)."""
+    rows, cols = shape
+    t = _matrix(lrs, "Q4_K", rows, cols, 21)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    x[1] *= 1e-3  # per-item scales differ by orders of magnitude
+    x[2] *= 50.0
+    got = backend.matvec_batched(t, x)
+    for b in range(batch):
+        ref = orc.matvec(orc.SCALAR, t.data, int(t.quant_type), rows, cols, x[b])
+        _check_rows(got[b], ref)
+    backend.release(t)
