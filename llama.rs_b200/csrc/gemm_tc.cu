@@ -244,8 +244,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
     const uint64_t pol = evict_first_policy();
     constexpr uint32_t idesc = idesc_f16(kRows, kN);
-    for (int hs = 0; hs < 2 * nsb && ok; hs++) {
-      const int sb = hs >> 1, half = hs & 1, buf = hs & 1, tb = sb & 1;
+    // the raw super-block (header + 128 code bytes) one super-block ahead
+    uint4 cur[9], nxt[9];
+    auto load_sb = [&](int sbg, uint4(&dst)[9]) {
+      const uint8_t* u = rp + (size_t)sbg * 144;
+#pragma unroll
+      for (int i = 0; i < 9; i++) dst[i] = ldg128(u + 16 * i);
+    };
+    if (nsb > 0) load_sb(s0, cur);
+    for (int sb = 0; sb < nsb && ok; sb++) {
+      if (sb + 1 < nsb) load_sb(s0 + sb + 1, nxt);
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+      if (!ok) break;
+      const int hs = 2 * sb + half, buf = half, tb = sb & 1;
       const int sbg = s0 + sb;
       if (hs >= 2) ok = mbar_wait_bounded(&mma_done[buf], ((hs - 2) >> 1) & 1);
       if (!ok) break;
@@ -260,11 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
                       &full_b[buf], pol);
       }
       // decode: row r, columns [128*half, 128*half + 128) of super-block sbg
-      const uint8_t* u = rp + (size_t)sbg * 144;
-      const uint4 hd = ldg128(u);
+      const uint4 hd = cur[0];
       uint4 q[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) q[i] = ldg128(u + 16 + 64 * half + 16 * i);
+      for (int i = 0; i < 4; i++) q[i] = cur[1 + 4 * half + i];
 #pragma unroll
       for (int gl = 0; gl < 4; gl++) {
         const int g = 4 * half + gl;
@@ -336,6 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
         }
       }
       // the other producers learn of a failed wait at their next bounded wait
+          }
+#pragma unroll
+      for (int i = 0; i < 9; i++) cur[i] = nxt[i];
     }
   } else {
     // ---------------- epilogue: TMEM -> per-item sums ----------------
