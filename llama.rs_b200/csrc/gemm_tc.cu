@@ -25,12 +25,13 @@
 // is written by xsplit_tc_kernel in exactly the shared-memory image, so it is
 // staged with one cp.async.bulk per 128-column chunk.
 //
-// Pipeline (256 threads, one CTA per SM):
-//   warps 0-3 (one weight row per thread) decode each half super-block into
-//     the A tile (double-buffered), thread 0 also issues the bulk copy of the
-//     x tile and, once the 128 rows are written, the MMAs (8 x K=16 per half,
-//     plus the A_min MMA) and tcgen05.commit;
-//   warps 4-7 (TMEM lanes 32*(w-4)...) read the finished super-block's
+// Pipeline (416 threads, one CTA per SM):
+//   warps 0-7 (two threads per weight row, two 32-column groups each) decode
+//     each half super-block into an A tile (three buffers);
+//   warp 12 (one thread) issues the bulk copies of the x tiles two half steps
+//     ahead (three buffers) and, once an A tile is complete, its MMAs
+//     (8 x K=16, plus the A_min MMA per super-block) and tcgen05.commit;
+//   warps 8-11 (TMEM lanes 32*(w-8)...) read the finished super-block's
 //     accumulators with tcgen05.ld and update 64 per-item f32 sums;
 //   TMEM holds two super-blocks (2 x (128 + 128) columns) so the epilogue of
 //   super-block s overlaps the MMAs of s+1.
@@ -57,11 +58,11 @@ constexpr int kTileA = kRows * kKC * 2;  // 32 KB
 constexpr int kTileB = kN * kKC * 2;     // 32 KB
 constexpr int kTileMin = 128 * 16 * 2;   // 4 KB (A_min or B_min)
 constexpr int kSBO = (kKC / 8) * 128;    // 2048
-constexpr int kThreads = 256;
+constexpr int kThreads = 416;  // 8 producer warps (2 per row), 4 epilogue warps, 1 issuer
 constexpr uint32_t kTmemCols = 512;
 
-// smem: A[2] | B[2] | Amin[2] | Bmin[2] | barriers
-constexpr int kOffA = 0, kOffB = 2 * kTileA, kOffAmin = kOffB + 2 * kTileB,
+// smem: A[3] | B[3] | Amin[2] | Bmin[2] | barriers
+constexpr int kOffA = 0, kOffB = 3 * kTileA, kOffAmin = kOffB + 3 * kTileB,
               kOffBmin = kOffAmin + 2 * kTileMin, kOffBar = kOffBmin + 2 * kTileMin;
 constexpr int kSmem = kOffBar + 128;
 
@@ -201,21 +202,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full_b = bars;        // [2] x tile landed
-  uint64_t* mma_done = bars + 2;  // [2] MMAs of a half step finished (A/B buffer free)
-  uint64_t* acc_full = bars + 4;  // [2] super-block accumulator ready
-  uint64_t* acc_empty = bars + 6; // [2] epilogue finished reading it
-  uint64_t* a_full = bars + 8;    // [2] the 128 producer rows of an A tile are written
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* full_b = bars;          // [3] x tile landed
+  uint64_t* a_full = bars + 3;      // [3] the 256 producer threads wrote an A tile
+  uint64_t* mma_done = bars + 6;    // [3] MMAs of a half step finished (A/B buffers free)
+  uint64_t* acc_full = bars + 9;    // [2] super-block accumulator ready
+  uint64_t* acc_empty = bars + 11;  // [2] epilogue finished reading it
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = smem_u32(smem);
 
   if (tid == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < 3; i++) {
       mbar_init(&full_b[i], 1);
+      mbar_init(&a_full[i], 256);
       mbar_init(&mma_done[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
-      mbar_init(&a_full[i], 128);
     }
     fence_barrier_init();
   }
@@ -234,127 +237,95 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
   const int nsb_all = a.cols / 256;
   const int s0 = (int)((long long)blockIdx.y * nsb_all / a.kgroups);
   const int s1 = (int)((long long)(blockIdx.y + 1) * nsb_all / a.kgroups);
-  const int nsb = s1 - s0;
+  const int nsb = s1 - s0, nhs = 2 * nsb;
   const int row0 = blockIdx.x * kRows;
   bool ok = true;
 
-  if (warp < 4) {
-    // ---------------- producers: decode A, issue copies and MMAs ----------------
-    const int r = tid;
+  if (warp < 8) {
+    // ---------------- producers: decode the A tiles ----------------
+    // thread (c, r): row r, groups 2c and 2c+1 of every half super-block
+    const int r = tid & 127, c = tid >> 7;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
-    const uint64_t pol = evict_first_policy();
-    constexpr uint32_t idesc = idesc_f16(kRows, kN);
-    // the raw super-block (header + 128 code bytes) one super-block ahead
-    uint4 cur[9], nxt[9];
-    auto load_sb = [&](int sbg, uint4(&dst)[9]) {
+    // this thread's raw bytes of a super-block (header, 32 code bytes per half),
+    // one super-block ahead
+    uint4 cur[5], nxt[5];
+    auto load_sb = [&](int sbg, uint4(&dst)[5]) {
       const uint8_t* u = rp + (size_t)sbg * 144;
-#pragma unroll
-      for (int i = 0; i < 9; i++) dst[i] = ldg128(u + 16 * i);
+      dst[0] = ldg128(u);
+      dst[1] = ldg128(u + 16 + 32 * c);
+      dst[2] = ldg128(u + 32 + 32 * c);
+      dst[3] = ldg128(u + 80 + 32 * c);
+      dst[4] = ldg128(u + 96 + 32 * c);
     };
     if (nsb > 0) load_sb(s0, cur);
     for (int sb = 0; sb < nsb && ok; sb++) {
       if (sb + 1 < nsb) load_sb(s0 + sb + 1, nxt);
 #pragma unroll
       for (int half = 0; half < 2; half++) {
-      if (!ok) break;
-      const int hs = 2 * sb + half, buf = half, tb = sb & 1;
-      const int sbg = s0 + sb;
-      if (hs >= 2) ok = mbar_wait_bounded(&mma_done[buf], ((hs - 2) >> 1) & 1);
-      if (!ok) break;
-      uint8_t* A = smem + kOffA + buf * kTileA;
-      if (tid == 0) {
-        const uint32_t bytes = kTileB + (half == 0 ? kTileMin : 0);
-        mbar_expect_tx(&full_b[buf], bytes);
-        tma_load_1d(smem + kOffB + buf * kTileB, a.xt + (size_t)(2 * sbg + half) * kTileB, kTileB,
-                    &full_b[buf], pol);
-        if (half == 0)
-          tma_load_1d(smem + kOffBmin + tb * kTileMin, a.xm + (size_t)sbg * kTileMin, kTileMin,
-                      &full_b[buf], pol);
-      }
-      // decode: row r, columns [128*half, 128*half + 128) of super-block sbg
-      const uint4 hd = cur[0];
-      uint4 q[4];
+        const int hs = 2 * sb + half, ab = hs % 3;
+        if (hs >= 3) ok = ok && mbar_wait_bounded(&mma_done[ab], ((hs - 3) / 3) & 1);
+        if (!ok) break;
+        uint8_t* A = smem + kOffA + ab * kTileA;
+        const uint4 hd = cur[0];
+        uint4 q[2] = {cur[1 + 2 * half], cur[2 + 2 * half]};
 #pragma unroll
-      for (int i = 0; i < 4; i++) q[i] = cur[1 + 4 * half + i];
-#pragma unroll
-      for (int gl = 0; gl < 4; gl++) {
-        const int g = 4 * half + gl;
-        uint32_t sc;
-        if (g < 4) {
-          sc = byte_of(hd.y, g) & 63u;
-        } else {
-          sc = (byte_of(hd.w, g - 4) & 15u) | ((byte_of(hd.y, g - 4) >> 6) << 4);
-        }
-        const uint32_t sc2 = h2u((float)sc, (float)sc);
-        const uint32_t nb2 = h2u(-1024.0f * (float)sc, -1024.0f * (float)sc);
-        // group g uses pair p = g/2 (bytes 32*(p - 2*half) .. of this half's 64 bytes),
-        // low nibbles for even g, high for odd
-        const int sh = 4 * (g & 1);
-        const uint32_t* wq = reinterpret_cast<const uint32_t*>(q) + 8 * (gl >> 1);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const uint32_t w0 = wq[2 * e] >> sh, w1 = wq[2 * e + 1] >> sh;
-          uint4 v;
-          v.x = hfma2u((w0 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-          v.y = hfma2u(((w0 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-          v.z = hfma2u((w1 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-          v.w = hfma2u(((w1 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-          const int j = gl * 4 + e;  // k-group within the 128-column tile
-          *reinterpret_cast<uint4*>(A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16) = v;
-        }
-      }
-      if (half == 0) {
-        // A_min row: 32*m_g for the 8 groups, then 8 zeros
-        uint32_t mw[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          float m2[2];
-#pragma unroll
-          for (int k = 0; k < 2; k++) {
-            const int g = 2 * i + k;
-            const uint32_t mn = g < 4 ? (byte_of(hd.z, g) & 63u)
-                                      : ((byte_of(hd.w, g - 4) >> 4) | ((byte_of(hd.z, g - 4) >> 6) << 4));
-            m2[k] = 32.0f * (float)mn;
+        for (int gl = 0; gl < 2; gl++) {
+          const int g = 4 * half + 2 * c + gl;
+          uint32_t sc;
+          if (g < 4) {
+            sc = byte_of(hd.y, g) & 63u;
+          } else {
+            sc = (byte_of(hd.w, g - 4) & 15u) | ((byte_of(hd.y, g - 4) >> 6) << 4);
           }
-          mw[i] = h2u(m2[0], m2[1]);
-        }
-        uint8_t* Am = smem + kOffAmin + tb * kTileMin;
-        *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + (r & 7) * 16) =
-            make_uint4(mw[0], mw[1], mw[2], mw[3]);
-        *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async();
-      mbar_arrive(&a_full[buf]);
-      if (tid == 0) {
-        ok = mbar_wait_bounded(&a_full[buf], (hs >> 1) & 1) &&
-             mbar_wait_bounded(&full_b[buf], (hs >> 1) & 1);
-        if (ok && half == 0 && sb >= 2) ok = mbar_wait_bounded(&acc_empty[tb], ((sb - 2) >> 1) & 1);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t d_main = tmem + tb * 256, d_min = d_main + kN;
-          const uint32_t a0 = sbase + kOffA + buf * kTileA, b0 = sbase + kOffB + buf * kTileB;
+          const uint32_t sc2 = h2u((float)sc, (float)sc);
+          const uint32_t nb2 = h2u(-1024.0f * (float)sc, -1024.0f * (float)sc);
+          // groups 2p and 2p+1 share the 32 code bytes of pair p: low, high nibbles
+          const int sh = 4 * gl;
+          const uint32_t* wq = reinterpret_cast<const uint32_t*>(q);
 #pragma unroll
-          for (int t = 0; t < kKC / 16; t++)
-            tc_mma(d_main, smem_desc(a0 + t * 256, 128, kSBO), smem_desc(b0 + t * 256, 128, kSBO),
-                   idesc, (half | t) != 0);
-          if (half == 0)
-            tc_mma(d_min, smem_desc(sbase + kOffAmin + tb * kTileMin, 128, 256),
-                   smem_desc(sbase + kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
-          tc_commit(&mma_done[buf]);
-          if (half == 1) tc_commit(&acc_full[tb]);
-        } else if (a.error_flag) {
-          atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
-        }
-      }
-      // the other producers learn of a failed wait at their next bounded wait
+          for (int e = 0; e < 4; e++) {
+            const uint32_t w0 = wq[2 * e] >> sh, w1 = wq[2 * e + 1] >> sh;
+            uint4 v;
+            v.x = hfma2u((w0 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+            v.y = hfma2u(((w0 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+            v.z = hfma2u((w1 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+            v.w = hfma2u(((w1 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+            const int j = (2 * c + gl) * 4 + e;  // k-group within the 128-column tile
+            *reinterpret_cast<uint4*>(A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16) = v;
           }
+        }
+        if (half == 0 && c == 0) {
+          // A_min row: 32*m_g for the 8 groups, then 8 zeros
+          uint32_t mw[4];
 #pragma unroll
-      for (int i = 0; i < 9; i++) cur[i] = nxt[i];
+          for (int i = 0; i < 4; i++) {
+            float m2[2];
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+              const int g = 2 * i + k;
+              const uint32_t mn =
+                  g < 4 ? (byte_of(hd.z, g) & 63u)
+                        : ((byte_of(hd.w, g - 4) >> 4) | ((byte_of(hd.z, g - 4) >> 6) << 4));
+              m2[k] = 32.0f * (float)mn;
+            }
+            mw[i] = h2u(m2[0], m2[1]);
+          }
+          uint8_t* Am = smem + kOffAmin + (sb & 1) * kTileMin;
+          *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + (r & 7) * 16) =
+              make_uint4(mw[0], mw[1], mw[2], mw[3]);
+          *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + 128 + (r & 7) * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+        mbar_arrive(&a_full[ab]);
+      }
+#pragma unroll
+      for (int i = 0; i < 5; i++) cur[i] = nxt[i];
     }
-  } else {
+  } else if (warp < 12) {
     // ---------------- epilogue: TMEM -> per-item sums ----------------
-    const int r = tid - 128;  // TMEM lane / row
-    const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+    const int r = tid - 256;  // TMEM lane / row
+    const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
     float acc[kItems];
 #pragma unroll
@@ -364,20 +335,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
       const uint32_t hx = *reinterpret_cast<const uint32_t*>(rp + (size_t)(s0 + sb) * 144);
       const float d = f16_bits((uint16_t)(hx & 0xffffu)), dmin = f16_bits((uint16_t)(hx >> 16));
       ok = mbar_wait_bounded(&acc_full[tb], (sb >> 1) & 1);
-      if (!ok) {
-        if (a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
-        break;
-      }
+      if (!ok) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kN / 32; c++) {
+      for (int cc = 0; cc < kN / 32; cc++) {
         float T[32], M[32];
-        tc_ld32(tmem + lane_off + tb * 256 + 32 * c, T);
-        tc_ld32(tmem + lane_off + tb * 256 + kN + 32 * c, M);
+        tc_ld32(tmem + lane_off + tb * 256 + 32 * cc, T);
+        tc_ld32(tmem + lane_off + tb * 256 + kN + 32 * cc, M);
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const int item = 16 * c + i;
-          acc[item] = fmaf(d, T[2 * i] + T[2 * i + 1], fmaf(-dmin, M[2 * i] + M[2 * i + 1], acc[item]));
+          const int item = 16 * cc + i;
+          acc[item] =
+              fmaf(d, T[2 * i] + T[2 * i + 1], fmaf(-dmin, M[2 * i] + M[2 * i + 1], acc[item]));
         }
       }
       tc_fence_before();
@@ -391,6 +360,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
       for (int i = 0; i < kItems; i++)
         if (i < a.batch) pp[(size_t)i * a.rows] = acc[i] * a.xscale[i];
     }
+    if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+  } else if (lane == 0) {
+    // ---------------- issuer: x copies and MMAs ----------------
+    const uint64_t pol = evict_first_policy();
+    constexpr uint32_t idesc = idesc_f16(kRows, kN);
+    // x tile of half step h (and, at even h, the super-block's B_min) into B[h % 3]
+    auto issue_x = [&](int h) {
+      const int sbg = s0 + (h >> 1), bi = h % 3;
+      mbar_expect_tx(&full_b[bi], kTileB + ((h & 1) == 0 ? kTileMin : 0));
+      tma_load_1d(smem + kOffB + bi * kTileB, a.xt + (size_t)(2 * sbg + (h & 1)) * kTileB, kTileB,
+                  &full_b[bi], pol);
+      if ((h & 1) == 0)
+        tma_load_1d(smem + kOffBmin + ((h >> 1) & 1) * kTileMin, a.xm + (size_t)sbg * kTileMin,
+                    kTileMin, &full_b[bi], pol);
+    };
+    for (int h = 0; h < 2 && h < nhs; h++) issue_x(h);
+    for (int hs = 0; hs < nhs && ok; hs++) {
+      const int sb = hs >> 1, half = hs & 1, ab = hs % 3, tb = sb & 1;
+      ok = mbar_wait_bounded(&a_full[ab], (hs / 3) & 1) &&
+           mbar_wait_bounded(&full_b[ab], (hs / 3) & 1);
+      if (ok && half == 0 && sb >= 2) ok = mbar_wait_bounded(&acc_empty[tb], ((sb - 2) >> 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_main = tmem + tb * 256, d_min = d_main + kN;
+      const uint32_t a0 = sbase + kOffA + ab * kTileA, b0 = sbase + kOffB + ab * kTileB;
+#pragma unroll
+      for (int t = 0; t < kKC / 16; t++)
+        tc_mma(d_main, smem_desc(a0 + t * 256, 128, kSBO), smem_desc(b0 + t * 256, 128, kSBO),
+               idesc, (half | t) != 0);
+      if (half == 0)
+        tc_mma(d_min, smem_desc(sbase + kOffAmin + tb * kTileMin, 128, 256),
+               smem_desc(sbase + kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
+      tc_commit(&mma_done[ab]);
+      if (half == 1) tc_commit(&acc_full[tb]);
+      // B[(hs+2) % 3] was last read by half step hs-1
+      if (hs + 2 < nhs) {
+        if (hs >= 1) ok = mbar_wait_bounded(&mma_done[(hs + 2) % 3], ((hs - 1) / 3) & 1);
+        if (!ok) break;
+        issue_x(hs + 2);
+      }
+    }
+    if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
   }
   tc_fence_before();
   __syncthreads();
