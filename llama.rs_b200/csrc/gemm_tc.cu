@@ -61,10 +61,24 @@ constexpr int kSBO = (kKC / 8) * 128;    // 2048
 constexpr int kThreads = 416;  // 8 producer warps (2 per row), 4 epilogue warps, 1 issuer
 constexpr uint32_t kTmemCols = 512;
 
-// smem: A[3] | B[3] | Amin[2] | Bmin[2] | barriers
-constexpr int kOffA = 0, kOffB = 3 * kTileA, kOffAmin = kOffB + 3 * kTileB,
-              kOffBmin = kOffAmin + 2 * kTileMin, kOffBar = kOffBmin + 2 * kTileMin;
-constexpr int kSmem = kOffBar + 128;
+// Per-type pipeline shape.  Q4_K: one A tile (sc*q) per half super-block plus
+// the A_min MMA; three A and three x buffers.  Q6_K: two A tiles per half
+// super-block, (q-32)*(sc & 15) and (q-32)*(sc - (sc & 15)), both exact in
+// f16, accumulated into the same TMEM columns; two A and two x buffers.
+template <int T>
+struct TcShape {
+  static constexpr bool kMins = T == LRS_GGML_Q4_K;
+  static constexpr int kAParts = T == LRS_GGML_Q6_K ? 2 : 1;  // A tiles per half step
+  static constexpr int kAB = T == LRS_GGML_Q6_K ? 2 : 3;      // A buffers
+  static constexpr int kBB = T == LRS_GGML_Q6_K ? 2 : 3;      // x buffers
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kAB * kAParts * kTileA;
+  static constexpr int kOffAmin = kOffB + kBB * kTileB;
+  static constexpr int kOffBmin = kOffAmin + (kMins ? 2 * kTileMin : 0);
+  static constexpr int kOffBar = kOffBmin + (kMins ? 2 * kTileMin : 0);
+  static constexpr int kSmem = kOffBar + 128;
+  static constexpr int kBytes = T == LRS_GGML_Q6_K ? 210 : 144;
+};
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(256)
 }
 
 struct TcArgs {
-  const uint8_t* w;  // Q4_K rows
+  const uint8_t* w;  // block rows
   int rows, rb, cols, batch, kgroups;
   const uint8_t* xt;
   const uint8_t* xm;
@@ -198,13 +212,64 @@ struct TcArgs {
   int* error_flag;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_constant__ TcArgs a) {
+// Four bytes at a 2-byte aligned address (Q6_K blocks are 210 bytes).
+__device__ __forceinline__ uint32_t ldg32_a2(const uint8_t* p) {
+  const uintptr_t ad = reinterpret_cast<uintptr_t>(p);
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(ad & ~uintptr_t(3));
+  uint32_t lo, hi;
+  asm("ld.global.nc.b32 %0, [%1];" : "=r"(lo) : "l"(b));
+  asm("ld.global.nc.b32 %0, [%1];" : "=r"(hi) : "l"(b + 4));
+  return __funnelshift_r(lo, hi, (uint32_t)(ad & 3) * 8);
+}
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Raw bytes one producer thread (c, r) needs from one super-block.
+template <int T>
+struct Raw;
+template <>
+struct Raw<LRS_GGML_Q4_K> {
+  uint4 v[5];  // header, then 32 code bytes of pair c (half 0) and pair 2+c (half 1)
+  __device__ __forceinline__ void load(const uint8_t* u, int c) {
+    v[0] = ldg128(u);
+    v[1] = ldg128(u + 16 + 32 * c);
+    v[2] = ldg128(u + 32 + 32 * c);
+    v[3] = ldg128(u + 80 + 32 * c);
+    v[4] = ldg128(u + 96 + 32 * c);
+  }
+};
+template <>
+struct Raw<LRS_GGML_Q6_K> {
+  uint32_t ql[2][8], qh[2][8], sc[2][2];  // per half: ql bytes of quarters c, c+2; qh; scales
+  __device__ __forceinline__ void load(const uint8_t* u, int c) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        ql[h][i] = ldg32_a2(u + 64 * h + 32 * c + 4 * i);
+        qh[h][i] = ldg32_a2(u + 128 + 32 * h + 4 * i);
+      }
+      sc[h][0] = ldg32_a2(u + 192 + 8 * h);
+      sc[h][1] = ldg32_a2(u + 196 + 8 * h);
+    }
+  }
+};
+
+template <int T>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
+  using S = TcShape<T>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full_b = bars;          // [3] x tile landed
-  uint64_t* a_full = bars + 3;      // [3] the 256 producer threads wrote an A tile
-  uint64_t* mma_done = bars + 6;    // [3] MMAs of a half step finished (A/B buffers free)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
+  uint64_t* full_b = bars;          // [kBB] x tile landed
+  uint64_t* a_full = bars + 3;      // [kAB] the 256 producer threads wrote an A tile
+  uint64_t* mma_done = bars + 6;    // [kAB] MMAs of a half step finished (A, x buffers free)
   uint64_t* acc_full = bars + 9;    // [2] super-block accumulator ready
   uint64_t* acc_empty = bars + 11;  // [2] epilogue finished reading it
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -243,84 +308,106 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
 
   if (warp < 8) {
     // ---------------- producers: decode the A tiles ----------------
-    // thread (c, r): row r, groups 2c and 2c+1 of every half super-block
+    // thread (c, r): row r, 32-column groups 2c, 2c+1 (Q4_K) or quarters c, c+2
+    // (Q6_K) of every half super-block
     const int r = tid & 127, c = tid >> 7;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
-    // this thread's raw bytes of a super-block (header, 32 code bytes per half),
-    // one super-block ahead
-    uint4 cur[5], nxt[5];
-    auto load_sb = [&](int sbg, uint4(&dst)[5]) {
-      const uint8_t* u = rp + (size_t)sbg * 144;
-      dst[0] = ldg128(u);
-      dst[1] = ldg128(u + 16 + 32 * c);
-      dst[2] = ldg128(u + 32 + 32 * c);
-      dst[3] = ldg128(u + 80 + 32 * c);
-      dst[4] = ldg128(u + 96 + 32 * c);
-    };
-    if (nsb > 0) load_sb(s0, cur);
+    Raw<T> cur, nxt;
+    if (nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
     for (int sb = 0; sb < nsb && ok; sb++) {
-      if (sb + 1 < nsb) load_sb(s0 + sb + 1, nxt);
+      if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
 #pragma unroll
       for (int half = 0; half < 2; half++) {
-        const int hs = 2 * sb + half, ab = hs % 3;
-        if (hs >= 3) ok = ok && mbar_wait_bounded(&mma_done[ab], ((hs - 3) / 3) & 1);
+        const int hs = 2 * sb + half, ab = hs % S::kAB;
+        if (hs >= S::kAB) ok = ok && mbar_wait_bounded(&mma_done[ab], ((hs - S::kAB) / S::kAB) & 1);
         if (!ok) break;
-        uint8_t* A = smem + kOffA + ab * kTileA;
-        const uint4 hd = cur[0];
-        uint4 q[2] = {cur[1 + 2 * half], cur[2 + 2 * half]};
+        uint8_t* A = smem + S::kOffA + ab * S::kAParts * kTileA;
+        if constexpr (T == LRS_GGML_Q4_K) {
+          const uint4 hd = cur.v[0];
+          uint4 q[2] = {cur.v[1 + 2 * half], cur.v[2 + 2 * half]};
 #pragma unroll
-        for (int gl = 0; gl < 2; gl++) {
-          const int g = 4 * half + 2 * c + gl;
-          uint32_t sc;
-          if (g < 4) {
-            sc = byte_of(hd.y, g) & 63u;
-          } else {
-            sc = (byte_of(hd.w, g - 4) & 15u) | ((byte_of(hd.y, g - 4) >> 6) << 4);
-          }
-          const uint32_t sc2 = h2u((float)sc, (float)sc);
-          const uint32_t nb2 = h2u(-1024.0f * (float)sc, -1024.0f * (float)sc);
-          // groups 2p and 2p+1 share the 32 code bytes of pair p: low, high nibbles
-          const int sh = 4 * gl;
-          const uint32_t* wq = reinterpret_cast<const uint32_t*>(q);
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const uint32_t w0 = wq[2 * e] >> sh, w1 = wq[2 * e + 1] >> sh;
-            uint4 v;
-            v.x = hfma2u((w0 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-            v.y = hfma2u(((w0 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-            v.z = hfma2u((w1 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-            v.w = hfma2u(((w1 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
-            const int j = (2 * c + gl) * 4 + e;  // k-group within the 128-column tile
-            *reinterpret_cast<uint4*>(A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16) = v;
-          }
-        }
-        if (half == 0 && c == 0) {
-          // A_min row: 32*m_g for the 8 groups, then 8 zeros
-          uint32_t mw[4];
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            float m2[2];
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-              const int g = 2 * i + k;
-              const uint32_t mn =
-                  g < 4 ? (byte_of(hd.z, g) & 63u)
-                        : ((byte_of(hd.w, g - 4) >> 4) | ((byte_of(hd.z, g - 4) >> 6) << 4));
-              m2[k] = 32.0f * (float)mn;
+          for (int gl = 0; gl < 2; gl++) {
+            const int g = 4 * half + 2 * c + gl;
+            uint32_t sc;
+            if (g < 4) {
+              sc = byte_of(hd.y, g) & 63u;
+            } else {
+              sc = (byte_of(hd.w, g - 4) & 15u) | ((byte_of(hd.y, g - 4) >> 6) << 4);
             }
-            mw[i] = h2u(m2[0], m2[1]);
+            const uint32_t sc2 = h2u((float)sc, (float)sc);
+            const uint32_t nb2 = h2u(-1024.0f * (float)sc, -1024.0f * (float)sc);
+            // groups 2p and 2p+1 share the 32 code bytes of pair p: low, high nibbles
+            const int sh = 4 * gl;
+            const uint32_t* wq = reinterpret_cast<const uint32_t*>(q);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const uint32_t w0 = wq[2 * e] >> sh, w1 = wq[2 * e + 1] >> sh;
+              uint4 v;
+              v.x = hfma2u((w0 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+              v.y = hfma2u(((w0 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+              v.z = hfma2u((w1 & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+              v.w = hfma2u(((w1 >> 8) & 0x000F000Fu) | 0x64006400u, sc2, nb2);
+              const int j = (2 * c + gl) * 4 + e;  // k-group within the 128-column tile
+              *reinterpret_cast<uint4*>(A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16) = v;
+            }
           }
-          uint8_t* Am = smem + kOffAmin + (sb & 1) * kTileMin;
-          *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + (r & 7) * 16) =
-              make_uint4(mw[0], mw[1], mw[2], mw[3]);
-          *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + 128 + (r & 7) * 16) =
-              make_uint4(0, 0, 0, 0);
+          if (half == 0 && c == 0) {
+            // A_min row: 32*m_g for the 8 groups, then 8 zeros
+            uint32_t mw[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              float m2[2];
+#pragma unroll
+              for (int k = 0; k < 2; k++) {
+                const int g = 2 * i + k;
+                const uint32_t mn =
+                    g < 4 ? (byte_of(hd.z, g) & 63u)
+                          : ((byte_of(hd.w, g - 4) >> 4) | ((byte_of(hd.z, g - 4) >> 6) << 4));
+                m2[k] = 32.0f * (float)mn;
+              }
+              mw[i] = h2u(m2[0], m2[1]);
+            }
+            uint8_t* Am = smem + S::kOffAmin + (sb & 1) * kTileMin;
+            *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + (r & 7) * 16) =
+                make_uint4(mw[0], mw[1], mw[2], mw[3]);
+            *reinterpret_cast<uint4*>(Am + (r >> 3) * 256 + 128 + (r & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+        } else {
+          // Q6_K half `half`: quarter qq of 32 columns: code = nibble (qq >> 1) of
+          // ql[32 (qq & 1) + l] | 2 bits (2 qq) of qh[l] << 4; scale sc[2 qq + l / 16]
+#pragma unroll
+          for (int k = 0; k < 2; k++) {
+            const int qq = c + 2 * k;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const uint32_t scw = cur.sc[half][(2 * qq + (e >> 1)) >> 2];
+              const int scv = (int)(int8_t)byte_of(scw, (2 * qq + (e >> 1)) & 3);
+              const float sl = (float)(scv & 15), sr = (float)(scv - (scv & 15));
+              const uint32_t sl2 = h2u(sl, sl), sr2 = h2u(sr, sr);
+              uint32_t u[4];
+#pragma unroll
+              for (int m = 0; m < 2; m++) {
+                const uint32_t lw = cur.ql[half][2 * e + m] >> (4 * k);
+                const uint32_t hw = cur.qh[half][2 * e + m] >> (2 * qq);
+                const uint32_t p0 = (lw & 0x000F000Fu) | ((hw & 0x00030003u) << 4);
+                const uint32_t p1 = ((lw >> 8) & 0x000F000Fu) | (((hw >> 8) & 0x00030003u) << 4);
+                u[2 * m] = h2sub(p0 | 0x64006400u, 0x64206420u);      // q - 32
+                u[2 * m + 1] = h2sub(p1 | 0x64006400u, 0x64206420u);
+              }
+              const int j = qq * 4 + e;
+              uint8_t* dst = A + (r >> 3) * kSBO + j * 128 + (r & 7) * 16;
+              *reinterpret_cast<uint4*>(dst) =
+                  make_uint4(h2mul(u[0], sl2), h2mul(u[1], sl2), h2mul(u[2], sl2), h2mul(u[3], sl2));
+              *reinterpret_cast<uint4*>(dst + kTileA) =
+                  make_uint4(h2mul(u[0], sr2), h2mul(u[1], sr2), h2mul(u[2], sr2), h2mul(u[3], sr2));
+            }
+          }
         }
         fence_proxy_async();
         mbar_arrive(&a_full[ab]);
       }
-#pragma unroll
-      for (int i = 0; i < 5; i++) cur[i] = nxt[i];
+      cur = nxt;
     }
   } else if (warp < 12) {
     // ---------------- epilogue: TMEM -> per-item sums ----------------
@@ -332,21 +419,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
     for (int i = 0; i < kItems; i++) acc[i] = 0.0f;
     for (int sb = 0; sb < nsb && ok; sb++) {
       const int tb = sb & 1;
-      const uint32_t hx = *reinterpret_cast<const uint32_t*>(rp + (size_t)(s0 + sb) * 144);
-      const float d = f16_bits((uint16_t)(hx & 0xffffu)), dmin = f16_bits((uint16_t)(hx >> 16));
+      float d, dmin = 0.0f;
+      if constexpr (T == LRS_GGML_Q4_K) {
+        const uint32_t hx = *reinterpret_cast<const uint32_t*>(rp + (size_t)(s0 + sb) * 144);
+        d = f16_bits((uint16_t)(hx & 0xffffu));
+        dmin = f16_bits((uint16_t)(hx >> 16));
+      } else {
+        d = f16_bits(*reinterpret_cast<const uint16_t*>(rp + (size_t)(s0 + sb) * 210 + 208));
+      }
       ok = mbar_wait_bounded(&acc_full[tb], (sb >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < kN / 32; cc++) {
-        float T[32], M[32];
-        tc_ld32(tmem + lane_off + tb * 256 + 32 * cc, T);
-        tc_ld32(tmem + lane_off + tb * 256 + kN + 32 * cc, M);
+        float Tv[32];
+        tc_ld32(tmem + lane_off + tb * 256 + 32 * cc, Tv);
+        if constexpr (S::kMins) {
+          float M[32];
+          tc_ld32(tmem + lane_off + tb * 256 + kN + 32 * cc, M);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int item = 16 * cc + i;
-          acc[item] =
-              fmaf(d, T[2 * i] + T[2 * i + 1], fmaf(-dmin, M[2 * i] + M[2 * i + 1], acc[item]));
+          for (int i = 0; i < 16; i++) {
+            const int item = 16 * cc + i;
+            acc[item] = fmaf(d, Tv[2 * i] + Tv[2 * i + 1],
+                             fmaf(-dmin, M[2 * i] + M[2 * i + 1], acc[item]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const int item = 16 * cc + i;
+            acc[item] = fmaf(d, Tv[2 * i] + Tv[2 * i + 1], acc[item]);
+          }
         }
       }
       tc_fence_before();
@@ -365,40 +467,45 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
     // ---------------- issuer: x copies and MMAs ----------------
     const uint64_t pol = evict_first_policy();
     constexpr uint32_t idesc = idesc_f16(kRows, kN);
-    // x tile of half step h (and, at even h, the super-block's B_min) into B[h % 3]
+    // x tile of half step h (and, at even h, the super-block's B_min) into B[h % kBB]
     auto issue_x = [&](int h) {
-      const int sbg = s0 + (h >> 1), bi = h % 3;
-      mbar_expect_tx(&full_b[bi], kTileB + ((h & 1) == 0 ? kTileMin : 0));
-      tma_load_1d(smem + kOffB + bi * kTileB, a.xt + (size_t)(2 * sbg + (h & 1)) * kTileB, kTileB,
-                  &full_b[bi], pol);
-      if ((h & 1) == 0)
-        tma_load_1d(smem + kOffBmin + ((h >> 1) & 1) * kTileMin, a.xm + (size_t)sbg * kTileMin,
+      const int sbg = s0 + (h >> 1), bi = h % S::kBB;
+      const bool mins = S::kMins && (h & 1) == 0;
+      mbar_expect_tx(&full_b[bi], kTileB + (mins ? kTileMin : 0));
+      tma_load_1d(smem + S::kOffB + bi * kTileB, a.xt + (size_t)(2 * sbg + (h & 1)) * kTileB,
+                  kTileB, &full_b[bi], pol);
+      if (mins)
+        tma_load_1d(smem + S::kOffBmin + ((h >> 1) & 1) * kTileMin, a.xm + (size_t)sbg * kTileMin,
                     kTileMin, &full_b[bi], pol);
     };
-    for (int h = 0; h < 2 && h < nhs; h++) issue_x(h);
+    for (int h = 0; h < S::kBB - 1 && h < nhs; h++) issue_x(h);
     for (int hs = 0; hs < nhs && ok; hs++) {
-      const int sb = hs >> 1, half = hs & 1, ab = hs % 3, tb = sb & 1;
-      ok = mbar_wait_bounded(&a_full[ab], (hs / 3) & 1) &&
-           mbar_wait_bounded(&full_b[ab], (hs / 3) & 1);
+      const int sb = hs >> 1, half = hs & 1, ab = hs % S::kAB, bb = hs % S::kBB, tb = sb & 1;
+      ok = mbar_wait_bounded(&a_full[ab], (hs / S::kAB) & 1) &&
+           mbar_wait_bounded(&full_b[bb], (hs / S::kBB) & 1);
       if (ok && half == 0 && sb >= 2) ok = mbar_wait_bounded(&acc_empty[tb], ((sb - 2) >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
       const uint32_t d_main = tmem + tb * 256, d_min = d_main + kN;
-      const uint32_t a0 = sbase + kOffA + ab * kTileA, b0 = sbase + kOffB + ab * kTileB;
+      const uint32_t a0 = sbase + S::kOffA + ab * S::kAParts * kTileA,
+                     b0 = sbase + S::kOffB + bb * kTileB;
 #pragma unroll
       for (int t = 0; t < kKC / 16; t++)
-        tc_mma(d_main, smem_desc(a0 + t * 256, 128, kSBO), smem_desc(b0 + t * 256, 128, kSBO),
-               idesc, (half | t) != 0);
-      if (half == 0)
-        tc_mma(d_min, smem_desc(sbase + kOffAmin + tb * kTileMin, 128, 256),
-               smem_desc(sbase + kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
+#pragma unroll
+        for (int part = 0; part < S::kAParts; part++)
+          tc_mma(d_main, smem_desc(a0 + part * kTileA + t * 256, 128, kSBO),
+                 smem_desc(b0 + t * 256, 128, kSBO), idesc, (half | t | part) != 0);
+      if (S::kMins && half == 0)
+        tc_mma(d_min, smem_desc(sbase + S::kOffAmin + tb * kTileMin, 128, 256),
+               smem_desc(sbase + S::kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
       tc_commit(&mma_done[ab]);
       if (half == 1) tc_commit(&acc_full[tb]);
-      // B[(hs+2) % 3] was last read by half step hs-1
-      if (hs + 2 < nhs) {
-        if (hs >= 1) ok = mbar_wait_bounded(&mma_done[(hs + 2) % 3], ((hs - 1) / 3) & 1);
+      // B[(hs + kBB - 1) % kBB] was last read by half step hs - 1
+      const int hn = hs + S::kBB - 1;
+      if (hn < nhs) {
+        if (hs >= 1) ok = mbar_wait_bounded(&mma_done[(hs - 1) % S::kAB], ((hs - 1) / S::kAB) & 1);
         if (!ok) break;
-        issue_x(hs + 2);
+        issue_x(hn);
       }
     }
     if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
@@ -418,7 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4k_kernel(const __grid_c
 bool gemm_tc_supported(const GemvParams& p) {
   if (p.batch <= 32 || p.batch > kItems || p.cols % 256 || p.norm_w) return false;
   for (int i = 0; i < p.nseg; i++)
-    if (p.seg[i].type != LRS_GGML_Q4_K) return false;
+    if (p.seg[i].type != LRS_GGML_Q4_K && p.seg[i].type != LRS_GGML_Q6_K) return false;
+  for (int i = 1; i < p.nseg; i++)
+    if (p.seg[i].type != p.seg[0].type) return false;
   return true;
 }
 
@@ -444,8 +553,13 @@ size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms) {
 cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_q4k_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<LRS_GGML_Q4_K>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TcShape<LRS_GGML_Q4_K>::kSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_tc_kernel<LRS_GGML_Q6_K>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               TcShape<LRS_GGML_Q6_K>::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -480,7 +594,13 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       a.part = cur;
       a.error_flag = p.error_flag;
       cur += (size_t)kgroups * B * a.rows;
-      gemm_tc_q4k_kernel<<<dim3((a.rows + kRows - 1) / kRows, kgroups), kThreads, kSmem, st>>>(a);
+      const dim3 grid((a.rows + kRows - 1) / kRows, kgroups);
+      if (p.seg[i].type == LRS_GGML_Q6_K)
+        gemm_tc_kernel<LRS_GGML_Q6_K>
+            <<<grid, kThreads, TcShape<LRS_GGML_Q6_K>::kSmem, st>>>(a);
+      else
+        gemm_tc_kernel<LRS_GGML_Q4_K>
+            <<<grid, kThreads, TcShape<LRS_GGML_Q4_K>::kSmem, st>>>(a);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
   }

@@ -725,11 +725,42 @@ cudaError_t launch_cfg(const void* kernel, size_t smem, int grid, int threads,
 
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
   const bool pair = p.epi == EPI_SWIGLU;
-  // LRS_NO_TCGEN05=1 keeps Q4_K batches on the mma.sync kernel (comparison runs)
+  // LRS_NO_TCGEN05=1 keeps K-quant batches on the mma.sync kernel (comparison runs)
   static const bool tc_off = getenv("LRS_NO_TCGEN05") != nullptr;
-  if (!tc_off && p.scratch && gemm_tc_supported(p) &&
-      p.scratch_bytes >= gemm_tc_scratch_bytes(p, num_sms))
-    return gemm_tc_launch(p, p.scratch, num_sms, stream);
+  if (!tc_off && p.scratch && p.batch > 32) {
+    if (gemm_tc_supported(p)) {
+      if (p.scratch_bytes >= gemm_tc_scratch_bytes(p, num_sms))
+        return gemm_tc_launch(p, p.scratch, num_sms, stream);
+    } else if (p.nseg > 1 && !p.fast) {
+      // mixed types (q/k/v): each run of same-type segments on its own path
+      bool any = false;
+      for (int i = 0; i < p.nseg; i++) {
+        GemvParams q = p;
+        q.nseg = 1;
+        q.seg[0] = p.seg[i];
+        any = any || gemm_tc_supported(q);
+      }
+      if (any) {
+        int i = 0;
+        while (i < p.nseg) {
+          int j = i + 1;
+          while (j < p.nseg && p.seg[j].type == p.seg[i].type) j++;
+          GemvParams q = p;
+          q.nseg = j - i;
+          const int t0 = p.seg[i].tile0;
+          for (int k = 0; k < q.nseg; k++) {
+            q.seg[k] = p.seg[i + k];
+            q.seg[k].tile0 -= t0;
+          }
+          q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
+          cudaError_t e = gemv_launch(q, stream, num_sms, pdl);
+          if (e != cudaSuccess) return e;
+          i = j;
+        }
+        return cudaSuccess;
+      }
+    }
+  }
   if (p.batch >= 2 && p.scratch && gemm_supported(p) &&
       p.scratch_bytes >= gemm_scratch_bytes(p.batch, p.cols, num_sms))
     return gemm_launch(p, p.scratch, num_sms, stream);

@@ -132,10 +132,12 @@ def test_sweep_shapes_every_row(lrs, orc, backend, qt, shape):
 
 @pytest.mark.parametrize("shape", [(1000, 512), (300, 3584), (4864, 896 * 2)], ids=str)
 @pytest.mark.parametrize("batch", [33, 64])
-def test_tcgen05_q4k_batches(lrs, orc, backend, shape, batch):
-    """Q4_K batches of 33..64 run on the tcgen05 kernel (TMEM accumulators)."""
+@pytest.mark.parametrize("qt", ["Q4_K", "Q6_K"])
+def test_tcgen05_kquant_batches(lrs, orc, backend, qt, shape, batch):
+    """Q4_K / Q6_K batches of 33..64 run on the tcgen05 kernel (TMEM accumulators)."""
     rows, cols = shape
-    t = _matrix(lrs, "Q4_K", rows, cols, 21)
+    t = _matrix(lrs, qt, rows, cols, 21)
+    assert t.quant_type == lrs.QuantType[qt]
     rng = np.random.default_rng(3)
     x = rng.standard_normal((batch, cols)).astype(np.float32)
     x[1] *= 1e-3  # per-item scales differ by orders of magnitude
