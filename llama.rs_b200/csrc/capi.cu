@@ -504,7 +504,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
                       mat_of(L.v, m->v, kvw, L.vb)};
     if ((rc = gemv_plan(&p, qkv, 3, EPI_STORE, B))) return rc;
     p.error_flag = m->be->d_err;
-    if (B == 1) {
+    if (B == 1 || gemm_supported(p)) {  // the norm is fused into the x preparation
       p.x = m->residual;
       p.norm_w = L.in_norm;
       p.norm_eps = c.rms_norm_eps;
@@ -540,7 +540,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
     if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B))) return rc;
     p.error_flag = m->be->d_err;
-    if (B == 1) {
+    if (B == 1 || gemm_supported(p)) {
       p.x = m->residual;
       p.norm_w = L.post_norm;
       p.norm_eps = c.rms_norm_eps;
@@ -569,7 +569,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   p.error_flag = m->be->d_err;
   p.argmax_keys = m->keys + (lm_item >= 0 ? lm_item : 0);
   p.argmax_base = m->vocab0;
-  if (nb == 1) {
+  if (nb == 1 || gemm_supported(p)) {
     p.x = xin;
     p.norm_w = m->final_norm;
     p.norm_eps = c.rms_norm_eps;

@@ -131,14 +131,28 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
 // xq: [groups][tiles][1024 B]; xs: [groups][tiles][4] float2; xscale: [tiles * 8].
 __global__ void __launch_bounds__(256)
     xsplit_kernel(const float* x, int x_ld, int cols, int batch, int tiles, uint8_t* xq,
-                  float* xs, float* xscale) {
+                  float* xs, float* xscale, const float* norm_w, float norm_eps) {
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = x + (size_t)b * x_ld;
   __shared__ float red[8];
+  // fused RMSNorm (RMSNorm::forward, src/model.rs:65-73): x * (inv * w)
+  float inv_rms = 1.0f;
+  if (norm_w && b < batch) {
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += 256) ss = fmaf(xr[c], xr[c], ss);
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < 8; k++) tot += red[k];
+    inv_rms = 1.0f / sqrtf(tot / (float)cols + norm_eps);
+    __syncthreads();
+  }
+  auto xval = [&](int c) { return norm_w ? xr[c] * (inv_rms * norm_w[c]) : xr[c]; };
   float mx = 0.0f;
   if (b < batch)
-    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xr[c]));
+    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xval(c)));
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red[warp] = mx;
   __syncthreads();
@@ -151,7 +165,7 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) xscale[b] = ldexpf(1.0f, e - 14);
   const int j = b >> 3, gid = b & 7;
   for (int g = warp; g * 32 < cols; g += 8) {
-    const float v = b < batch ? xr[g * 32 + lane] * inv : 0.0f;
+    const float v = b < batch ? xval(g * 32 + lane) * inv : 0.0f;
     const __half h = __float2half_rn(v);
     const __half l = __float2half_rn(v - __half2float(h));
     float sum = v;
@@ -669,7 +683,7 @@ int layout_tiles(int batch) {
 }  // namespace
 
 bool gemm_supported(const GemvParams& p) {
-  if (p.batch < 2 || p.cols % 32 || p.norm_w) return false;
+  if (p.batch < 2 || p.cols % 32) return false;
   for (int i = 0; i < p.nseg; i++)
     if (!quantized(p.seg[i].type)) return false;
   return true;
@@ -718,7 +732,8 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
   float* xscale = reinterpret_cast<float*>(
       align(reinterpret_cast<uint8_t*>(xs) + (size_t)(cols / 32) * tiles * kSRec));
   float* part = reinterpret_cast<float*>(align(xscale + tiles * 8));
-  xsplit_kernel<<<tiles * 8, 256, 0, st>>>(p.x, p.x_ld, cols, Ball, tiles, xq, xs, xscale);
+  xsplit_kernel<<<tiles * 8, 256, 0, st>>>(p.x, p.x_ld, cols, Ball, tiles, xq, xs, xscale,
+                                            p.norm_w, p.norm_eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows_cta = pair ? Shape<true>::kRows : Shape<false>::kRows;

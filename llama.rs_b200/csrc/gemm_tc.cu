@@ -160,14 +160,28 @@ __device__ __forceinline__ int tile_off(int n, int k, int sbo) {
 // xscale: [64] item scales.
 __global__ void __launch_bounds__(256)
     xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, uint8_t* xt, uint8_t* xm,
-                     float* xscale) {
+                     float* xscale, const float* norm_w, float norm_eps) {
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = x + (size_t)b * x_ld;
   __shared__ float red[8];
+  // fused RMSNorm (RMSNorm::forward, src/model.rs:65-73): x * (inv * w)
+  float inv_rms = 1.0f;
+  if (norm_w && b < batch) {
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += 256) ss = fmaf(xr[c], xr[c], ss);
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < 8; k++) tot += red[k];
+    inv_rms = 1.0f / sqrtf(tot / (float)cols + norm_eps);
+    __syncthreads();
+  }
+  auto xval = [&](int c) { return norm_w ? xr[c] * (inv_rms * norm_w[c]) : xr[c]; };
   float mx = 0.0f;
   if (b < batch)
-    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xr[c]));
+    for (int c = threadIdx.x; c < cols; c += 256) mx = fmaxf(mx, fabsf(xval(c)));
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red[warp] = mx;
   __syncthreads();
@@ -179,7 +193,7 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) xscale[b] = ldexpf(1.0f, e - 14);
   for (int g = warp; g * 32 < cols; g += 8) {
     const int k = g * 32 + lane;
-    const float v = b < batch ? xr[k] * inv : 0.0f;
+    const float v = b < batch ? xval(k) * inv : 0.0f;
     const __half h = __float2half_rn(v);
     const __half l = __float2half_rn(v - __half2float(h));
     uint8_t* tile = xt + (size_t)(k / kKC) * kTileB;
@@ -316,6 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
     for (int sb = 0; sb < nsb && ok; sb++) {
       if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
+      if (sb + 2 < nsb) {  // two super-blocks ahead into L2
+        const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
+        if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
+      }
 #pragma unroll
       for (int half = 0; half < 2; half++) {
         const int hs = 2 * sb + half, ab = hs % S::kAB;
@@ -523,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 }  // namespace
 
 bool gemm_tc_supported(const GemvParams& p) {
-  if (p.batch <= 32 || p.batch > kItems || p.cols % 256 || p.norm_w) return false;
+  if (p.batch <= 32 || p.batch > kItems || p.cols % 256) return false;
   for (int i = 0; i < p.nseg; i++)
     if (p.seg[i].type != LRS_GGML_Q4_K && p.seg[i].type != LRS_GGML_Q6_K) return false;
   for (int i = 1; i < p.nseg; i++)
@@ -572,7 +590,8 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
   uint8_t* xm = xt + (size_t)(cols / kKC) * kTileB;
   float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * kTileMin);
   float* part = xscale + kItems;
-  xsplit_tc_kernel<<<kItems, 256, 0, st>>>(p.x, p.x_ld, cols, B, xt, xm, xscale);
+  xsplit_tc_kernel<<<kItems, 256, 0, st>>>(p.x, p.x_ld, cols, B, xt, xm, xscale, p.norm_w,
+                                            p.norm_eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int kgroups = tc_kgroups(p, sms);
