@@ -379,7 +379,7 @@ def run_ours(args, wl):
                     "d2h_bytes_per_step": 4 * B + 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None,
-                         "kernel": ("gemm_mma_kernel: batched quantized matmul (x split, matmul, "
+                         "kernel": ("gemm_tc_kernel (tcgen05, Q4_K/Q6_K) + gemm_mma_kernel (Q8_0): batched quantized matmul (x split, matmul, "
                                     "K-split epilogue) of every projection and the LM head"
                                     if B > 1 else "gemv5_kernel: batch-1 quantized GEMV"),
                          "bytes_per_launch": wbytes / gemv_n, "ms_per_launch": gemv_ms / gemv_n,

@@ -50,12 +50,14 @@
 namespace lrs {
 namespace {
 
-constexpr int kItems = 64;
-constexpr int kN = 2 * kItems;       // B rows: (item, hi/lo)
+constexpr int kMaxItems = 64;
 constexpr int kRows = 128;           // weight rows per CTA = TMEM lanes
 constexpr int kKC = 128;             // columns per A/B tile (half a super-block)
 constexpr int kTileA = kRows * kKC * 2;  // 32 KB
-constexpr int kTileB = kN * kKC * 2;     // 32 KB
+// x tile of NI items: N = 2 NI rows (item, hi/lo) x 128 columns
+__host__ __device__ constexpr int tile_b(int ni) { return 2 * ni * kKC * 2; }
+// B_min tile: N rows x 16 positions
+__host__ __device__ constexpr int tile_bmin(int ni) { return 2 * ni * 16 * 2; }
 constexpr int kTileMin = 128 * 16 * 2;   // 4 KB (A_min or B_min)
 constexpr int kSBO = (kKC / 8) * 128;    // 2048
 constexpr int kThreads = 416;  // 8 producer warps (2 per row), 4 epilogue warps, 1 issuer
@@ -65,8 +67,11 @@ constexpr uint32_t kTmemCols = 512;
 // the A_min MMA; three A and three x buffers.  Q6_K: two A tiles per half
 // super-block, (q-32)*(sc & 15) and (q-32)*(sc - (sc & 15)), both exact in
 // f16, accumulated into the same TMEM columns; two A and two x buffers.
-template <int T>
+template <int T, int NI>
 struct TcShape {
+  static constexpr int kN = 2 * NI;
+  static constexpr int kTileB = tile_b(NI);
+  static constexpr int kTileBmin = tile_bmin(NI);
   static constexpr bool kMins = T == LRS_GGML_Q4_K;
   static constexpr int kAParts = T == LRS_GGML_Q6_K ? 2 : 1;  // A tiles per half step
   static constexpr int kAB = T == LRS_GGML_Q6_K ? 2 : 3;      // A buffers
@@ -75,7 +80,7 @@ struct TcShape {
   static constexpr int kOffB = kOffA + kAB * kAParts * kTileA;
   static constexpr int kOffAmin = kOffB + kBB * kTileB;
   static constexpr int kOffBmin = kOffAmin + (kMins ? 2 * kTileMin : 0);
-  static constexpr int kOffBar = kOffBmin + (kMins ? 2 * kTileMin : 0);
+  static constexpr int kOffBar = kOffBmin + (kMins ? 2 * kTileBmin : 0);
   static constexpr int kSmem = kOffBar + 128;
   static constexpr int kBytes = T == LRS_GGML_Q6_K ? 210 : 144;
 };
@@ -159,8 +164,8 @@ __device__ __forceinline__ int tile_off(int n, int k, int sbo) {
 // xt: [cols/128][N x 128] f16 tiles; xm: [cols/256][N x 16] group-sum tiles;
 // xscale: [64] item scales.
 __global__ void __launch_bounds__(256)
-    xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, uint8_t* xt, uint8_t* xm,
-                     float* xscale, const float* norm_w, float norm_eps) {
+    xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, int ni, uint8_t* xt,
+                     uint8_t* xm, float* xscale, const float* norm_w, float norm_eps) {
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = x + (size_t)b * x_ld;
@@ -196,13 +201,13 @@ __global__ void __launch_bounds__(256)
     const float v = b < batch ? xval(k) * inv : 0.0f;
     const __half h = __float2half_rn(v);
     const __half l = __float2half_rn(v - __half2float(h));
-    uint8_t* tile = xt + (size_t)(k / kKC) * kTileB;
+    uint8_t* tile = xt + (size_t)(k / kKC) * tile_b(ni);
     *reinterpret_cast<__half*>(tile + tile_off(2 * b, k % kKC, kSBO)) = h;
     *reinterpret_cast<__half*>(tile + tile_off(2 * b + 1, k % kKC, kSBO)) = l;
     float sum = v;
     for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     // group sums / 32 (exact), hi/lo, at position g % 8 of the super-block's B_min
-    uint8_t* mt = xm + (size_t)(g / 8) * kTileMin;
+    uint8_t* mt = xm + (size_t)(g / 8) * tile_bmin(ni);
     if (lane < 2) {
       const float s = sum * (1.0f / 32.0f);
       const __half sh = __float2half_rn(s);
@@ -275,9 +280,10 @@ struct Raw<LRS_GGML_Q6_K> {
   }
 };
 
-template <int T>
+template <int T, int NI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
-  using S = TcShape<T>;
+  using S = TcShape<T, NI>;
+  constexpr int kN = S::kN, kTileB = S::kTileB;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
@@ -432,9 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int r = tid - 256;  // TMEM lane / row
     const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
-    float acc[kItems];
+    float acc[NI];
 #pragma unroll
-    for (int i = 0; i < kItems; i++) acc[i] = 0.0f;
+    for (int i = 0; i < NI; i++) acc[i] = 0.0f;
     for (int sb = 0; sb < nsb && ok; sb++) {
       const int tb = sb & 1;
       float d, dmin = 0.0f;
@@ -477,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (ok && row < a.rows) {
       float* pp = a.part + (size_t)blockIdx.y * a.batch * a.rows + row;
 #pragma unroll
-      for (int i = 0; i < kItems; i++)
+      for (int i = 0; i < NI; i++)
         if (i < a.batch) pp[(size_t)i * a.rows] = acc[i] * a.xscale[i];
     }
     if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
@@ -489,12 +495,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     auto issue_x = [&](int h) {
       const int sbg = s0 + (h >> 1), bi = h % S::kBB;
       const bool mins = S::kMins && (h & 1) == 0;
-      mbar_expect_tx(&full_b[bi], kTileB + (mins ? kTileMin : 0));
+      mbar_expect_tx(&full_b[bi], kTileB + (mins ? S::kTileBmin : 0));
       tma_load_1d(smem + S::kOffB + bi * kTileB, a.xt + (size_t)(2 * sbg + (h & 1)) * kTileB,
                   kTileB, &full_b[bi], pol);
       if (mins)
-        tma_load_1d(smem + S::kOffBmin + ((h >> 1) & 1) * kTileMin, a.xm + (size_t)sbg * kTileMin,
-                    kTileMin, &full_b[bi], pol);
+        tma_load_1d(smem + S::kOffBmin + ((h >> 1) & 1) * S::kTileBmin,
+                    a.xm + (size_t)sbg * S::kTileBmin, S::kTileBmin, &full_b[bi], pol);
     };
     for (int h = 0; h < S::kBB - 1 && h < nhs; h++) issue_x(h);
     for (int hs = 0; hs < nhs && ok; hs++) {
@@ -515,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                  smem_desc(b0 + t * 256, 128, kSBO), idesc, (half | t | part) != 0);
       if (S::kMins && half == 0)
         tc_mma(d_min, smem_desc(sbase + S::kOffAmin + tb * kTileMin, 128, 256),
-               smem_desc(sbase + S::kOffBmin + tb * kTileMin, 128, 256), idesc, 0);
+               smem_desc(sbase + S::kOffBmin + tb * S::kTileBmin, 128, 256), idesc, 0);
       tc_commit(&mma_done[ab]);
       if (half == 1) tc_commit(&acc_full[tb]);
       // B[(hs + kBB - 1) % kBB] was last read by half step hs - 1
@@ -541,57 +547,69 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 }  // namespace
 
 bool gemm_tc_supported(const GemvParams& p) {
-  if (p.batch <= 32 || p.batch > kItems || p.cols % 256) return false;
-  for (int i = 0; i < p.nseg; i++)
+  // measured: Q4_K gains from 4 items up, Q6_K (two MMAs per K step) from 17
+  if (p.batch < 4 || p.batch > kMaxItems || p.cols % 256) return false;
+  for (int i = 0; i < p.nseg; i++) {
+    if (p.seg[i].type == LRS_GGML_Q6_K && p.batch <= 16) return false;
     if (p.seg[i].type != LRS_GGML_Q4_K && p.seg[i].type != LRS_GGML_Q6_K) return false;
+  }
   for (int i = 1; i < p.nseg; i++)
     if (p.seg[i].type != p.seg[0].type) return false;
   return true;
 }
 
 namespace {
+int tc_items(int batch) { return batch <= 16 ? 16 : batch <= 32 ? 32 : 64; }
 int tc_kgroups(const GemvParams& p, int sms) {
   int ctas = 0;
   for (int i = 0; i < p.nseg; i++) ctas += (p.seg[i].rows + kRows - 1) / kRows;
   const int nsb = p.cols / 256;
   return ctas >= sms ? 1 : std::max(1, std::min(nsb, sms / ctas));
 }
+
+template <int T, int NI>
+cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TcShape<T, NI>::kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  gemm_tc_kernel<T, NI><<<grid, kThreads, TcShape<T, NI>::kSmem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int NI>
+cudaError_t launch_tc_type(int type, const TcArgs& a, dim3 grid, cudaStream_t st) {
+  return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI>(a, grid, st)
+                               : launch_tc<LRS_GGML_Q4_K, NI>(a, grid, st);
+}
 }  // namespace
 
 size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms) {
-  const int kg = tc_kgroups(p, sms);
+  const int kg = tc_kgroups(p, sms), ni = tc_items(p.batch);
   size_t rows = 0;
   for (int i = 0; i < p.nseg; i++) rows += p.seg[i].rows;
-  return (size_t)(p.cols / kKC) * kTileB + (size_t)(p.cols / 256) * kTileMin + kItems * 4 +
-         (size_t)kg * p.batch * rows * 4 * (p.epi == EPI_SWIGLU ? 2 : 1) + 1024;
+  return (size_t)(p.cols / kKC) * tile_b(ni) + (size_t)(p.cols / 256) * tile_bmin(ni) +
+         kMaxItems * 4 + (size_t)kg * p.batch * rows * 4 * (p.epi == EPI_SWIGLU ? 2 : 1) + 1024;
 }
 
 // Partial sums for every segment (and the pair's second matrix), then the
 // fixed-order epilogue shared with gemm_mma.cu.
 cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<LRS_GGML_Q4_K>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcShape<LRS_GGML_Q4_K>::kSmem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_tc_kernel<LRS_GGML_Q6_K>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               TcShape<LRS_GGML_Q6_K>::kSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  const int cols = p.cols, B = p.batch;
+  const int cols = p.cols, B = p.batch, ni = tc_items(B);
   const bool pair = p.epi == EPI_SWIGLU;
   auto align = [](void* q) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255));
   };
   uint8_t* xt = align(scratch);
-  uint8_t* xm = xt + (size_t)(cols / kKC) * kTileB;
-  float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * kTileMin);
-  float* part = xscale + kItems;
-  xsplit_tc_kernel<<<kItems, 256, 0, st>>>(p.x, p.x_ld, cols, B, xt, xm, xscale, p.norm_w,
-                                            p.norm_eps);
+  uint8_t* xm = xt + (size_t)(cols / kKC) * tile_b(ni);
+  float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * tile_bmin(ni));
+  float* part = xscale + kMaxItems;
+  xsplit_tc_kernel<<<ni, 256, 0, st>>>(p.x, p.x_ld, cols, B, ni, xt, xm, xscale, p.norm_w,
+                                       p.norm_eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int kgroups = tc_kgroups(p, sms);
@@ -614,13 +632,10 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       a.error_flag = p.error_flag;
       cur += (size_t)kgroups * B * a.rows;
       const dim3 grid((a.rows + kRows - 1) / kRows, kgroups);
-      if (p.seg[i].type == LRS_GGML_Q6_K)
-        gemm_tc_kernel<LRS_GGML_Q6_K>
-            <<<grid, kThreads, TcShape<LRS_GGML_Q6_K>::kSmem, st>>>(a);
-      else
-        gemm_tc_kernel<LRS_GGML_Q4_K>
-            <<<grid, kThreads, TcShape<LRS_GGML_Q4_K>::kSmem, st>>>(a);
-      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+      e = ni == 16 ? launch_tc_type<16>(p.seg[i].type, a, grid, st)
+                   : ni == 32 ? launch_tc_type<32>(p.seg[i].type, a, grid, st)
+                              : launch_tc_type<64>(p.seg[i].type, a, grid, st);
+      if (e != cudaSuccess) return e;
     }
   }
   return gemm_partials_epilogue(p, parts, kgroups, st);

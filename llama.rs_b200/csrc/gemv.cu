@@ -727,7 +727,7 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
   const bool pair = p.epi == EPI_SWIGLU;
   // LRS_NO_TCGEN05=1 keeps K-quant batches on the mma.sync kernel (comparison runs)
   static const bool tc_off = getenv("LRS_NO_TCGEN05") != nullptr;
-  if (!tc_off && p.scratch && p.batch > 32) {
+  if (!tc_off && p.scratch && p.batch >= 4) {
     if (gemm_tc_supported(p)) {
       if (p.scratch_bytes >= gemm_tc_scratch_bytes(p, num_sms))
         return gemm_tc_launch(p, p.scratch, num_sms, stream);

@@ -131,10 +131,10 @@ def test_sweep_shapes_every_row(lrs, orc, backend, qt, shape):
 
 
 @pytest.mark.parametrize("shape", [(1000, 512), (300, 3584), (4864, 896 * 2)], ids=str)
-@pytest.mark.parametrize("batch", [33, 64])
-@pytest.mark.parametrize("qt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("batch", [5, 17, 33, 64])
+@pytest.mark.parametrize("qt", ["Q4_K", "Q6_K"])  # Q6_K from 17 items
 def test_tcgen05_kquant_batches(lrs, orc, backend, qt, shape, batch):
-    """Q4_K / Q6_K batches of 33..64 run on the tcgen05 kernel (TMEM accumulators)."""
+    """Q4_K / Q6_K batches of 4..64 run on the tcgen05 kernel (TMEM accumulators)."""
     rows, cols = shape
     t = _matrix(lrs, qt, rows, cols, 21)
     assert t.quant_type == lrs.QuantType[qt]
