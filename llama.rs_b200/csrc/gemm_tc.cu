@@ -153,12 +153,6 @@ __device__ __forceinline__ uint4 ldg128(const uint8_t* p) {
 }
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xffu; }
 
-// Byte offset of element (row n, position k) of a K-major no-swizzle tile with
-// 16 k-groups per row group; the column order inside 4 columns is (0, 2, 1, 3).
-__device__ __forceinline__ int tile_off(int n, int k, int sbo) {
-  const int c4 = k & 3, pos = (k & ~3) | (c4 == 1 ? 2 : c4 == 2 ? 1 : c4);
-  return (n >> 3) * sbo + (pos >> 3) * 128 + (n & 7) * 16 + (pos & 7) * 2;
-}
 
 // ---- x preparation: one CTA per item slot (64, zero-padded) -------------------
 // xt: [cols/128][N x 128] f16 tiles; xm: [cols/256][N x 16] group-sum tiles;
@@ -195,28 +189,61 @@ __global__ void __launch_bounds__(256)
   int e = 14;
   if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);
   const float inv = ldexpf(1.0f, 14 - e);
-  if (threadIdx.x == 0) xscale[b] = ldexpf(1.0f, e - 14);
-  for (int g = warp; g * 32 < cols; g += 8) {
-    const int k = g * 32 + lane;
-    const float v = b < batch ? xval(k) * inv : 0.0f;
-    const __half h = __float2half_rn(v);
-    const __half l = __float2half_rn(v - __half2float(h));
-    uint8_t* tile = xt + (size_t)(k / kKC) * tile_b(ni);
-    *reinterpret_cast<__half*>(tile + tile_off(2 * b, k % kKC, kSBO)) = h;
-    *reinterpret_cast<__half*>(tile + tile_off(2 * b + 1, k % kKC, kSBO)) = l;
-    float sum = v;
-    for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    // group sums / 32 (exact), hi/lo, at position g % 8 of the super-block's B_min
-    uint8_t* mt = xm + (size_t)(g / 8) * tile_bmin(ni);
-    if (lane < 2) {
-      const float s = sum * (1.0f / 32.0f);
-      const __half sh = __float2half_rn(s);
-      const __half val = lane == 0 ? sh : __float2half_rn(s - __half2float(sh));
-      const int n = 2 * b + lane, pos = g % 8;
-      *reinterpret_cast<__half*>(mt + (n >> 3) * 256 + (n & 7) * 16 + pos * 2) = val;
-      // positions 8..15 (second core matrix) stay zero
-      if ((g % 8) == 0)
-        *reinterpret_cast<uint4*>(mt + (n >> 3) * 256 + 128 + (n & 7) * 16) = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0 && blockIdx.y == 0) xscale[b] = ldexpf(1.0f, e - 14);
+  // one warp per super-block (256 columns), 8 columns per lane: f16 hi / lo in
+  // tile order (one 16-byte store each), group sums / 32 into B_min
+  for (int sb = blockIdx.y * 8 + warp; sb * 256 < cols; sb += 8 * gridDim.y) {
+    const int k0 = sb * 256 + 8 * lane;
+    float v[8];
+    if (b < batch) {
+      const float4 p0 = *reinterpret_cast<const float4*>(xr + k0);
+      const float4 p1 = *reinterpret_cast<const float4*>(xr + k0 + 4);
+      v[0] = p0.x, v[1] = p0.y, v[2] = p0.z, v[3] = p0.w, v[4] = p1.x, v[5] = p1.y, v[6] = p1.z,
+      v[7] = p1.w;
+      if (norm_w) {
+        const float4 w0 = *reinterpret_cast<const float4*>(norm_w + k0);
+        const float4 w1 = *reinterpret_cast<const float4*>(norm_w + k0 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = v[i] * (inv_rms * wv[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] *= inv;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = 0.0f;
+    }
+    __half h[8], l[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      h[i] = __float2half_rn(v[i]);
+      l[i] = __float2half_rn(v[i] - __half2float(h[i]));
+    }
+    // column order inside 4 columns: (0, 2, 1, 3)
+    auto pack = [](const __half* q, int i0, int i1) {
+      return (uint32_t)__half_as_ushort(q[i0]) | ((uint32_t)__half_as_ushort(q[i1]) << 16);
+    };
+    const uint4 hv = make_uint4(pack(h, 0, 2), pack(h, 1, 3), pack(h, 4, 6), pack(h, 5, 7));
+    const uint4 lv = make_uint4(pack(l, 0, 2), pack(l, 1, 3), pack(l, 4, 6), pack(l, 5, 7));
+    uint8_t* tile = xt + (size_t)(k0 / kKC) * tile_b(ni) + (lane & 15) * 128;
+    const int nh = 2 * b, nl = 2 * b + 1;
+    *reinterpret_cast<uint4*>(tile + (nh >> 3) * kSBO + (nh & 7) * 16) = hv;
+    *reinterpret_cast<uint4*>(tile + (nl >> 3) * kSBO + (nl & 7) * 16) = lv;
+    float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    uint8_t* mt = xm + (size_t)sb * tile_bmin(ni);
+    if ((lane & 3) == 0) {
+      const float sg = sum * (1.0f / 32.0f);
+      const __half sh = __float2half_rn(sg);
+      const __half sl = __float2half_rn(sg - __half2float(sh));
+      const int pos = lane >> 2;
+      *reinterpret_cast<__half*>(mt + (nh >> 3) * 256 + (nh & 7) * 16 + pos * 2) = sh;
+      *reinterpret_cast<__half*>(mt + (nl >> 3) * 256 + (nl & 7) * 16 + pos * 2) = sl;
+    }
+    if (lane == 0) {  // positions 8..15 (second core matrix) are zero
+      *reinterpret_cast<uint4*>(mt + (nh >> 3) * 256 + 128 + (nh & 7) * 16) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(mt + (nl >> 3) * 256 + 128 + (nl & 7) * 16) = make_uint4(0, 0, 0, 0);
     }
   }
 }
@@ -608,8 +635,8 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
   uint8_t* xm = xt + (size_t)(cols / kKC) * tile_b(ni);
   float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * tile_bmin(ni));
   float* part = xscale + kMaxItems;
-  xsplit_tc_kernel<<<ni, 256, 0, st>>>(p.x, p.x_ld, cols, B, ni, xt, xm, xscale, p.norm_w,
-                                       p.norm_eps);
+  xsplit_tc_kernel<<<dim3(ni, 4), 256, 0, st>>>(p.x, p.x_ld, cols, B, ni, xt, xm, xscale,
+                                                p.norm_w, p.norm_eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int kgroups = tc_kgroups(p, sms);
