@@ -568,7 +568,6 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   if ((rc = gemv_plan(&p, &lmm, 1, EPI_ARGMAX, nb))) return rc;
   p.error_flag = m->be->d_err;
   p.argmax_keys = m->keys + (lm_item >= 0 ? lm_item : 0);
-  p.argmax_base = m->vocab0;
   if (nb == 1 || gemm_supported(p)) {
     p.x = xin;
     p.norm_w = m->final_norm;
@@ -580,7 +579,9 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   p.x_ld = h;
   LRS_CUDA(model_gemv(m, p, st, sms));
   if (tp) {
-    // the shard argmaxes meet in one MAX all-reduce of the packed keys
+    // shard rows -> vocabulary ids, then the shard argmaxes meet in one MAX
+    // all-reduce of the packed keys
+    LRS_CUDA(launch_key_offset(p.argmax_keys, nb, (uint32_t)m->vocab0, st));
     LRS_NCCL(nccl().AllReduce(p.argmax_keys, p.argmax_keys, (size_t)nb, ncclUint64, ncclMax,
                               m->comm, st));
     if (want_logits)

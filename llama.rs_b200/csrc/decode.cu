@@ -420,6 +420,16 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
   return cudaGetLastError();
 }
 
+__global__ void key_offset_kernel(unsigned long long* keys, int n, uint32_t offset) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n && keys[i]) keys[i] += offset;
+}
+
+cudaError_t launch_key_offset(unsigned long long* keys, int n, uint32_t offset, cudaStream_t st) {
+  key_offset_kernel<<<(n + 63) / 64, 64, 0, st>>>(keys, n, offset);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_advance(const unsigned long long* keys, int* tok, int* pos, int batch,
                            int* step, int n_steps, uint32_t* tokens_out, uint32_t* last,
                            cudaStream_t st) {

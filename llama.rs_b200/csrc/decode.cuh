@@ -42,6 +42,8 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
                              float* part, float* att, cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
+// keys[i] += offset (the packed argmax keys of a vocabulary shard; 0 stays 0).
+cudaError_t launch_key_offset(unsigned long long* keys, int n, uint32_t offset, cudaStream_t st);
 cudaError_t launch_advance(const unsigned long long* keys, int* tok, int* pos, int batch,
                            int* step, int n_steps, uint32_t* tokens_out, uint32_t* last,
                            cudaStream_t st);

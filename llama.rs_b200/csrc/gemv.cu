@@ -195,7 +195,7 @@ __device__ void process_tile(const GemvParams& p, const GemvSeg& s, int tile, co
           }
         }
         if (p.epi == EPI_ARGMAX) {
-          unsigned long long key = tid < nr ? argmax_pack(y, (uint32_t)(r + p.argmax_base)) : 0ull;
+          unsigned long long key = tid < nr ? argmax_pack(y, (uint32_t)r) : 0ull;
 #pragma unroll
           for (int o = 16; o >= 1; o >>= 1) {
             unsigned long long other = shfl_xor_u64(key, o);
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
             break;
           default: {
             if (out) *out = y;
-            const unsigned long long k2 = argmax_pack(y, (uint32_t)(row + p.argmax_base));
+            const unsigned long long k2 = argmax_pack(y, (uint32_t)row);
             key = k2 > key ? k2 : key;
           }
         }

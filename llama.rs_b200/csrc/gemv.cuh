@@ -34,7 +34,7 @@ struct GemvParams {
   const float* norm_w;  // fused RMSNorm of x (batch 1 only) or null
   float norm_eps;
   unsigned long long* argmax_keys;  // [batch], EPI_ARGMAX
-  int argmax_base;  // added to the row index in the argmax key (a vocabulary shard's first row)
+  int argmax_base;  // added to the row index in the argmax key (batched paths; 0 otherwise)
   int stage_bytes, stages, x_in_smem;
   int fast;  // 1: batch-1 direct-load kernel (int8-split x, dp4a)
   int wpg;   // batch-1 kernel: warps sharing one row group (long rows split across warps)
