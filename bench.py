@@ -169,6 +169,18 @@ def cpu_decode_rate(orc, lrs, sm, cfg, wl, threads, budget_s=15.0):
     return n / r["decode_s"], n
 
 
+def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
+    """The `config` object both arms print for a workload."""
+    return {"workload": f"{wl['model']} {wl['quant']}: {total_seqs} sequences x "
+                        f"({P} prompt + greedy decode), ctx {wl['ctx']}, "
+                        + (f"{layers} layers (profiling case), " if layers else "") +
+                        (f"tensor-parallel over {world} GPUs" if tp else
+                         f"data-parallel over {world} GPU(s)"),
+            "parallelism": f"tp{world}" if tp else f"dp{world}",
+            "sequences_per_gpu": total_seqs if tp else total_seqs // max(world, 1), "prompt": P,
+            "kv_cache": "bf16" if kv_bf16 else "f32"}
+
+
 def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -198,8 +210,10 @@ def run_reference(args, wl):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and ids)",
-        "config": {"workload": f"{wl['model']} {wl['quant']} greedy decode", "kernel": "avx2",
-                   "threads": threads},
+        "config": dict(workload_config(wl, args.seqs or wl["seqs"], args.prompt or wl["prompt"],
+                                       args.gpus, args.tp and args.gpus > 1, wl.get("layers", 0),
+                                       args.kv_bf16),
+                       kernel="avx2", threads=threads),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample + "; C++ restatement of the reference AVX2 backend "
                                             "(src/simd.rs) -- the Rust reference cannot be built "
@@ -365,15 +379,8 @@ def run_ours(args, wl):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random weights N(0,0.02), uniform prompt ids)",
-            "config": {"workload": f"{wl['model']} {wl['quant']}: {total_seqs} sequences x "
-                                   f"({P} prompt + greedy decode), ctx {wl['ctx']}, "
-                                   + (f"{cfg.num_hidden_layers} layers (profiling case), "
-                                      if wl.get("layers") else "") +
-                                   (f"tensor-parallel over {world} GPUs" if tp else
-                                      f"data-parallel over {world} GPU(s)"),
-                       "parallelism": f"tp{world}" if tp else f"dp{world}",
-                       "sequences_per_gpu": B, "prompt": P,
-                       "kv_cache": "bf16" if args.kv_bf16 else "f32",
+            "config": {**workload_config(wl, total_seqs, P, world, tp, wl.get("layers", 0),
+                                         args.kv_bf16),
                        "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights streamed per step"},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
                     "d2h_bytes_per_step": 4 * B + 4},
