@@ -168,6 +168,15 @@ _sig("lrs_matvec", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_batched", C.c_int32, _P, _P, _F, C.c_size_t, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_noalloc", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_device", C.c_int32, _P, _P, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+_sig("lrs_gguf_open", C.c_int32, C.c_char_p, C.POINTER(_P))
+_sig("lrs_gguf_close", None, _P)
+_sig("lrs_gguf_version", C.c_uint32, _P)
+_sig("lrs_gguf_tensor_count", C.c_size_t, _P)
+_sig("lrs_gguf_metadata_u64", C.c_int32, _P, C.c_char_p, C.POINTER(C.c_uint64))
+_sig("lrs_gguf_metadata_f32", C.c_int32, _P, C.c_char_p, C.POINTER(C.c_float))
+_sig("lrs_gguf_metadata_str", C.c_int32, _P, C.c_char_p, C.POINTER(C.c_char_p))
+_sig("lrs_gguf_tensor", C.c_int32, _P, C.c_char_p, C.POINTER(_TensorDesc))
+_sig("lrs_gguf_qwen2_desc", C.c_int32, _P, C.c_uint32, C.POINTER(C.POINTER(_ModelDesc)))
 _sig("lrs_tp_unique_id", C.c_int32, C.c_char_p)
 _sig("lrs_model_create_tp", C.c_int32, _P, C.POINTER(_ModelDesc), C.POINTER(_ModelOptions),
      C.c_uint32, C.c_uint32, C.c_char_p, C.POINTER(_P))
@@ -204,7 +213,10 @@ EXPORTED_SYMBOLS = (
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
     "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels",
-    "lrs_tp_unique_id", "lrs_model_create_tp", "lrs_model_tp_world", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
+    "lrs_tp_unique_id", "lrs_model_create_tp", "lrs_model_tp_world",
+    "lrs_gguf_open", "lrs_gguf_close", "lrs_gguf_version", "lrs_gguf_tensor_count",
+    "lrs_gguf_metadata_u64", "lrs_gguf_metadata_f32", "lrs_gguf_metadata_str", "lrs_gguf_tensor",
+    "lrs_gguf_qwen2_desc", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
 )
 
@@ -721,6 +733,150 @@ class CudaQwen2Model:
 
 
 # ------------------------------------------------------ benchmark configs --
+class GgufFile:
+    """GgufFile (src/gguf.rs:72-230) over the C reader: metadata, QuantTensor
+    views into the mapped file, and the Qwen2 model description of
+    GgufLoader::load (src/loader.rs:233-398) for lrs_model_create."""
+
+    def __init__(self, path: str):
+        h = _P()
+        _check(_lib.lrs_gguf_open(os.fsencode(path), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            _lib.lrs_gguf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def version(self) -> int:
+        return int(_lib.lrs_gguf_version(self._h))
+
+    @property
+    def tensor_count(self) -> int:
+        return int(_lib.lrs_gguf_tensor_count(self._h))
+
+    def metadata_u64(self, key: str) -> int:
+        v = C.c_uint64()
+        _check(_lib.lrs_gguf_metadata_u64(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+    def metadata_f32(self, key: str) -> float:
+        v = C.c_float()
+        _check(_lib.lrs_gguf_metadata_f32(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+    def metadata_str(self, key: str) -> str:
+        v = C.c_char_p()
+        _check(_lib.lrs_gguf_metadata_str(self._h, key.encode(), C.byref(v)))
+        return v.value.decode()
+
+    def tensor(self, name: str) -> QuantTensor:
+        td = _TensorDesc()
+        _check(_lib.lrs_gguf_tensor(self._h, name.encode(), C.byref(td)))
+        buf = (C.c_uint8 * td.nbytes).from_address(td.data) if td.nbytes else b""
+        return QuantTensor(np.frombuffer(buf, dtype=np.uint8), (td.rows, td.cols),
+                           QuantType(td.ggml_type))
+
+    def qwen2_desc(self, recipe: LoadQuantization = LoadQuantization.NONE):
+        """The model description (valid while this object lives)."""
+        out = C.POINTER(_ModelDesc)()
+        _check(_lib.lrs_gguf_qwen2_desc(self._h, int(recipe), C.byref(out)))
+        return out
+
+
+# GGUF metadata value types (the format's numbering, src/gguf.rs:313-343)
+GGUF_U32, GGUF_I32, GGUF_F32, GGUF_STR, GGUF_U64 = 4, 5, 6, 8, 10
+
+
+def write_gguf(path: str, metadata, tensors, alignment: int = 32, version: int = 3) -> None:
+    """Writes a GGUF file.  metadata: [(key, gguf_type, value)] with the scalar
+    types above; tensors: [(name, ggml_type, dims in GGML order (row width
+    first), bytes)].  Tensor data is aligned to `alignment`."""
+    import struct
+
+    def gstr(v: str) -> bytes:
+        b = v.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    fmt = {4: "<I", 5: "<i", 6: "<f", 10: "<Q"}
+    head = bytearray(b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(metadata)))
+    for key, ty, val in metadata:
+        head += gstr(key) + struct.pack("<I", ty)
+        head += gstr(val) if ty == GGUF_STR else struct.pack(fmt[ty], val)
+    off = 0
+    offsets = []
+    for name, ty, dims, data in tensors:
+        head += gstr(name) + struct.pack("<I", len(dims))
+        head += b"".join(struct.pack("<Q", d) for d in dims)
+        head += struct.pack("<IQ", ty, off)
+        offsets.append(off)
+        off += (len(data) + alignment - 1) // alignment * alignment
+    data_start = (len(head) + alignment - 1) // alignment * alignment
+    with open(path, "wb") as f:
+        f.write(head)
+        f.write(b"\0" * (data_start - len(head)))
+        for (name, ty, dims, data), o in zip(tensors, offsets):
+            f.seek(data_start + o)
+            f.write(data)
+        f.truncate(data_start + off)
+
+
+def write_qwen2_gguf(path: str, desc, alignment: int = 32) -> None:
+    """Writes the model behind an lrs_model_desc as a Qwen2 GGUF file with the
+    names GgufLoader expects (src/loader.rs:244-398); a tied head (the
+    embedding's bytes) is written without output.weight."""
+    d = desc.contents
+    c = d.config
+    h, kvw = c.hidden_size, c.num_key_value_heads * c.head_dim
+    meta = [("general.architecture", GGUF_STR, "qwen2"),
+            ("general.alignment", GGUF_U32, alignment),
+            ("qwen2.embedding_length", GGUF_U64, c.hidden_size),
+            ("qwen2.feed_forward_length", GGUF_U64, c.intermediate_size),
+            ("qwen2.attention.head_count", GGUF_U32, c.num_attention_heads),
+            ("qwen2.attention.head_count_kv", GGUF_U32, c.num_key_value_heads),
+            ("qwen2.block_count", GGUF_U32, c.num_hidden_layers),
+            ("qwen2.attention.layer_norm_rms_epsilon", GGUF_F32, c.rms_norm_eps),
+            ("qwen2.rope.freq_base", GGUF_F32, c.rope_theta),
+            ("qwen2.context_length", GGUF_U64, c.max_position_embeddings)]
+    tensors = []
+
+    def mat(name, td):
+        tensors.append((name, td.ggml_type, [td.cols, td.rows],
+                        bytes((C.c_uint8 * td.nbytes).from_address(td.data))))
+
+    def vec(name, ptr, n):
+        if ptr:
+            tensors.append((name, int(QuantType.F32), [n],
+                            bytes((C.c_uint8 * (4 * n)).from_address(ptr))))
+
+    mat("token_embd.weight", d.embed_tokens)
+    vec("output_norm.weight", d.final_norm, h)
+    for i in range(c.num_hidden_layers):
+        L, p = d.layers[i], f"blk.{i}"
+        vec(f"{p}.attn_norm.weight", L.input_layernorm, h)
+        mat(f"{p}.attn_q.weight", L.q_proj)
+        vec(f"{p}.attn_q.bias", L.q_bias, h)
+        mat(f"{p}.attn_k.weight", L.k_proj)
+        vec(f"{p}.attn_k.bias", L.k_bias, kvw)
+        mat(f"{p}.attn_v.weight", L.v_proj)
+        vec(f"{p}.attn_v.bias", L.v_bias, kvw)
+        mat(f"{p}.attn_output.weight", L.o_proj)
+        vec(f"{p}.ffn_norm.weight", L.post_attention_layernorm, h)
+        mat(f"{p}.ffn_gate.weight", L.gate_proj)
+        mat(f"{p}.ffn_up.weight", L.up_proj)
+        mat(f"{p}.ffn_down.weight", L.down_proj)
+    if d.lm_head.data != d.embed_tokens.data:
+        mat("output.weight", d.lm_head)
+    write_gguf(path, meta, tensors, alignment)
+
+
 def tp_unique_id() -> bytes:
     """The 128-byte NCCL id for lrs_model_create_tp (rank 0 makes it)."""
     buf = C.create_string_buffer(128)

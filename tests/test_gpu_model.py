@@ -131,3 +131,21 @@ def test_c3_width_64_sequences(lrs, orc, backend):
     for s in (0, 31, 63):
         ref = orc.OracleModel(sm.desc(), 256).benchmark_tokens(prompts[s], n_dec)
         _assert_tokens(ref, fed[:, s])
+
+
+def test_model_from_gguf_file(lrs, orc, backend, tmp_path):
+    """A q4km model written as GGUF and loaded through lrs_gguf_qwen2_desc
+    (tensors uploaded straight from the mapped file) decodes like the oracle."""
+    cfg = _cfg(lrs, 512, 1024, 8, 2, 2, 2000, 64, False)
+    sm = lrs.SynthModel(cfg, 12, lrs.LoadQuantization.Q4KM)
+    path = str(tmp_path / "m.gguf")
+    lrs.write_qwen2_gguf(path, sm.desc())
+    g = lrs.GgufFile(path)
+    model = lrs.CudaQwen2Model(backend, g.qwen2_desc(lrs.LoadQuantization.Q4KM), max_seq_len=256)
+    prompt = lrs.prompt_tokens(12, 30, cfg.vocab_size)
+    ref = orc.OracleModel(sm.desc(), 256).benchmark_tokens(prompt, 16, keep_logits=True)
+    logits, first = model.prefill(prompt, 0)
+    produced = model.decode_greedy([first], [len(prompt)], 16)[:, 0]
+    assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
+    _assert_tokens(ref, np.concatenate([[first], produced[:-1]]))
+    model.close()
