@@ -36,6 +36,14 @@ lrs_status lrs_quantize_matrix(uint32_t ggml_type, const float* values, size_t r
                                void* out, size_t out_cap, uint32_t* out_type, size_t* out_len);
 size_t lrs_quantized_size(uint32_t ggml_type, size_t rows, size_t cols);
 
+/* The same encoders on the GPU (no counterpart in the reference, which
+ * encodes on the host): `d_values` and `d_out` are device pointers, one
+ * thread per block on the backend's stream; returns when the bytes are
+ * written.  The bytes equal lrs_quantize_matrix's for the same input. */
+lrs_status lrs_quantize_matrix_device(lrs_backend* backend, uint32_t ggml_type,
+                                      const float* d_values, size_t rows, size_t cols, void* d_out,
+                                      size_t out_cap, uint32_t* out_type, size_t* out_len);
+
 /* Deterministic N(0, std) values of the synthetic models: element i of the
  * tensor called `name` under `seed` (counter-based, so any slice can be
  * generated independently).  Writes out[0..n) = value(offset + k). */

@@ -168,6 +168,8 @@ _sig("lrs_matvec", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_batched", C.c_int32, _P, _P, _F, C.c_size_t, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_noalloc", C.c_int32, _P, _P, _F, C.c_size_t, _F, C.c_size_t)
 _sig("lrs_matvec_device", C.c_int32, _P, _P, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+_sig("lrs_quantize_matrix_device", C.c_int32, _P, C.c_uint32, C.c_void_p, C.c_size_t, C.c_size_t,
+     C.c_void_p, C.c_size_t, _U32, C.POINTER(C.c_size_t))
 _sig("lrs_gguf_open", C.c_int32, C.c_char_p, C.POINTER(_P))
 _sig("lrs_gguf_close", None, _P)
 _sig("lrs_gguf_version", C.c_uint32, _P)
@@ -214,7 +216,7 @@ EXPORTED_SYMBOLS = (
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
     "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels",
     "lrs_tp_unique_id", "lrs_model_create_tp", "lrs_model_tp_world",
-    "lrs_gguf_open", "lrs_gguf_close", "lrs_gguf_version", "lrs_gguf_tensor_count",
+    "lrs_quantize_matrix_device", "lrs_gguf_open", "lrs_gguf_close", "lrs_gguf_version", "lrs_gguf_tensor_count",
     "lrs_gguf_metadata_u64", "lrs_gguf_metadata_f32", "lrs_gguf_metadata_str", "lrs_gguf_tensor",
     "lrs_gguf_qwen2_desc", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
@@ -417,6 +419,16 @@ class CudaBackend:
         """Queues a batched matvec on device pointers (no synchronization)."""
         t = self.upload(weight)
         _check(_lib.lrs_matvec_device(self._h, t, d_in, batch, d_out, stream))
+
+    def quantize_device(self, d_values: int, rows: int, cols: int, quant_type: "QuantType",
+                        d_out: int, out_cap: int):
+        """The load-time encoders on the GPU (lrs_quantize_matrix_device): device
+        pointers in and out; returns (type produced, bytes written)."""
+        t = np.zeros(1, np.uint32)
+        n = C.c_size_t()
+        _check(_lib.lrs_quantize_matrix_device(self._h, int(quant_type), d_values, rows, cols, d_out,
+                                               out_cap, _uptr(t), C.byref(n)))
+        return QuantType(int(t[0])), n.value
 
     def dequantize_rows(self, weight: QuantTensor, row0: int, nrows: int) -> np.ndarray:
         """value_at for rows [row0, row0 + nrows) (QuantTensor::row_into)."""
