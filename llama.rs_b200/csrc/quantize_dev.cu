@@ -1,5 +1,6 @@
-// quantize_dev.cu -- the load-time GGML encoders on the device (SURVEY next
-// step: encode the 7B/32B weights on the GPU instead of the host).  One thread
+// quantize_dev.cu -- the load-time GGML encoders on the device, so F32/F16/
+// BF16 weights of the 7B/32B models encode in HBM instead of on the host
+// (maybe_quantize, src/loader.rs:406-447).  One thread
 // encodes one block with the same code as the host (encoders.h); this file is
 // compiled with --fmad=false so every f32 operation rounds like the
 // reference's, and the bytes equal lrs_quantize_matrix's.
