@@ -1,9 +1,10 @@
-// gemm_tc.cu -- batched Q4_K matmul (33..64 items: decode batches and prefill
-// chunks) on the 5th-generation tensor cores: tcgen05.mma with the
+// gemm_tc.cu -- batched Q4_K / Q6_K matmul (4..64 items: decode batches and
+// prefill chunks) on the 5th-generation tensor cores: tcgen05.mma with the
 // accumulators in tensor memory (TMEM).
 //
 // Replaces B independent CpuBackend::matvec calls (src/backend.rs:143-162)
-// for Q4_K weights, the bulk of the q4k/q4km models (q, k, o, gate, up).
+// for Q4_K and Q6_K weights, the bulk of the q4k/q4km models (q, k, o, gate,
+// up in Q4_K; down in Q6_K under q4km).
 //
 // Arithmetic.  A Q4_K super-block row is w_k = d*sc_g*q_k - dmin*m_g
 // (value_at, src/quant.rs:404-440) with 6-bit sc_g, m_g per 32-column group g.

@@ -303,20 +303,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 // all its rows straight from global memory (R loads in flight per lane, no
 // staging, no block barrier), multiplies codes by xh and xl with dp4a into
 // exact int32 sums per run, and applies the scales (gemv_fast.cuh).  One warp
-// reduction per row ends the group.  Dense types (F32/F16/BF16) keep float x.
-template <int T>
-struct XLayout {
-  using P = fast::Piece<T>;
-  static constexpr bool kDense = T == LRS_GGML_F32 || T == LRS_GGML_F16 || T == LRS_GGML_BF16;
-  static constexpr int PV = P::kValues;        // values per piece
-  static constexpr int NRUN = PV / 8;          // 8-column runs per piece
-  static constexpr int CH = PV / 16;           // 16-byte chunks of xh (and of xl) per piece
-  // bytes of the staged x for `npieces` pieces
-  __host__ __device__ static size_t bytes(int npieces) {
-    if constexpr (kDense) return (size_t)npieces * PV * 4;
-    return (size_t)npieces * (2 * CH * 16 + NRUN * 8);
-  }
-};
+// reduction per row ends the group.  Dense types (F32/F16/BF16) keep float x
+// (XLayout, gemv_fast.cuh).
 
 // Bulk-prefetches the rows of row group g (R rows, both matrices of a pair)
 // into L2 so that the lanes' loads of the group hit L2 instead of HBM.
@@ -765,7 +753,9 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
       p.scratch_bytes >= gemm_scratch_bytes(p.batch, p.cols, num_sms))
     return gemm_launch(p, p.scratch, num_sms, stream);
   if (p.fast) {
-    // Direct-load batch-1 kernel, one launch per run of same-type segments.
+    // Direct-load batch-1 kernel (or, with LRS_GEMV_STREAM=1, the bulk-copy
+    // ring of gemv_stream.cu), one launch per run of same-type segments.
+    const bool stream_on = gemv_stream_enabled();
     int i = 0;
     while (i < p.nseg) {
       int j = i + 1;
@@ -778,6 +768,12 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
         q.seg[k].tile0 -= t0;
       }
       q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
+      if (stream_on) {
+        cudaError_t e = gemv_stream_launch(q, stream, num_sms, pdl);
+        if (e != cudaSuccess) return e;
+        i = j;
+        continue;
+      }
       const void* kernel = fast_kernel(q.seg[0].type, pair);
       const size_t smem = 256 + fast_x_bytes(q.seg[0].type, q.cols);
       const int occ = std::max(1, occupancy(kernel, (int)smem, kGemvThreads));

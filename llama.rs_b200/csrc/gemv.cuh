@@ -39,8 +39,8 @@ struct GemvParams {
   int fast;  // 1: batch-1 direct-load kernel (int8-split x, dp4a)
   int wpg;   // batch-1 kernel: warps sharing one row group (long rows split across warps)
   int* error_flag;
-  // Device scratch for the batched tensor-core path (gemm_i8.cu); when null or
-  // smaller than gemm_scratch_bytes, batches run on the CUDA-core kernel.
+  // Device scratch for the batched tensor-core paths (gemm_mma.cu, gemm_tc.cu);
+  // when null or too small, batches run on the CUDA-core kernel.
   void* scratch;
   size_t scratch_bytes;
 };
@@ -59,7 +59,7 @@ int gemv_plan(GemvParams* p, const GemvMat* mats, int nmat, int epi, int batch);
 // Launches on `stream` (with programmatic dependent launch when pdl != 0).
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl);
 
-// Batched (2..) quantized matmul on the integer tensor cores (gemm_i8.cu).
+// Batched (2..64) quantized matmul on the tensor cores with mma.sync (gemm_mma.cu).
 bool gemm_supported(const GemvParams& p);
 size_t gemm_scratch_bytes(int batch, int max_cols, int sms);
 cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
@@ -67,9 +67,15 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
 cudaError_t gemm_partials_epilogue(const GemvParams& p, const float* const* parts, int kgroups,
                                    cudaStream_t stream);
 
-// Batched Q4_K matmul on tcgen05 (gemm_tc.cu), 33..64 items.
+// Batched Q4_K / Q6_K matmul on tcgen05 (gemm_tc.cu), 4..64 items.
 bool gemm_tc_supported(const GemvParams& p);
 size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms);
 cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
+
+// Batch-1 GEMV through a shared-memory ring of bulk copies (gemv_stream.cu),
+// for one run of same-type segments planned by gemv_plan (p.fast).  Used
+// instead of gemv5_kernel when LRS_GEMV_STREAM=1.
+bool gemv_stream_enabled();
+cudaError_t gemv_stream_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl);
 
 }  // namespace lrs

@@ -360,4 +360,120 @@ template <>
 struct Piece<LRS_GGML_BF16> : PieceDense<LRS_GGML_BF16> {};
 
 }  // namespace fast
+// ---- x prepared for the factored dots -------------------------------------
+// Each 8-column run r of x (after the optional RMSNorm) is split as
+//     x ~= s_r * (xh + xl / 256),  xh, xl int8,  s_r = max|x_run| / 127,
+// (about 15 bits of x; the dot's error is ~1e-5 relative) together with the
+// exact float sum X_r of the run.  The layout is piece-transposed: 16-byte
+// chunk k of piece p sits at (k * npieces + p) * 16, so the lanes of a warp,
+// which handle consecutive pieces, read consecutive chunks.  Dense types
+// (F32/F16/BF16) keep float x, piece-major.
+template <int T>
+struct XLayout {
+  using P = fast::Piece<T>;
+  static constexpr bool kDense = T == LRS_GGML_F32 || T == LRS_GGML_F16 || T == LRS_GGML_BF16;
+  static constexpr int PV = P::kValues;        // values per piece
+  static constexpr int NRUN = PV / 8;          // 8-column runs per piece
+  static constexpr int CH = PV / 16;           // 16-byte chunks of xh (and of xl) per piece
+  // bytes of the staged x for `npieces` pieces
+  __host__ __device__ static size_t bytes(int npieces) {
+    if constexpr (kDense) return (size_t)npieces * PV * 4;
+    return (size_t)npieces * (2 * CH * 16 + NRUN * 8);
+  }
+};
+
+// Views of the staged x at xq for `npieces` pieces.
+template <int T>
+struct XView {
+  using XL = XLayout<T>;
+  uint4* xh4;  // [CH][npieces]
+  uint4* xl4;  // [CH][npieces]
+  float* sxa;  // [NRUN][npieces]: s_r / 256
+  float* Xa;   // [NRUN][npieces]: X_r
+  float* xf;   // dense: [npieces][PV]
+  __device__ __forceinline__ XView(uint8_t* xq, int npieces) {
+    xh4 = reinterpret_cast<uint4*>(xq);
+    xl4 = xh4 + (size_t)XL::CH * npieces;
+    sxa = reinterpret_cast<float*>(xl4 + (size_t)XL::CH * npieces);
+    Xa = sxa + (size_t)XL::NRUN * npieces;
+    xf = reinterpret_cast<float*>(xq);
+  }
+};
+
+// Stages x (cols values; RMSNorm::forward of src/model.rs:65-73 first when
+// norm_w is set) at xq in the XLayout of type T.  NT threads take part (tid in
+// [0, NT)); `sync()` is their barrier; red holds NT / 32 floats.  Ends with a
+// sync, so xq is ready for all NT threads on return.
+template <int T, int NT, class Sync>
+__device__ __forceinline__ void prep_x(const float* x, const float* norm_w, float norm_eps, int cols,
+                                       uint8_t* xq, float* red, int tid, Sync sync) {
+  using BT = BlockTraits<T>;
+  using P = fast::Piece<T>;
+  using XL = XLayout<T>;
+  constexpr int PV = XL::PV, NRUN = XL::NRUN;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int npieces = cols / PV;
+  XView<T> xv(xq, npieces);
+  float inv_rms = 1.0f;
+  if (norm_w) {
+    float ss = 0.0f;
+    for (int c = tid; c < cols; c += NT) ss = fmaf(x[c], x[c], ss);
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    sync();
+    float tot = 0.0f;
+    for (int w = 0; w < NT / 32; w++) tot += red[w];
+    inv_rms = 1.0f / sqrtf(tot / (float)cols + norm_eps);
+  }
+  // One thread per (piece, run): gather the run's 8 values, normalize, split.
+  for (int t = tid; t < npieces * NRUN; t += NT) {
+    const int pc = t % npieces, r = t / npieces;
+    const int unit = pc / P::kPieces, sub = pc % P::kPieces;
+    const int col = unit * BT::kValues + P::col(sub, 2 * r);
+    float v[8];
+    const float4 a = *reinterpret_cast<const float4*>(x + col);
+    const float4 b = *reinterpret_cast<const float4*>(x + col + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    if (norm_w) {
+      const float4 wa = *reinterpret_cast<const float4*>(norm_w + col);
+      const float4 wb = *reinterpret_cast<const float4*>(norm_w + col + 4);
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int c = 0; c < 8; c++) v[c] = v[c] * (inv_rms * w[c]);
+    }
+    if constexpr (XL::kDense) {
+#pragma unroll
+      for (int c = 0; c < 8; c++) xv.xf[(size_t)pc * PV + 8 * r + c] = v[c];
+    } else {
+      float mx = 0.0f, sum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; c++) mx = fmaxf(mx, fabsf(v[c]));
+      sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+      const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+      const float inv = 1.0f / sc;
+      uint32_t hw[2], lw[2];
+#pragma unroll
+      for (int w = 0; w < 2; w++) {
+        hw[w] = lw[w] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float q = v[4 * w + c] * inv;
+          const float h = rintf(q);
+          const float l = fminf(fmaxf(rintf((q - h) * 256.0f), -127.0f), 127.0f);
+          hw[w] |= ((uint32_t)(int)h & 0xffu) << (8 * c);
+          lw[w] |= ((uint32_t)(int)l & 0xffu) << (8 * c);
+        }
+      }
+      // run r = words 2r, 2r+1 of the piece = 8 bytes of chunk r / 2
+      uint32_t* hc = reinterpret_cast<uint32_t*>(xv.xh4 + (size_t)(r >> 1) * npieces + pc) + 2 * (r & 1);
+      uint32_t* lc = reinterpret_cast<uint32_t*>(xv.xl4 + (size_t)(r >> 1) * npieces + pc) + 2 * (r & 1);
+      hc[0] = hw[0], hc[1] = hw[1];
+      lc[0] = lw[0], lc[1] = lw[1];
+      xv.sxa[(size_t)r * npieces + pc] = sc * (1.0f / 256.0f);
+      xv.Xa[(size_t)r * npieces + pc] = sum;
+    }
+  }
+  sync();
+}
+
 }  // namespace lrs
