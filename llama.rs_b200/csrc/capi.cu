@@ -375,6 +375,7 @@ struct lrs_model {
   int max_items = 0, max_split = 64;
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+  int* attn_cnt = nullptr;  // [max_items][kv heads] split counters of the attention combine
   void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
   // tensor parallelism: this process holds shard tp_rank of tp_world
   int tp_rank = 0, tp_world = 1;
@@ -526,7 +527,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
                                L.kpool, L.vpool, kv_bf16, st));
     LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
-                              m->att, st));
+                              m->att, m->attn_cnt, m->be->d_err, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
     GemvMat om = mat_of(L.o, m->residual, h);
@@ -822,8 +823,10 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->d_pos, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_seq, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_step, 4)) ||
-      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
+      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->attn_cnt, B * cl.num_key_value_heads * 4)))
     return cleanup(rc);
+  LRS_CUDA(cudaMemset(m->attn_cnt, 0, B * cl.num_key_value_heads * 4));
   m->gemm_scratch_bytes = gemm_scratch_bytes((int)B, std::max(h, I), m->be->sms);
   {
     // the tcgen05 path keeps all K-group partials of a launch: size for the

@@ -9,7 +9,7 @@ not start on a 16-byte boundary (Q6_K/Q5_0/Q8_0 row sizes), a segment run
 RMSNorm) through the model.
 
 The kernel is selected per launch by LRS_GEMV_STREAM=1; these tests run when
-LRS_GEMV_STREAM_TEST=1 is set as well.
+LRS_TEST_NEW_KERNELS=1 is set as well.
 """
 import os
 
@@ -18,8 +18,8 @@ import pytest
 
 pytestmark = [
     pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("LRS_GEMV_STREAM_TEST") != "1",
-                       reason="stream GEMV parity runs with LRS_GEMV_STREAM_TEST=1"),
+    pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
+                       reason="stream GEMV parity runs with LRS_TEST_NEW_KERNELS=1"),
 ]
 TOL = 1e-3
 LOGIT_TOL = 2e-2
