@@ -287,13 +287,14 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
   p.x_ld = w->t.cols;
   p.error_flag = be->d_err;
   if (batch > 1 && gemm_supported(p)) {
-    const size_t need = gemm_scratch_bytes((int)batch, w->t.cols, be->sms);
+    const size_t need = gemm_scratch_bytes((int)batch, w->t.cols, be->sms) + kScratchCounterBytes;
     if (be->scratch_cap < need) {
       cudaFree(be->d_scratch);  // synchronizes with work that may still use it
       be->d_scratch = nullptr;
       be->scratch_cap = 0;
       if (cudaMalloc(&be->d_scratch, need) != cudaSuccess)
         return fail(LRS_ERR_OOM, "cudaMalloc of matmul scratch failed");
+      LRS_CUDA(cudaMemset(be->d_scratch, 0, need));  // the tail counters start at zero
       be->scratch_cap = need;
     }
     p.scratch = be->d_scratch;
@@ -844,7 +845,9 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         m->gemm_scratch_bytes = std::max(m->gemm_scratch_bytes, gemm_tc_scratch_bytes(p, m->be->sms));
     }
   }
+  m->gemm_scratch_bytes += kScratchCounterBytes;
   if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
+  LRS_CUDA(cudaMemset(m->gemm_scratch, 0, m->gemm_scratch_bytes));  // the tail counters start at zero
   if (world > 1 &&
       (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))
     return cleanup(rc);

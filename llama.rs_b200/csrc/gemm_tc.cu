@@ -43,6 +43,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.h"
 #include "device_common.cuh"
@@ -160,7 +161,11 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8
 // xscale: [64] item scales.
 __global__ void __launch_bounds__(256)
     xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, int ni, uint8_t* xt,
-                     uint8_t* xm, float* xscale, const float* norm_w, float norm_eps) {
+                     uint8_t* xm, float* xscale, const float* norm_w, float norm_eps,
+                     int pdl_trigger) {
+  // lets a matmul launched with programmatic dependent launch start decoding
+  // its weights now; it reads what this kernel writes after griddepcontrol.wait
+  if (pdl_trigger) pdl_launch_dependents();
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = x + (size_t)b * x_ld;
@@ -257,6 +262,22 @@ struct TcArgs {
   const float* xscale;
   float* part;  // [kgroups][batch][rows]
   int* error_flag;
+  // Fused-mode launch (the FUSED kernel variant, programmatic dependent
+  // launch): x tiles and scales are read only after griddepcontrol.wait, so the
+  // producers decode weights while x is prepared.
+  int pdl;
+  // Output step in the kernel (0: partials only, for gemm_partials_epilogue or
+  // a later fused launch).  With kgroups > 1 the CTA that finishes last for its
+  // row block adds the kgroups partials in order 0..kgroups-1 (the order of
+  // gemm_epilogue_kernel) and applies it; counters[row block] is zero between
+  // launches (reset by that CTA).
+  int fused;
+  int epi, out_ld, argmax_base;
+  float* out;
+  const float* bias;
+  const float* gate_part;  // EPI_SWIGLU (the up matrix): the gate launch's partials
+  unsigned long long* keys;
+  int* counters;
 };
 
 // Four bytes at a 2-byte aligned address (Q6_K blocks are 210 bytes).
@@ -276,6 +297,9 @@ __device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
 }
+
+// Barrier of the four epilogue warps only (named barrier 2, 128 threads).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 // Raw bytes one producer thread (c, r) needs from one super-block.
 template <int T>
@@ -308,7 +332,7 @@ struct Raw<LRS_GGML_Q6_K> {
   }
 };
 
-template <int T, int NI>
+template <int T, int NI, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
   using S = TcShape<T, NI>;
   constexpr int kN = S::kN, kTileB = S::kTileB;
@@ -508,11 +532,62 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
     // partial sums, in units of the true x (item scales are powers of two)
     const int row = row0 + r;
-    if (ok && row < a.rows) {
+    const bool live = row < a.rows;
+    if constexpr (FUSED) pdl_wait();  // xscale, and outputs the previous kernels may read
+    if (ok && live) {
       float* pp = a.part + (size_t)blockIdx.y * a.batch * a.rows + row;
 #pragma unroll
       for (int i = 0; i < NI; i++)
         if (i < a.batch) pp[(size_t)i * a.rows] = acc[i] * a.xscale[i];
+    }
+    if (FUSED && a.fused) {
+      // the CTA that finishes last for this row block (the only one when
+      // kgroups == 1) adds the partials in K-group order and applies the step
+      bool last = true;
+      if (a.kgroups > 1) {
+        __threadfence();
+        epilogue_sync();
+        __shared__ int last_sh;
+        if (r == 0) last_sh = atomicAdd(&a.counters[blockIdx.x], 1) == a.kgroups - 1;
+        epilogue_sync();
+        last = last_sh != 0;
+        if (last) __threadfence();
+      }
+      if (last) {
+        // LinearLayer::forward + bias / residual add / SwiGLU / greedy argmax
+        // (src/model.rs:33-46, 236-238, 251-254, 258-260; src/engine.rs:233-241)
+#pragma unroll 1
+        for (int i = 0; i < a.batch; i++) {
+          unsigned long long key = 0ull;
+          if (live) {
+            float y = 0.0f;
+            for (int k = 0; k < a.kgroups; k++)
+              y += __ldcg(a.part + ((size_t)k * a.batch + i) * a.rows + row);
+            float* o = a.out ? a.out + (size_t)i * a.out_ld + row : nullptr;
+            if (a.epi == EPI_STORE) {
+              *o = a.bias ? y + a.bias[row] : y;
+            } else if (a.epi == EPI_ADD) {
+              *o += y;
+            } else if (a.epi == EPI_SWIGLU) {
+              float g = 0.0f;
+              for (int k = 0; k < a.kgroups; k++)
+                g += __ldcg(a.gate_part + ((size_t)k * a.batch + i) * a.rows + row);
+              *o = (g / (1.0f + expf(-g))) * y;
+            } else {
+              if (o) *o = y;
+              key = argmax_pack(y, (uint32_t)(row + a.argmax_base));
+            }
+          }
+          if (a.epi == EPI_ARGMAX) {
+            for (int sh = 16; sh >= 1; sh >>= 1) {
+              const unsigned long long v2 = __shfl_xor_sync(0xffffffffu, key, sh);
+              key = v2 > key ? v2 : key;
+            }
+            if (lane == 0 && key) atomicMax(&a.keys[i], key);
+          }
+        }
+        if (a.kgroups > 1 && r == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
+      }
     }
     if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
   } else if (lane == 0) {
@@ -530,6 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         tma_load_1d(smem + S::kOffBmin + ((h >> 1) & 1) * S::kTileBmin,
                     a.xm + (size_t)sbg * S::kTileBmin, S::kTileBmin, &full_b[bi], pol);
     };
+    if constexpr (FUSED) pdl_wait();  // the x tiles come from xsplit_tc_kernel
     for (int h = 0; h < S::kBB - 1 && h < nhs; h++) issue_x(h);
     for (int hs = 0; hs < nhs && ok; hs++) {
       const int sb = hs >> 1, half = hs & 1, ab = hs % S::kAB, bb = hs % S::kBB, tb = sb & 1;
@@ -595,24 +671,42 @@ int tc_kgroups(const GemvParams& p, int sms) {
   return ctas >= sms ? 1 : std::max(1, std::min(nsb, sms / ctas));
 }
 
-template <int T, int NI>
+template <int T, int NI, bool FUSED>
 cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI, FUSED>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          TcShape<T, NI>::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gemm_tc_kernel<T, NI><<<grid, kThreads, TcShape<T, NI>::kSmem, st>>>(a);
-  return cudaGetLastError();
+  if constexpr (!FUSED) {
+    gemm_tc_kernel<T, NI, false><<<grid, kThreads, TcShape<T, NI>::kSmem, st>>>(a);
+    return cudaGetLastError();
+  }
+  // programmatic dependent launch: the producers start while xsplit_tc_kernel runs
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = TcShape<T, NI>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr1[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<TcArgs*>(&a)};
+  return cudaLaunchKernelExC(&cfg, (const void*)gemm_tc_kernel<T, NI, FUSED>, args);
 }
 
 template <int NI>
 cudaError_t launch_tc_type(int type, const TcArgs& a, dim3 grid, cudaStream_t st) {
-  return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI>(a, grid, st)
-                               : launch_tc<LRS_GGML_Q4_K, NI>(a, grid, st);
+  if (a.pdl)
+    return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI, true>(a, grid, st)
+                                 : launch_tc<LRS_GGML_Q4_K, NI, true>(a, grid, st);
+  return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI, false>(a, grid, st)
+                               : launch_tc<LRS_GGML_Q4_K, NI, false>(a, grid, st);
 }
 }  // namespace
 
@@ -636,11 +730,22 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
   uint8_t* xm = xt + (size_t)(cols / kKC) * tile_b(ni);
   float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * tile_bmin(ni));
   float* part = xscale + kMaxItems;
+  const int kgroups = tc_kgroups(p, sms);
+  // LRS_TC_FUSED=1: output step in the matmul (no epilogue launch) and the
+  // matmul overlapping the x preparation; needs the counters at the tail of
+  // the scratch (zero between launches)
+  int* counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(scratch) + p.scratch_bytes -
+                                         kScratchCounterBytes);
+  int max_blocks = 0;
+  for (int i = 0; i < p.nseg; i++) max_blocks = std::max(max_blocks, (p.seg[i].rows + kRows - 1) / kRows);
+  const bool fused = gemm_tc_fused_enabled() &&
+                     p.scratch_bytes >= gemm_tc_scratch_bytes(p, sms) + kScratchCounterBytes &&
+                     max_blocks <= (int)(kScratchCounterBytes / sizeof(int)) &&
+                     reinterpret_cast<uintptr_t>(counters) % 4 == 0;
   xsplit_tc_kernel<<<dim3(ni, 4), 256, 0, st>>>(p.x, p.x_ld, cols, B, ni, xt, xm, xscale,
-                                                p.norm_w, p.norm_eps);
+                                                p.norm_w, p.norm_eps, fused ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const int kgroups = tc_kgroups(p, sms);
   const float* parts[kGemvMaxSeg];
   float* cur = part;
   for (int i = 0; i < p.nseg; i++) {
@@ -658,6 +763,18 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       a.xscale = xscale;
       a.part = cur;
       a.error_flag = p.error_flag;
+      if (fused) {
+        a.pdl = 1;
+        a.fused = !pair || m == 1;  // the gate launch of a pair only leaves partials
+        a.epi = p.epi;
+        a.out = p.seg[i].out;
+        a.out_ld = p.seg[i].out_ld;
+        a.bias = p.seg[i].bias;
+        a.argmax_base = p.argmax_base;
+        a.keys = p.argmax_keys;
+        a.gate_part = pair && m == 1 ? cur - (size_t)kgroups * B * a.rows : nullptr;
+        a.counters = counters;
+      }
       cur += (size_t)kgroups * B * a.rows;
       const dim3 grid((a.rows + kRows - 1) / kRows, kgroups);
       e = ni == 16 ? launch_tc_type<16>(p.seg[i].type, a, grid, st)
@@ -666,7 +783,13 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       if (e != cudaSuccess) return e;
     }
   }
+  if (fused) return cudaSuccess;
   return gemm_partials_epilogue(p, parts, kgroups, st);
+}
+
+bool gemm_tc_fused_enabled() {
+  const char* v = getenv("LRS_TC_FUSED");
+  return v && v[0] == '1';
 }
 
 }  // namespace lrs

@@ -67,10 +67,17 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
 cudaError_t gemm_partials_epilogue(const GemvParams& p, const float* const* parts, int kgroups,
                                    cudaStream_t stream);
 
-// Batched Q4_K / Q6_K matmul on tcgen05 (gemm_tc.cu), 4..64 items.
+// The last kScratchCounterBytes of a matmul scratch buffer are counters that
+// must be zero when the buffer is allocated; kernels that use them leave them
+// zero.  Scratch sizes passed in GemvParams include them.
+constexpr size_t kScratchCounterBytes = 16384;
+
+// Batched Q4_K / Q6_K matmul on tcgen05 (gemm_tc.cu), 4..64 items.  With
+// LRS_TC_FUSED=1 the output step runs in the matmul kernel (gemm_tc_fused_enabled).
 bool gemm_tc_supported(const GemvParams& p);
 size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms);
 cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
+bool gemm_tc_fused_enabled();
 
 // Batch-1 GEMV through a shared-memory ring of bulk copies (gemv_stream.cu),
 // for one run of same-type segments planned by gemv_plan (p.fast).  Used
