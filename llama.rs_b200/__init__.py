@@ -840,10 +840,14 @@ def write_gguf(path: str, metadata, tensors, alignment: int = 32, version: int =
         f.truncate(data_start + off)
 
 
-def write_qwen2_gguf(path: str, desc, alignment: int = 32) -> None:
+def write_qwen2_gguf(path: str, desc, alignment: int = 32, retype=None) -> None:
     """Writes the model behind an lrs_model_desc as a Qwen2 GGUF file with the
     names GgufLoader expects (src/loader.rs:244-398); a tied head (the
-    embedding's bytes) is written without output.weight."""
+    embedding's bytes) is written without output.weight.
+
+    retype(name, rows, cols) -> QuantType or None re-encodes F32 matrices per
+    tensor, as a quantizing tool writes mixed files (Q4_K_M-style files hold
+    several block types across tensors and layers)."""
     d = desc.contents
     c = d.config
     h, kvw = c.hidden_size, c.num_key_value_heads * c.head_dim
@@ -860,8 +864,15 @@ def write_qwen2_gguf(path: str, desc, alignment: int = 32) -> None:
     tensors = []
 
     def mat(name, td):
-        tensors.append((name, td.ggml_type, [td.cols, td.rows],
-                        bytes((C.c_uint8 * td.nbytes).from_address(td.data))))
+        data = bytes((C.c_uint8 * td.nbytes).from_address(td.data))
+        ty = td.ggml_type
+        want = retype(name, td.rows, td.cols) if retype else None
+        if want is not None and int(want) != ty:
+            if ty != int(QuantType.F32):
+                raise LrsError(1, f"{name}: only F32 tensors can be re-encoded")
+            q = QuantTensor.quantize(np.frombuffer(data, dtype=np.float32), td.rows, td.cols, want)
+            data, ty = q.data.tobytes(), int(q.quant_type)
+        tensors.append((name, ty, [td.cols, td.rows], data))
 
     def vec(name, ptr, n):
         if ptr:

@@ -377,6 +377,7 @@ struct lrs_model {
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
   int* attn_cnt = nullptr;  // [max_items][kv heads] split counters of the attention combine
+  float* act2 = nullptr;    // up projection when a layer's gate and up differ in type
   void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
   // tensor parallelism: this process holds shard tp_rank of tp_world
   int tp_rank = 0, tp_world = 1;
@@ -539,19 +540,34 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     LRS_CUDA(model_gemv(m, p, st, sms));
     if ((rc = allreduce_residual())) return rc;
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
-    GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
-    if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B))) return rc;
-    p.error_flag = m->be->d_err;
-    if (B == 1 || gemm_supported(p)) {
-      p.x = m->residual;
-      p.norm_w = L.post_norm;
-      p.norm_eps = c.rms_norm_eps;
-    } else {
-      LRS_CUDA(launch_rmsnorm(m->residual, L.post_norm, c.rms_norm_eps, h, B, m->xn, st));
-      p.x = m->xn;
+    bool xn_ready = false;
+    auto ffn_input = [&](GemvParams& q) -> int32_t {
+      q.error_flag = m->be->d_err;
+      if (B == 1 || gemm_supported(q)) {  // the norm is fused into the x preparation
+        q.x = m->residual;
+        q.norm_w = L.post_norm;
+        q.norm_eps = c.rms_norm_eps;
+      } else {
+        if (!xn_ready)
+          LRS_CUDA(launch_rmsnorm(m->residual, L.post_norm, c.rms_norm_eps, h, B, m->xn, st));
+        xn_ready = true;
+        q.x = m->xn;
+      }
+      q.x_ld = h;
+      return LRS_OK;
+    };
+    if (L.gate.type == L.up.type) {  // one launch over the row pair, SwiGLU in its epilogue
+      GemvMat gu = mat_of(L.gate, m->act, I, nullptr, &L.up);
+      if ((rc = gemv_plan(&p, &gu, 1, EPI_SWIGLU, B)) || (rc = ffn_input(p))) return rc;
+      LRS_CUDA(model_gemv(m, p, st, sms));
+    } else {  // mixed files: gate and up of different types, then SwiGLU
+      GemvMat gm = mat_of(L.gate, m->act, I), um = mat_of(L.up, m->act2, I);
+      if ((rc = gemv_plan(&p, &gm, 1, EPI_STORE, B)) || (rc = ffn_input(p))) return rc;
+      LRS_CUDA(model_gemv(m, p, st, sms));
+      if ((rc = gemv_plan(&p, &um, 1, EPI_STORE, B)) || (rc = ffn_input(p))) return rc;
+      LRS_CUDA(model_gemv(m, p, st, sms));
+      LRS_CUDA(launch_swiglu(m->act, m->act2, (size_t)B * I, st));
     }
-    p.x_ld = h;
-    LRS_CUDA(model_gemv(m, p, st, sms));
     // down_proj + residual (src/model.rs:255-260)
     GemvMat dm = mat_of(L.down, m->residual, h);
     if ((rc = gemv_plan(&p, &dm, 1, res_epi, B))) return rc;
@@ -762,8 +778,6 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         (rc = upload_mat(rows_of(s.up_proj, rank * I, I), I, h, "up_proj", &L.up)) ||
         (rc = upload_mat(d_loc, h, I, "down_proj", &L.down)))
       return cleanup(rc);
-    if (L.gate.type != L.up.type)
-      return cleanup(fail(LRS_ERR_UNSUPPORTED, "gate_proj and up_proj must share a GGML type"));
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
         (rc = upload_vec(m.get(), s.q_bias ? s.q_bias + rank * qw : nullptr, qw, &L.qb)) ||
@@ -828,6 +842,10 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->attn_cnt, B * cl.num_key_value_heads * 4)))
     return cleanup(rc);
   LRS_CUDA(cudaMemset(m->attn_cnt, 0, B * cl.num_key_value_heads * 4));
+  for (const auto& L : m->layers)
+    if (L.gate.type != L.up.type && !m->act2 &&
+        (rc = model_alloc(m.get(), (void**)&m->act2, B * I * 4)))
+      return cleanup(rc);
   m->gemm_scratch_bytes = gemm_scratch_bytes((int)B, std::max(h, I), m->be->sms);
   {
     // the tcgen05 path keeps all K-group partials of a launch: size for the

@@ -726,9 +726,25 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
   return cudaGetLastError();
 }
 
+// g[i] = silu(g[i]) * u[i] (src/model.rs:251-254), for gate and up
+// projections of different GGML types that ran as two launches.
+__global__ void swiglu_kernel(float* g, const float* u, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float y = g[i];
+    g[i] = (y / (1.0f + expf(-y))) * u[i];
+  }
+}
+
 __global__ void key_offset_kernel(unsigned long long* keys, int n, uint32_t offset) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n && keys[i]) keys[i] += offset;
+}
+
+cudaError_t launch_swiglu(float* g, const float* u, size_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, u, n);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_key_offset(unsigned long long* keys, int n, uint32_t offset, cudaStream_t st) {

@@ -49,6 +49,8 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
                              cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
+// g[i] = silu(g[i]) * u[i] over n floats (SwiGLU of separately computed gate / up).
+cudaError_t launch_swiglu(float* g, const float* u, size_t n, cudaStream_t st);
 // keys[i] += offset (the packed argmax keys of a vocabulary shard; 0 stays 0).
 cudaError_t launch_key_offset(unsigned long long* keys, int n, uint32_t offset, cudaStream_t st);
 cudaError_t launch_advance(const unsigned long long* keys, int* tok, int* pos, int batch,
