@@ -139,6 +139,20 @@ class _SynthSpec(C.Structure):
                 ("threads", C.c_uint32)]
 
 
+class Sampler(C.Structure):
+    """EngineOptions' sampling fields (src/engine.rs:11-33), with the reference's
+    defaults: temperature 0.7, top_p 0.9, top_k 40, repetition_penalty 1.1."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32),
+                ("repetition_penalty", C.c_float)]
+
+    def __init__(self, temperature: float = 0.7, top_p: float = 0.9, top_k: int = 40,
+                 repetition_penalty: float = 1.1):
+        super().__init__(temperature, top_p, top_k, repetition_penalty)
+
+
+#: LRS_SAMPLE_MAX_TOP_K: the largest top_k the device sampler takes
+SAMPLE_MAX_TOP_K = 4096
+
 _P = C.c_void_p
 _F = C.POINTER(C.c_float)
 _U32 = C.POINTER(C.c_uint32)
@@ -204,6 +218,11 @@ _sig("lrs_synth_fill", None, C.c_uint64, C.c_char_p, C.c_float, C.c_uint64, C.c_
 _sig("lrs_synth_model_create", C.c_int32, C.POINTER(_SynthSpec), C.POINTER(_P))
 _sig("lrs_synth_model_desc", C.POINTER(_ModelDesc), _P)
 _sig("lrs_synth_model_destroy", None, _P)
+_sig("lrs_sampler_check", C.c_int32, C.POINTER(Sampler), C.c_size_t)
+_sig("lrs_sample_logits", C.c_int32, _P, C.c_void_p, C.c_size_t, C.POINTER(Sampler), _U32,
+     C.c_size_t, C.c_float, _U32)
+_sig("lrs_model_forward_sample", C.c_int32, _P, C.c_uint32, C.c_uint32, C.c_uint32,
+     C.POINTER(Sampler), _U32, C.c_size_t, C.c_float, _U32)
 
 #: every symbol include/*.h declares (checked by the CPU tests)
 EXPORTED_SYMBOLS = (
@@ -220,6 +239,7 @@ EXPORTED_SYMBOLS = (
     "lrs_gguf_metadata_u64", "lrs_gguf_metadata_f32", "lrs_gguf_metadata_str", "lrs_gguf_tensor",
     "lrs_gguf_qwen2_desc", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
+    "lrs_sampler_check", "lrs_sample_logits", "lrs_model_forward_sample",
 )
 
 
@@ -419,6 +439,15 @@ class CudaBackend:
         """Queues a batched matvec on device pointers (no synchronization)."""
         t = self.upload(weight)
         _check(_lib.lrs_matvec_device(self._h, t, d_in, batch, d_out, stream))
+
+    def sample_logits(self, d_logits: int, vocab: int, params: Sampler, recent, u: float) -> int:
+        """sample_current_logits (src/engine.rs:253-325) on device logits
+        (lrs_sample_logits); u in [0, 1) is the reference's thread_rng draw."""
+        r = np.ascontiguousarray(np.asarray(recent, dtype=np.uint32))
+        out = np.zeros(1, dtype=np.uint32)
+        _check(_lib.lrs_sample_logits(self._h, d_logits, vocab, C.byref(params), _uptr(r), r.size,
+                                      u, _uptr(out)))
+        return int(out[0])
 
     def quantize_device(self, d_values: int, rows: int, cols: int, quant_type: "QuantType",
                         d_out: int, out_cap: int):
@@ -681,6 +710,16 @@ class CudaQwen2Model:
         _check(_lib.lrs_model_forward_token(self._h, seq, token_id, pos, 0, None, None))
         return None
 
+    def forward_sample(self, token_id: int, pos: int, params: Sampler, recent, u: float,
+                       seq: int = 0) -> int:
+        """InferenceEngine::forward_step (src/engine.rs:96-106) with the sampler on
+        the device: the next token for draw u in [0, 1)."""
+        r = np.ascontiguousarray(np.asarray(recent, dtype=np.uint32))
+        out = np.zeros(1, dtype=np.uint32)
+        _check(_lib.lrs_model_forward_sample(self._h, seq, token_id, pos, C.byref(params),
+                                             _uptr(r), r.size, u, _uptr(out)))
+        return int(out[0])
+
     def prefill(self, tokens: Sequence[int], start_pos: int = 0, seq: int = 0,
                 want_logits: bool = True):
         """Prompt pass; returns (last logits, argmax) like the reference's prefill."""
@@ -898,6 +937,11 @@ def write_qwen2_gguf(path: str, desc, alignment: int = 32, retype=None) -> None:
     if d.lm_head.data != d.embed_tokens.data:
         mat("output.weight", d.lm_head)
     write_gguf(path, meta, tensors, alignment)
+
+
+def sampler_check(params: Sampler, vocab: int) -> None:
+    """validate_sampling (src/engine.rs:327-339) plus the device top_k limit."""
+    _check(_lib.lrs_sampler_check(C.byref(params), vocab))
 
 
 def tp_unique_id() -> bytes:

@@ -22,6 +22,7 @@
 #include "decode.cuh"
 #include "gemv.cuh"
 #include "internal.h"
+#include "sample.cuh"
 
 namespace lrs {
 thread_local std::string g_last_error;
@@ -220,6 +221,7 @@ void lrs_backend_destroy(lrs_backend* be) {
   cudaFree(be->d_x);
   cudaFree(be->d_y);
   cudaFree(be->d_scratch);
+  cudaFree(be->d_sample);
   cudaStreamDestroy(be->stream);
   delete be;
 }
@@ -994,6 +996,35 @@ lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens,
     if ((rc = read_argmax(m, item, argmax_out))) return rc;
   }
   return LRS_OK;
+}
+
+lrs_status lrs_model_forward_sample(lrs_model* m, uint32_t seq, uint32_t token, uint32_t pos,
+                                    const lrs_sampler* params, const uint32_t* recent,
+                                    size_t n_recent, float u, uint32_t* next_out) {
+  // InferenceEngine::forward_step, src/engine.rs:96-106: forward_token with
+  // LogitsMode::Compute, then sample_current_logits on the device logits
+  if (!m || !next_out || (n_recent && !recent)) return fail(LRS_ERR_INVALID, "null argument");
+  int32_t rc = lrs_sampler_check(params, m->vocab_full);
+  if (rc) return rc;
+  if (!(u >= 0.0f && u < 1.0f)) return fail(LRS_ERR_INVALID, "u must be in [0, 1)");
+  if (seq >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
+  if ((size_t)pos + 1 > m->opt.max_seq_len)
+    return fail(LRS_ERR_INVALID, "position " + std::to_string(pos) + " exceeds configured context " +
+                                     std::to_string(m->opt.max_seq_len));
+  if (token >= m->vocab_full)
+    return fail(LRS_ERR_INVALID, "token id " + std::to_string(token) + " is outside vocabulary");
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  if ((rc = ensure_pages(m, (int)seq, pos))) return rc;
+  int t = (int)token, p = (int)pos, s = (int)seq;
+  if ((rc = set_items(m, 1, &t, &p, &s))) return rc;
+  if ((rc = enqueue_step(m, 1, 0, true, false, 0))) return rc;
+  uint32_t *d_recent, *d_out;
+  if ((rc = sample_buffers(m->be, recent, n_recent, &d_recent, &d_out))) return rc;
+  LRS_CUDA(launch_sample(m->tp_world > 1 ? m->logits_full : m->logits, (int)m->vocab_full,
+                         d_recent, (int)n_recent, *params, u, d_out, m->be->stream));
+  LRS_CUDA(cudaMemcpyAsync(next_out, d_out, 4, cudaMemcpyDeviceToHost, m->be->stream));
+  LRS_CUDA(cudaStreamSynchronize(m->be->stream));
+  return check_device_error(m->be);
 }
 
 lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t* seqs,

@@ -15,6 +15,8 @@ struct lrs_backend {
   size_t x_cap = 0, y_cap = 0;
   void* d_scratch = nullptr;  // batched tensor-core matmul scratch
   size_t scratch_cap = 0;
+  uint32_t* d_sample = nullptr;  // sampler: [token, recent window...]
+  size_t sample_cap = 0;
 };
 
 struct DevTensor {

@@ -9,6 +9,7 @@
 #include <immintrin.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -685,6 +686,68 @@ int orc_matvec(int kind, int threads, const uint8_t* w, uint32_t t, size_t rows,
   if (cols % bv) return 1;
   matvec(kind, resolve_threads(threads), w, t, rows, cols, x, y);
   return 0;
+}
+
+uint32_t orc_sample(const float* logits, size_t n, const uint32_t* recent, size_t n_recent,
+                    float temperature, float top_p, size_t top_k, float repetition_penalty,
+                    float u, float* margin_out) {
+  // sample_current_logits, src/engine.rs:253-325, step by step.
+  float margin = INFINITY;
+  if (margin_out) *margin_out = margin;
+  if (n == 0) return 0;
+  std::vector<char> seen(n, 0);
+  for (size_t i = 0; i < n_recent; i++)
+    if (recent[i] < n) seen[recent[i]] = 1;
+  std::vector<std::pair<uint32_t, float>> cand;
+  cand.reserve(n);
+  for (size_t t = 0; t < n; t++) {
+    float value = logits[t];
+    if (repetition_penalty != 1.0f && seen[t])
+      value = value > 0.0f ? value / repetition_penalty : value * repetition_penalty;
+    if (temperature > 0.0f) value /= temperature;
+    if (!std::isfinite(value)) value = -INFINITY;
+    cand.emplace_back((uint32_t)t, value);
+  }
+  // sort_unstable_by(|a, b| b.1.total_cmp(&a.1)); equal values: larger index first
+  std::sort(cand.begin(), cand.end(), [](const std::pair<uint32_t, float>& a,
+                                         const std::pair<uint32_t, float>& b) {
+    const int32_t ka = total_key(a.second), kb = total_key(b.second);
+    return ka != kb ? ka > kb : a.first > b.first;
+  });
+  if (temperature <= 0.0f) return cand[0].first;
+  if (top_k > 0 && top_k < cand.size()) cand.resize(top_k);
+  const float mx = cand[0].second;
+  float sum = 0.0f;
+  for (auto& c : cand) {
+    c.second = std::exp(c.second - mx);
+    sum += c.second;
+  }
+  if (!std::isfinite(sum) || sum <= 0.0f) return cand[0].first;
+  for (auto& c : cand) c.second /= sum;
+  float cumulative = 0.0f;
+  size_t cutoff = cand.size();
+  for (size_t i = 0; i < cand.size(); i++) {
+    const float before = cumulative;
+    cumulative += cand[i].second;
+    if (cumulative >= top_p) {
+      cutoff = i + 1;
+      margin = std::min(margin, std::min(cumulative - top_p, top_p - before));
+      break;
+    }
+  }
+  float kept_sum = 0.0f;
+  for (size_t i = 0; i < cutoff; i++) kept_sum += cand[i].second;
+  float random = u * kept_sum;
+  for (size_t i = 0; i < cutoff; i++) {
+    const float before = random;
+    random -= cand[i].second;
+    if (random <= 0.0f) {
+      if (margin_out) *margin_out = std::min(margin, std::min(before, -random));
+      return cand[i].first;
+    }
+  }
+  if (margin_out) *margin_out = std::min(margin, std::fabs(random));
+  return cand[cutoff - 1].first;
 }
 
 uint32_t orc_argmax(const float* logits, size_t n) {

@@ -51,6 +51,19 @@ int orc_benchmark_tokens(orc_model* m, const uint32_t* prompt, size_t n, size_t 
                          double* prefill_s, double* decode_s);
 /* Greedy argmax of the reference (last maximal index under f32::total_cmp). */
 uint32_t orc_argmax(const float* logits, size_t n);
+/* InferenceEngine::sample_current_logits (src/engine.rs:253-325) over `n`
+ * logits with the recent-token window `recent` (the seen flags), and the
+ * uniform draw `u` in [0, 1) that the reference takes from
+ * rand::thread_rng().gen::<f32>().  Equal values, whose order
+ * sort_unstable_by leaves unspecified, are ordered larger index first.
+ * *margin_out (may be NULL) receives the smallest distance, in probability
+ * units, between a decision and its boundary (the top-p cutoff and the draw);
+ * +inf when no such decision was made.  No reference test covers this
+ * function: it is pinned to the source only (tests/test_sampler.py restates
+ * it again in Python). */
+uint32_t orc_sample(const float* logits, size_t n, const uint32_t* recent, size_t n_recent,
+                    float temperature, float top_p, size_t top_k, float repetition_penalty,
+                    float u, float* margin_out);
 const char* orc_last_error(void);
 
 #ifdef __cplusplus

@@ -49,6 +49,8 @@ def _load():
     sig("orc_benchmark_tokens", C.c_int, P, U32, C.c_size_t, C.c_size_t, U32, F, F,
         C.POINTER(C.c_double), C.POINTER(C.c_double))
     sig("orc_argmax", C.c_uint32, F, C.c_size_t)
+    sig("orc_sample", C.c_uint32, F, C.c_size_t, U32, C.c_size_t, C.c_float, C.c_float,
+        C.c_size_t, C.c_float, C.c_float, F)
     sig("orc_last_error", C.c_char_p)
     return lib
 
@@ -110,6 +112,18 @@ def matvec(kind: int, data: np.ndarray, ggml_type: int, rows: int, cols: int, x:
 
 def avx2_available() -> bool:
     return bool(_lib.orc_avx2_available())
+
+
+def sample(logits: np.ndarray, recent, temperature: float, top_p: float, top_k: int,
+           repetition_penalty: float, u: float):
+    """sample_current_logits (src/engine.rs:253-325) with the draw u in [0, 1):
+    (token, distance of its decisions from their boundaries)."""
+    l = np.ascontiguousarray(logits, dtype=np.float32)
+    r = np.ascontiguousarray(np.asarray(recent, dtype=np.uint32))
+    m = np.zeros(1, np.float32)
+    tok = _lib.orc_sample(_f(l), l.size, _u(r), r.size, temperature, top_p, top_k,
+                          repetition_penalty, u, _f(m))
+    return int(tok), float(m[0])
 
 
 def argmax(logits: np.ndarray) -> int:
