@@ -62,14 +62,18 @@ __host__ __device__ constexpr int tile_b(int ni) { return 2 * ni * kKC * 2; }
 __host__ __device__ constexpr int tile_bmin(int ni) { return 2 * ni * 16 * 2; }
 constexpr int kTileMin = 128 * 16 * 2;   // 4 KB (A_min or B_min)
 constexpr int kSBO = (kKC / 8) * 128;    // 2048
-constexpr int kThreads = 416;  // 8 producer warps (2 per row), 4 epilogue warps, 1 issuer
 constexpr uint32_t kTmemCols = 512;
 
 // Per-type pipeline shape.  Q4_K: one A tile (sc*q) per half super-block plus
 // the A_min MMA; three A and three x buffers.  Q6_K: two A tiles per half
 // super-block, (q-32)*(sc & 15) and (q-32)*(sc - (sc & 15)), both exact in
 // f16, accumulated into the same TMEM columns; two A and two x buffers.
-template <int T, int NI>
+//
+// RAW (Q4_K only, opt-in): a loader warp copies each super-block's 128 raw
+// rows (144 bytes each, 16-byte aligned) into a two-stage shared-memory ring
+// with cp.async.bulk, and the producers decode from there instead of holding
+// the next super-block in registers; two x buffers make the room.
+template <int T, int NI, bool RAW = false>
 struct TcShape {
   static constexpr int kN = 2 * NI;
   static constexpr int kTileB = tile_b(NI);
@@ -77,14 +81,20 @@ struct TcShape {
   static constexpr bool kMins = T == LRS_GGML_Q4_K;
   static constexpr int kAParts = T == LRS_GGML_Q6_K ? 2 : 1;  // A tiles per half step
   static constexpr int kAB = T == LRS_GGML_Q6_K ? 2 : 3;      // A buffers
-  static constexpr int kBB = T == LRS_GGML_Q6_K ? 2 : 3;      // x buffers
+  static constexpr int kBB = T == LRS_GGML_Q6_K || RAW ? 2 : 3;  // x buffers
+  static constexpr int kRawStages = RAW ? 2 : 0;
+  static constexpr int kRawStage = kRows * 144;  // one super-block of 128 Q4_K rows
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kAB * kAParts * kTileA;
   static constexpr int kOffAmin = kOffB + kBB * kTileB;
   static constexpr int kOffBmin = kOffAmin + (kMins ? 2 * kTileMin : 0);
-  static constexpr int kOffBar = kOffBmin + (kMins ? 2 * kTileBmin : 0);
-  static constexpr int kSmem = kOffBar + 128;
+  static constexpr int kOffRaw = kOffBmin + (kMins ? 2 * kTileBmin : 0);
+  static constexpr int kOffBar = kOffRaw + kRawStages * kRawStage;
+  static constexpr int kSmem = kOffBar + (RAW ? 256 : 128);
   static constexpr int kBytes = T == LRS_GGML_Q6_K ? 210 : 144;
+  static constexpr int kThreads = RAW ? 448 : 416;  // + the raw loader warp
+  static_assert(!RAW || T == LRS_GGML_Q4_K, "the raw ring needs 16-byte aligned rows (Q4_K)");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -332,9 +342,10 @@ struct Raw<LRS_GGML_Q6_K> {
   }
 };
 
-template <int T, int NI, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
-  using S = TcShape<T, NI>;
+template <int T, int NI, bool FUSED, bool RAW>
+__global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ TcArgs a) {
+  using S = TcShape<T, NI, RAW>;
   constexpr int kN = S::kN, kTileB = S::kTileB;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
@@ -344,6 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   uint64_t* mma_done = bars + 6;    // [kAB] MMAs of a half step finished (A, x buffers free)
   uint64_t* acc_full = bars + 9;    // [2] super-block accumulator ready
   uint64_t* acc_empty = bars + 11;  // [2] epilogue finished reading it
+  uint64_t* raw_full = bars + 13;   // [2] RAW: a super-block's rows landed
+  uint64_t* raw_empty = bars + 15;  // [2] RAW: the producers finished with them
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = smem_u32(smem);
 
@@ -356,6 +369,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
+      if (RAW) {
+        mbar_init(&raw_full[i], 1);
+        mbar_init(&raw_empty[i], 256);
+      }
     }
     fence_barrier_init();
   }
@@ -385,12 +402,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int r = tid & 127, c = tid >> 7;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
     Raw<T> cur, nxt;
-    if (nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
+    if (!RAW && nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
     for (int sb = 0; sb < nsb && ok; sb++) {
-      if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
-      if (sb + 2 < nsb) {  // two super-blocks ahead into L2
-        const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
-        if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
+      if constexpr (RAW) {
+        // this super-block's rows from the ring (row r at r * 144: conflict-free)
+        const int rs = sb & 1;
+        ok = mbar_wait_bounded(&raw_full[rs], (uint32_t)((sb >> 1) & 1));
+        if (!ok) break;
+        const uint8_t* u = smem + S::kOffRaw + rs * S::kRawStage + r * 144;
+        cur.v[0] = *reinterpret_cast<const uint4*>(u);
+        cur.v[1] = *reinterpret_cast<const uint4*>(u + 16 + 32 * c);
+        cur.v[2] = *reinterpret_cast<const uint4*>(u + 32 + 32 * c);
+        cur.v[3] = *reinterpret_cast<const uint4*>(u + 80 + 32 * c);
+        cur.v[4] = *reinterpret_cast<const uint4*>(u + 96 + 32 * c);
+        mbar_arrive(&raw_empty[rs]);  // the values are in registers now
+      } else {
+        if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
+        if (sb + 2 < nsb) {  // two super-blocks ahead into L2
+          const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
+          if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
+        }
       }
 #pragma unroll
       for (int half = 0; half < 2; half++) {
@@ -483,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         fence_proxy_async();
         mbar_arrive(&a_full[ab]);
       }
-      cur = nxt;
+      if (!RAW) cur = nxt;
     }
   } else if (warp < 12) {
     // ---------------- epilogue: TMEM -> per-item sums ----------------
@@ -590,7 +621,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
     }
     if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
-  } else if (lane == 0) {
+  } else if (RAW && warp == 13) {
+    // ---------------- raw loader: super-block rows into the ring ----------------
+    const uint64_t pol = evict_first_policy();
+    for (int sb = 0; sb < nsb && ok; sb++) {
+      const int rs = sb & 1;
+      if (sb >= 2) {
+        if (lane == 0) ok = mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((sb - 2) >> 1) & 1));
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
+      if (lane == 0) mbar_expect_tx(&raw_full[rs], (uint32_t)S::kRawStage);
+      __syncwarp();
+      uint8_t* dst = smem + S::kOffRaw + rs * S::kRawStage;
+#pragma unroll
+      for (int k = 0; k < kRows / 32; k++) {
+        const int rr = lane + 32 * k;
+        const uint8_t* src =
+            a.w + (size_t)min(row0 + rr, a.rows - 1) * a.rb + (size_t)(s0 + sb) * 144;
+        tma_load_1d(dst + rr * 144, src, 144, &raw_full[rs], pol);
+      }
+    }
+    if (!ok && lane == 0 && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+  } else if (warp == 12 && lane == 0) {
     // ---------------- issuer: x copies and MMAs ----------------
     const uint64_t pol = evict_first_policy();
     constexpr uint32_t idesc = idesc_f16(kRows, kN);
@@ -671,25 +724,25 @@ int tc_kgroups(const GemvParams& p, int sms) {
   return ctas >= sms ? 1 : std::max(1, std::min(nsb, sms / ctas));
 }
 
-template <int T, int NI, bool FUSED>
+template <int T, int NI, bool FUSED, bool RAW = false>
 cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
+  using S = TcShape<T, NI, RAW>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI, FUSED>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcShape<T, NI>::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI, FUSED, RAW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   if constexpr (!FUSED) {
-    gemm_tc_kernel<T, NI, false><<<grid, kThreads, TcShape<T, NI>::kSmem, st>>>(a);
+    gemm_tc_kernel<T, NI, false, RAW><<<grid, S::kThreads, S::kSmem, st>>>(a);
     return cudaGetLastError();
   }
   // programmatic dependent launch: the producers start while xsplit_tc_kernel runs
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = TcShape<T, NI>::kSmem;
+  cfg.blockDim = dim3(S::kThreads);
+  cfg.dynamicSmemBytes = S::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr1[1];
   attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -697,16 +750,22 @@ cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
   cfg.attrs = attr1;
   cfg.numAttrs = 1;
   void* args[] = {const_cast<TcArgs*>(&a)};
-  return cudaLaunchKernelExC(&cfg, (const void*)gemm_tc_kernel<T, NI, FUSED>, args);
+  return cudaLaunchKernelExC(&cfg, (const void*)gemm_tc_kernel<T, NI, FUSED, RAW>, args);
 }
 
 template <int NI>
 cudaError_t launch_tc_type(int type, const TcArgs& a, dim3 grid, cudaStream_t st) {
-  if (a.pdl)
-    return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI, true>(a, grid, st)
-                                 : launch_tc<LRS_GGML_Q4_K, NI, true>(a, grid, st);
-  return type == LRS_GGML_Q6_K ? launch_tc<LRS_GGML_Q6_K, NI, false>(a, grid, st)
-                               : launch_tc<LRS_GGML_Q4_K, NI, false>(a, grid, st);
+  // LRS_TC_RAW=1: Q4_K through the raw-row ring
+  const char* rv = getenv("LRS_TC_RAW");
+  const bool raw = rv && rv[0] == '1';
+  if (type == LRS_GGML_Q6_K)
+    return a.pdl ? launch_tc<LRS_GGML_Q6_K, NI, true>(a, grid, st)
+                 : launch_tc<LRS_GGML_Q6_K, NI, false>(a, grid, st);
+  if (raw)
+    return a.pdl ? launch_tc<LRS_GGML_Q4_K, NI, true, true>(a, grid, st)
+                 : launch_tc<LRS_GGML_Q4_K, NI, false, true>(a, grid, st);
+  return a.pdl ? launch_tc<LRS_GGML_Q4_K, NI, true>(a, grid, st)
+               : launch_tc<LRS_GGML_Q4_K, NI, false>(a, grid, st);
 }
 }  // namespace
 

@@ -1,4 +1,5 @@
-"""GPU parity of the tcgen05 matmul with its output step fused (LRS_TC_FUSED=1).
+"""GPU parity of the tcgen05 matmul with its output step fused (LRS_TC_FUSED=1)
+and with Q4_K rows streamed through a shared-memory ring (LRS_TC_RAW=1).
 
 The fused kernel adds the K-group partials in the order of the separate
 epilogue kernel (in the CTA that finishes last for its row block) and applies
@@ -10,7 +11,8 @@ one and several K-groups, Q4_K and Q6_K, every epilogue through the model
 (q4k recipe: Q4_K LM head with the argmax in the matmul), and the backend's
 own scratch (matvec_batched).
 
-Selected per launch by LRS_TC_FUSED=1; runs when LRS_TEST_NEW_KERNELS=1.
+Selected per launch by LRS_TC_FUSED=1 / LRS_TC_RAW=1; runs when
+LRS_TEST_NEW_KERNELS=1.
 """
 import os
 
@@ -26,9 +28,13 @@ TOL = 1e-3
 LOGIT_TOL = 2e-2
 
 
-@pytest.fixture(autouse=True)
-def fused_on(monkeypatch):
-    monkeypatch.setenv("LRS_TC_FUSED", "1")
+@pytest.fixture(autouse=True, params=["fused", "fused+raw", "raw"])
+def fused_on(monkeypatch, request):
+    # the fused output step, the raw-row ring for Q4_K (LRS_TC_RAW=1), and both
+    if "fused" in request.param:
+        monkeypatch.setenv("LRS_TC_FUSED", "1")
+    if "raw" in request.param:
+        monkeypatch.setenv("LRS_TC_RAW", "1")
 
 
 def _check_rows(got, ref):
