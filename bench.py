@@ -32,9 +32,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
 # Opt-in kernels (read by the library at launch time): the bulk-copy batch-1
-# GEMV and the streamed decode attention.
+# GEMV, the streamed decode attention, the tcgen05 matmul's fused output step
+# and its raw-row ring.
 STREAM_GEMV = os.environ.get("LRS_GEMV_STREAM") == "1"
 ATTN_V3 = os.environ.get("LRS_ATTN_V3") == "1"
+TC_FUSED = os.environ.get("LRS_TC_FUSED") == "1"
+TC_RAW = os.environ.get("LRS_TC_RAW") == "1"
 
 def load_pkg():
     import importlib.util
@@ -186,7 +189,9 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
             "sequences_per_gpu": total_seqs if tp else total_seqs // max(world, 1), "prompt": P,
             "kv_cache": "bf16" if kv_bf16 else "f32",
             "kernels": {"gemv_b1": "stream" if STREAM_GEMV else "direct",
-                        "attention": "v3" if ATTN_V3 else "v2"}}
+                        "attention": "v3" if ATTN_V3 else "v2",
+                        "matmul_tc": "+".join(["tcgen05"] + (["fused"] if TC_FUSED else []) +
+                                              (["raw"] if TC_RAW else []))}}
 
 
 def run_reference(args, wl):
