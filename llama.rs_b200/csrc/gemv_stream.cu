@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kStreamThreads)
       float bias;
       float* out;
       int row;
-      bool live;
+      bool live, has_bias;
     };
     auto gather = [&](int j) {
       Rows e;
@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(kStreamThreads)
       }
       e.row = r0 + lane;
       e.out = sg.out ? sg.out + e.row : nullptr;
-      e.bias = (p.epi == EPI_STORE && sg.bias) ? __ldg(sg.bias + e.row) : 0.0f;
+      e.has_bias = p.epi == EPI_STORE && sg.bias;
+      e.bias = e.has_bias ? __ldg(sg.bias + e.row) : 0.0f;
       e.live = true;
       return e;
     };
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(kStreamThreads)
       if (!e.live) return;
       switch (p.epi) {
         case EPI_STORE:
-          *e.out = e.y[0] + e.bias;
+          *e.out = e.has_bias ? e.y[0] + e.bias : e.y[0];
           break;
         case EPI_ADD:
           // the only update of this element in the launch: one rounding, as
