@@ -218,6 +218,14 @@ _sig("lrs_synth_fill", None, C.c_uint64, C.c_char_p, C.c_float, C.c_uint64, C.c_
 _sig("lrs_synth_model_create", C.c_int32, C.POINTER(_SynthSpec), C.POINTER(_P))
 _sig("lrs_synth_model_desc", C.POINTER(_ModelDesc), _P)
 _sig("lrs_synth_model_destroy", None, _P)
+_sig("lrs_st_open", C.c_int32, C.c_char_p, C.POINTER(_P))
+_sig("lrs_st_close", None, _P)
+_sig("lrs_st_tensor_count", C.c_size_t, _P)
+_sig("lrs_st_tensor", C.c_int32, _P, C.c_char_p, C.POINTER(_TensorDesc))
+_sig("lrs_st_qwen2_desc", C.c_int32, _P, C.c_uint32, C.POINTER(C.POINTER(_ModelDesc)))
+_sig("lrs_model_load", C.c_int32, C.c_char_p, C.c_uint32, C.POINTER(_P),
+     C.POINTER(C.POINTER(_ModelDesc)))
+_sig("lrs_loaded_close", None, _P)
 _sig("lrs_sampler_check", C.c_int32, C.POINTER(Sampler), C.c_size_t)
 _sig("lrs_sample_logits", C.c_int32, _P, C.c_void_p, C.c_size_t, C.POINTER(Sampler), _U32,
      C.c_size_t, C.c_float, _U32)
@@ -240,6 +248,8 @@ EXPORTED_SYMBOLS = (
     "lrs_gguf_qwen2_desc", "lrs_recipe_type", "lrs_quantize_matrix", "lrs_quantized_size",
     "lrs_synth_fill", "lrs_synth_model_create", "lrs_synth_model_desc", "lrs_synth_model_destroy",
     "lrs_sampler_check", "lrs_sample_logits", "lrs_model_forward_sample",
+    "lrs_st_open", "lrs_st_close", "lrs_st_tensor_count", "lrs_st_tensor", "lrs_st_qwen2_desc",
+    "lrs_model_load", "lrs_loaded_close",
 )
 
 
@@ -937,6 +947,179 @@ def write_qwen2_gguf(path: str, desc, alignment: int = 32, retype=None) -> None:
     if d.lm_head.data != d.embed_tokens.data:
         mat("output.weight", d.lm_head)
     write_gguf(path, meta, tensors, alignment)
+
+
+class SafetensorsFile:
+    """SafetensorStore (src/loader.rs:535-645) over the C reader: a model
+    directory's shards, tensor views, and the description of
+    SafetensorsLoader::load (src/loader.rs:83-230) for lrs_model_create."""
+
+    def __init__(self, model_dir: str):
+        h = _P()
+        _check(_lib.lrs_st_open(os.fsencode(model_dir), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            _lib.lrs_st_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def tensor_count(self) -> int:
+        return int(_lib.lrs_st_tensor_count(self._h))
+
+    def tensor(self, name: str) -> QuantTensor:
+        td = _TensorDesc()
+        _check(_lib.lrs_st_tensor(self._h, name.encode(), C.byref(td)))
+        buf = (C.c_uint8 * td.nbytes).from_address(td.data) if td.nbytes else b""
+        return QuantTensor(np.frombuffer(buf, dtype=np.uint8), (td.rows, td.cols),
+                           QuantType(td.ggml_type))
+
+    def qwen2_desc(self, recipe: LoadQuantization = LoadQuantization.NONE):
+        """The model description (valid while this object lives)."""
+        out = C.POINTER(_ModelDesc)()
+        _check(_lib.lrs_st_qwen2_desc(self._h, int(recipe), C.byref(out)))
+        return out
+
+
+class LoadedModel:
+    """ModelLoader::load (src/loader.rs:46-79): a .gguf file, a .safetensors
+    file or a model directory, by the reference's format detection."""
+
+    def __init__(self, path: str, recipe: LoadQuantization = LoadQuantization.NONE):
+        h = _P()
+        d = C.POINTER(_ModelDesc)()
+        _check(_lib.lrs_model_load(os.fsencode(path), int(recipe), C.byref(h), C.byref(d)))
+        self._h = h
+        self._desc = d
+
+    def desc(self):
+        return self._desc
+
+    def close(self):
+        if self._h:
+            _lib.lrs_loaded_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_ST_DTYPES = {"F32": (np.float32, 4), "F16": (np.float16, 2), "BF16": (None, 2)}
+
+
+def write_safetensors(path: str, tensors, metadata=None) -> None:
+    """Writes a .safetensors file: tensors = [(name, dtype, shape, bytes)],
+    data in the listed order; metadata: optional {str: str}."""
+    import json
+    import struct
+    header = {}
+    off = 0
+    for name, dtype, shape, data in tensors:
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + len(data)]}
+        off += len(data)
+    if metadata:
+        header["__metadata__"] = dict(metadata)
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for _, _, _, data in tensors:
+            f.write(data)
+
+
+def _f32_to(values: np.ndarray, dtype: str) -> bytes:
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    if dtype == "F32":
+        return v.tobytes()
+    if dtype == "F16":
+        return v.astype(np.float16).tobytes()
+    b = v.view(np.uint32)  # BF16, round to nearest even
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    r = np.where(np.isnan(v), (b >> 16).astype(np.uint16) | 0x40, r)
+    return r.tobytes()
+
+
+def write_qwen2_safetensors(model_dir: str, desc, dtype: str = "F32", shards: int = 1,
+                            config_extra=None) -> None:
+    """Writes the F32 model behind an lrs_model_desc as a Hugging Face Qwen2
+    directory (config.json, model.safetensors or `shards` files with
+    model.safetensors.index.json), tensors in `dtype` (F32, F16 or BF16); a
+    tied head is written without lm_head.weight."""
+    import json
+    d = desc.contents
+    c = d.config
+    h, kvw = c.hidden_size, c.num_key_value_heads * c.head_dim
+    os.makedirs(model_dir, exist_ok=True)
+    tensors = []
+
+    def f32(ptr, n):
+        return np.frombuffer((C.c_float * n).from_address(ptr), dtype=np.float32)
+
+    def mat(name, td):
+        if td.ggml_type != int(QuantType.F32):
+            raise LrsError(1, f"{name}: write_qwen2_safetensors takes an F32 model")
+        tensors.append((name, dtype, [td.rows, td.cols], _f32_to(f32(td.data, td.rows * td.cols), dtype)))
+
+    def vec(name, ptr, n):
+        if ptr:
+            tensors.append((name, dtype, [n], _f32_to(f32(ptr, n), dtype)))
+
+    mat("model.embed_tokens.weight", d.embed_tokens)
+    vec("model.norm.weight", d.final_norm, h)
+    for i in range(c.num_hidden_layers):
+        L, p = d.layers[i], f"model.layers.{i}"
+        vec(f"{p}.input_layernorm.weight", L.input_layernorm, h)
+        vec(f"{p}.post_attention_layernorm.weight", L.post_attention_layernorm, h)
+        mat(f"{p}.self_attn.q_proj.weight", L.q_proj)
+        vec(f"{p}.self_attn.q_proj.bias", L.q_bias, h)
+        mat(f"{p}.self_attn.k_proj.weight", L.k_proj)
+        vec(f"{p}.self_attn.k_proj.bias", L.k_bias, kvw)
+        mat(f"{p}.self_attn.v_proj.weight", L.v_proj)
+        vec(f"{p}.self_attn.v_proj.bias", L.v_bias, kvw)
+        mat(f"{p}.self_attn.o_proj.weight", L.o_proj)
+        mat(f"{p}.mlp.gate_proj.weight", L.gate_proj)
+        mat(f"{p}.mlp.up_proj.weight", L.up_proj)
+        mat(f"{p}.mlp.down_proj.weight", L.down_proj)
+    tied = d.lm_head.data == d.embed_tokens.data
+    if not tied:
+        mat("lm_head.weight", d.lm_head)
+    cfg = {"model_type": "qwen2", "architectures": ["Qwen2ForCausalLM"],
+           "hidden_size": c.hidden_size, "intermediate_size": c.intermediate_size,
+           "num_attention_heads": c.num_attention_heads,
+           "num_key_value_heads": c.num_key_value_heads,
+           "num_hidden_layers": c.num_hidden_layers, "vocab_size": c.vocab_size,
+           "rms_norm_eps": float(np.float32(c.rms_norm_eps)),
+           "rope_theta": float(np.float32(c.rope_theta)),
+           "max_position_embeddings": c.max_position_embeddings,
+           "tie_word_embeddings": bool(tied), "torch_dtype": "float32"}
+    if config_extra:
+        cfg.update(config_extra)
+    with open(os.path.join(model_dir, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=2)
+    if shards <= 1:
+        write_safetensors(os.path.join(model_dir, "model.safetensors"), tensors)
+        return
+    per = (len(tensors) + shards - 1) // shards
+    weight_map = {}
+    for k in range(shards):
+        fname = f"model-{k + 1:05d}-of-{shards:05d}.safetensors"
+        part = tensors[k * per:(k + 1) * per]
+        write_safetensors(os.path.join(model_dir, fname), part)
+        weight_map.update({t[0]: fname for t in part})
+    with open(os.path.join(model_dir, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": sum(len(t[3]) for t in tensors)},
+                   "weight_map": weight_map}, f)
 
 
 def sampler_check(params: Sampler, vocab: int) -> None:

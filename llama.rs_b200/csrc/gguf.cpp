@@ -17,6 +17,7 @@
 #include "../../include/llamars_gguf.h"
 #include "../../include/llamars_synth.h"
 #include "common.h"
+#include "load_common.h"
 
 namespace {
 
@@ -173,31 +174,6 @@ struct Reader {
 };
 
 // Exact f16 -> f32 (`half` crate semantics: every f16 value is exact in f32).
-float f16_to_f32(uint16_t h) {
-  const uint32_t sign = (uint32_t)(h & 0x8000) << 16, exp = (h >> 10) & 0x1F, man = h & 0x3FF;
-  uint32_t bits;
-  if (exp == 0) {
-    if (man == 0) {
-      bits = sign;
-    } else {  // subnormal: normalise
-      int e = -1;
-      uint32_t m = man;
-      do {
-        e++;
-        m <<= 1;
-      } while ((m & 0x400) == 0);
-      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((m & 0x3FF) << 13);
-    }
-  } else if (exp == 31) {
-    bits = sign | 0x7F800000u | (man << 13);
-  } else {
-    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
-  }
-  float f;
-  memcpy(&f, &bits, 4);
-  return f;
-}
-
 }  // namespace
 
 struct lrs_gguf {
@@ -209,7 +185,7 @@ struct lrs_gguf {
   std::map<std::string, TensorInfo> tensors;
   size_t data_offset = 0;
   // owned by a built description
-  std::vector<std::unique_ptr<std::vector<uint8_t>>> blobs;
+  lrs::Blobs blobs;
   std::vector<std::unique_ptr<std::vector<float>>> vecs;
   std::vector<lrs_layer_desc> layers;
   lrs_model_desc desc{};
@@ -331,37 +307,6 @@ std::string shape_str(const lrs_tensor_desc& d, bool one_d) {
                : "[" + std::to_string(d.rows) + ", " + std::to_string(d.cols) + "]";
 }
 
-// QuantTensor::to_vec_f32 for the float types a norm vector or a float
-// matrix comes in (value_at, src/quant.rs:349-360).
-int32_t to_f32(const lrs_tensor_desc& d, const std::string& name, std::vector<float>* out) {
-  const size_t n = d.rows * d.cols;
-  out->resize(n);
-  const uint8_t* p = static_cast<const uint8_t*>(d.data);
-  switch (d.ggml_type) {
-    case LRS_GGML_F32:
-      memcpy(out->data(), p, n * 4);
-      return LRS_OK;
-    case LRS_GGML_F16:
-      for (size_t i = 0; i < n; i++) {
-        uint16_t h;
-        memcpy(&h, p + 2 * i, 2);
-        (*out)[i] = f16_to_f32(h);
-      }
-      return LRS_OK;
-    case LRS_GGML_BF16:
-      for (size_t i = 0; i < n; i++) {
-        uint16_t h;
-        memcpy(&h, p + 2 * i, 2);
-        const uint32_t b = (uint32_t)h << 16;
-        memcpy(&(*out)[i], &b, 4);
-      }
-      return LRS_OK;
-  }
-  return fail(LRS_ERR_UNSUPPORTED,
-              "tensor " + name + ": " + lrs::type_name(d.ggml_type) +
-                  " vectors are not supported by the CUDA backend's GGUF loader");
-}
-
 }  // namespace
 
 extern "C" {
@@ -475,32 +420,7 @@ lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_des
       return fail(LRS_ERR_INVALID, "tensor " + name + " has shape " + shape_str(*d, one_d) +
                                        ", expected [" + std::to_string(rows) + ", " +
                                        std::to_string(cols) + "]");
-    const uint32_t t = d->ggml_type;
-    if (recipe == LRS_RECIPE_NONE ||
-        (t != LRS_GGML_F32 && t != LRS_GGML_F16 && t != LRS_GGML_BF16))
-      return LRS_OK;  // a view into the mapping
-    std::vector<float> v;
-    if ((r2 = to_f32(*d, name, &v))) return r2;
-    const uint32_t qt = lrs_recipe_type(recipe, name.c_str(), rows, cols);
-    if (qt == LRS_GGML_F32) {  // the encoders' fallback keeps f32
-      auto buf = std::make_unique<std::vector<uint8_t>>(v.size() * 4);
-      memcpy(buf->data(), v.data(), buf->size());
-      d->data = buf->data();
-      d->nbytes = buf->size();
-      d->ggml_type = LRS_GGML_F32;
-      g->blobs.push_back(std::move(buf));
-      return LRS_OK;
-    }
-    auto buf = std::make_unique<std::vector<uint8_t>>(lrs_quantized_size(qt, rows, cols));
-    uint32_t made;
-    size_t len;
-    if ((r2 = lrs_quantize_matrix(qt, v.data(), rows, cols, buf->data(), buf->size(), &made, &len)))
-      return r2;
-    d->data = buf->data();
-    d->nbytes = len;
-    d->ggml_type = made;
-    g->blobs.push_back(std::move(buf));
-    return LRS_OK;
+    return lrs::maybe_quantize_desc(recipe, name, rows, cols, d, &g->blobs, "GGUF");
   };
   // load_gguf_vector (src/loader.rs:509-517)
   auto vector = [&](const std::string& name, size_t len, const float** outp) -> int32_t {
@@ -512,7 +432,7 @@ lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_des
       return fail(LRS_ERR_INVALID, "tensor " + name + " has shape " + shape_str(d, one_d) +
                                        ", expected [" + std::to_string(len) + "]");
     auto v = std::make_unique<std::vector<float>>();
-    if ((r2 = to_f32(d, name, v.get()))) return r2;
+    if ((r2 = lrs::desc_to_f32(d, name, v.get(), "GGUF"))) return r2;
     *outp = v->data();
     g->vecs.push_back(std::move(v));
     return LRS_OK;

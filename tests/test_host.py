@@ -12,7 +12,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _declared_symbols():
     names = set()
-    for h in ("llamars.h", "llamars_synth.h", "llamars_gguf.h", "llamars_sample.h"):
+    for h in ("llamars.h", "llamars_synth.h", "llamars_gguf.h", "llamars_sample.h",
+              "llamars_safetensors.h"):
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         names.update(re.findall(r"\b(lrs_[a-z0-9_]+)\s*\(", src))
