@@ -38,6 +38,7 @@ STREAM_GEMV = os.environ.get("LRS_GEMV_STREAM") == "1"
 ATTN_V3 = os.environ.get("LRS_ATTN_V3") == "1"
 TC_FUSED = os.environ.get("LRS_TC_FUSED") == "1"
 TC_RAW = os.environ.get("LRS_TC_RAW") == "1"
+TP_P2P = os.environ.get("LRS_TP_P2P") == "1"
 
 def load_pkg():
     import importlib.util
@@ -191,7 +192,8 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
             "kernels": {"gemv_b1": "stream" if STREAM_GEMV else "direct",
                         "attention": "v3" if ATTN_V3 else "v2",
                         "matmul_tc": "+".join(["tcgen05"] + (["fused"] if TC_FUSED else []) +
-                                              (["raw"] if TC_RAW else []))}}
+                                              (["raw"] if TC_RAW else [])),
+                        "tp_allreduce": "p2p" if TP_P2P else "nccl"}}
 
 
 def run_reference(args, wl):

@@ -23,6 +23,7 @@
 #include "gemv.cuh"
 #include "internal.h"
 #include "sample.cuh"
+#include "tp_p2p.cuh"
 
 namespace lrs {
 thread_local std::string g_last_error;
@@ -379,6 +380,16 @@ struct lrs_model {
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
   int* attn_cnt = nullptr;  // [max_items][kv heads] split counters of the attention combine
+  // tensor parallelism over peer memory (LRS_TP_P2P=1): exchange buffers
+  // [2][max_items * hidden], signal words [world], a launch counter, and the
+  // device arrays of every rank's (IPC-mapped) pointers
+  bool tp_p2p = false;
+  float* xbuf = nullptr;
+  int* tp_sig = nullptr;
+  unsigned* tp_tickets = nullptr;
+  const float** d_parts = nullptr;  // [2][world]
+  int** d_peer_sig = nullptr;       // [world]
+  std::vector<void*> ipc_opened;
   float* act2 = nullptr;    // up projection when a layer's gate and up differ in type
   void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
   // tensor parallelism: this process holds shard tp_rank of tp_world
@@ -449,6 +460,66 @@ int32_t upload_mat(const lrs_tensor_desc& d, size_t rows, size_t cols, const cha
   return upload(d.data, d.nbytes, rows, cols, d.ggml_type, out);
 }
 
+bool tp_p2p_requested() {
+  const char* e = getenv("LRS_TP_P2P");
+  return e && e[0] == '1';
+}
+
+// The peer-memory all-reduce: every rank allocates its exchange buffers and
+// signal words, the ranks swap CUDA IPC handles with one NCCL all-gather, and
+// each rank maps its peers' allocations (collective: all ranks call it).
+int32_t setup_tp_p2p(lrs_model* m, int h) {
+  const int world = m->tp_world, rank = m->tp_rank;
+  cudaStream_t st = m->be->stream;
+  const size_t xcount = 2 * (size_t)m->max_items * h;
+  // own cudaMalloc allocations: an IPC handle names the base of an allocation
+  LRS_CUDA(cudaMalloc((void**)&m->xbuf, xcount * 4));
+  m->allocs.push_back(m->xbuf);
+  LRS_CUDA(cudaMalloc((void**)&m->tp_sig, 256));
+  m->allocs.push_back(m->tp_sig);
+  LRS_CUDA(cudaMemset(m->tp_sig, 0, 256));
+  int32_t rc;
+  if ((rc = model_alloc(m, (void**)&m->tp_tickets, 4))) return rc;
+  LRS_CUDA(cudaMemset(m->tp_tickets, 0, 4));
+  cudaIpcMemHandle_t mine[2];
+  LRS_CUDA(cudaIpcGetMemHandle(&mine[0], m->xbuf));
+  LRS_CUDA(cudaIpcGetMemHandle(&mine[1], m->tp_sig));
+  uint8_t* d_hs = nullptr;
+  if ((rc = model_alloc(m, (void**)&d_hs, sizeof(mine) * (world + 1)))) return rc;
+  LRS_CUDA(cudaMemcpy(d_hs, mine, sizeof(mine), cudaMemcpyHostToDevice));
+  LRS_NCCL(nccl().AllGather(d_hs, d_hs + sizeof(mine), sizeof(mine), ncclInt8, m->comm, st));
+  std::vector<cudaIpcMemHandle_t> all(2 * (size_t)world);
+  LRS_CUDA(cudaMemcpyAsync(all.data(), d_hs + sizeof(mine), sizeof(mine) * world,
+                           cudaMemcpyDeviceToHost, st));
+  LRS_CUDA(cudaStreamSynchronize(st));
+  std::vector<const float*> parts(2 * (size_t)world);
+  std::vector<int*> sigs(world);
+  for (int p = 0; p < world; p++) {
+    float* x = m->xbuf;
+    int* g = m->tp_sig;
+    if (p != rank) {
+      void* px = nullptr;
+      void* pg = nullptr;
+      LRS_CUDA(cudaIpcOpenMemHandle(&px, all[2 * p], cudaIpcMemLazyEnablePeerAccess));
+      m->ipc_opened.push_back(px);
+      LRS_CUDA(cudaIpcOpenMemHandle(&pg, all[2 * p + 1], cudaIpcMemLazyEnablePeerAccess));
+      m->ipc_opened.push_back(pg);
+      x = static_cast<float*>(px);
+      g = static_cast<int*>(pg);
+    }
+    parts[p] = x;
+    parts[world + p] = x + (size_t)m->max_items * h;
+    sigs[p] = g;
+  }
+  if ((rc = model_alloc(m, (void**)&m->d_parts, parts.size() * sizeof(float*))) ||
+      (rc = model_alloc(m, (void**)&m->d_peer_sig, sigs.size() * sizeof(int*))))
+    return rc;
+  LRS_CUDA(cudaMemcpy(m->d_parts, parts.data(), parts.size() * sizeof(float*), cudaMemcpyHostToDevice));
+  LRS_CUDA(cudaMemcpy(m->d_peer_sig, sigs.data(), sigs.size() * sizeof(int*), cudaMemcpyHostToDevice));
+  m->tp_p2p = true;
+  return LRS_OK;
+}
+
 // Splits of each sequence's context: as many as fit in one wave of resident
 // attention CTAs (batch * kv heads * splits CTAs), so no tail wave.
 int nsplit_for(const lrs_model* m, int batch) {
@@ -489,11 +560,34 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   // Row-split projections (o, down): every rank adds its partial sum of the
   // residual update; rank 0 adds onto the residual, the others overwrite their
   // copy with the partial, and one sum all-reduce rebuilds the residual.
-  const int res_epi = tp && m->tp_rank != 0 ? EPI_STORE : EPI_ADD;
+  // With the peer-memory all-reduce every rank stores its partial into the
+  // exchange buffer of the call's parity instead, and tp_allreduce_add_kernel
+  // adds all ranks' partials onto the residual.
+  const int res_epi = tp && (m->tp_p2p || m->tp_rank != 0) ? EPI_STORE : EPI_ADD;
+  int ar_calls = 0;  // all-reduces queued by this step (2 per layer: parities alternate)
+  auto res_out = [&]() -> float* {
+    return m->tp_p2p ? m->xbuf + (size_t)(ar_calls & 1) * m->max_items * h : m->residual;
+  };
   auto allreduce_residual = [&]() -> int32_t {
-    if (tp)
+    if (tp && m->tp_p2p) {
+      TpArgs a;
+      a.residual = m->residual;
+      a.n = (size_t)B * h;
+      a.parts0 = m->d_parts;
+      a.parts1 = m->d_parts + m->tp_world;
+      a.parity = ar_calls & 1;
+      a.local_sig = m->tp_sig;
+      a.peer_sig = m->d_peer_sig;
+      a.tickets = m->tp_tickets;
+      a.rank = m->tp_rank;
+      a.world = m->tp_world;
+      a.error_flag = m->be->d_err;
+      LRS_CUDA(launch_tp_allreduce_add(a, st));
+    } else if (tp) {
       LRS_NCCL(nccl().AllReduce(m->residual, m->residual, (size_t)B * h, ncclFloat32, ncclSum,
                                 m->comm, st));
+    }
+    ar_calls++;
     return LRS_OK;
   };
   StepIO io{m->d_tok, m->d_pos, m->d_seq, m->d_pages, m->pages_per_seq};
@@ -534,7 +628,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
                               m->att, m->attn_cnt, m->be->d_err, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
-    GemvMat om = mat_of(L.o, m->residual, h);
+    GemvMat om = mat_of(L.o, res_out(), h);
     if ((rc = gemv_plan(&p, &om, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->att;
@@ -571,7 +665,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       LRS_CUDA(launch_swiglu(m->act, m->act2, (size_t)B * I, st));
     }
     // down_proj + residual (src/model.rs:255-260)
-    GemvMat dm = mat_of(L.down, m->residual, h);
+    GemvMat dm = mat_of(L.down, res_out(), h);
     if ((rc = gemv_plan(&p, &dm, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->act;
@@ -868,6 +962,7 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
   m->gemm_scratch_bytes += kScratchCounterBytes;
   if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
   LRS_CUDA(cudaMemset(m->gemm_scratch, 0, m->gemm_scratch_bytes));  // the tail counters start at zero
+  if (world > 1 && tp_p2p_requested() && (rc = setup_tp_p2p(m.get(), h))) return cleanup(rc);
   if (world > 1 &&
       (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))
     return cleanup(rc);
@@ -930,6 +1025,16 @@ void lrs_model_destroy(lrs_model* m) {
     cudaFree(L.up.d);
     cudaFree(L.down.d);
   }
+  if (m->tp_p2p && m->comm) {
+    // Peers may still be reading this rank's exchange buffer in their last
+    // all-reduce: one collective (which starts on every rank only after its
+    // earlier kernels finished) before the buffers are unmapped and freed.
+    const NcclApi& n = nccl();
+    if (n.ok && n.AllReduce(m->tp_sig, m->tp_sig, 1, ncclInt32, ncclMax, m->comm, m->be->stream) ==
+                    ncclSuccess)
+      cudaStreamSynchronize(m->be->stream);
+  }
+  for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   cudaFree(m->embed.d);
   if (!m->tied) cudaFree(m->lm.d);
   for (void* p : m->allocs) cudaFree(p);

@@ -43,10 +43,18 @@ json.dump(res, open(out, "w"))
 """
 
 
-def test_tp2_matches_oracle(lrs, orc, tmp_path):
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
+def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce):
+    """allreduce="p2p": the row-split projections are summed by the peer-memory
+    all-reduce (LRS_TP_P2P=1, tp_p2p.cu) instead of NCCL."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    if allreduce == "p2p" and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
+        pytest.skip("the peer-memory all-reduce runs with LRS_TEST_NEW_KERNELS=1")
+    env = {**os.environ, "NCCL_NVLS_ENABLE": "0"}
+    if allreduce == "p2p":
+        env["LRS_TP_P2P"] = "1"
     world = 2
     tp_id = lrs.tp_unique_id().hex()
     procs, outs = [], []
@@ -54,7 +62,7 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path):
         out = str(tmp_path / f"rank{r}.json")
         outs.append(out)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER, ROOT, str(r), str(world), tp_id,
-                                       out], env={**os.environ, "NCCL_NVLS_ENABLE": "0"}))
+                                       out], env=env))
     try:
         codes = [p.wait(timeout=600) for p in procs]
     finally:
@@ -71,6 +79,7 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path):
         assert np.abs(np.array(res[r]["logits"], np.float32) - ref["logits"][0]).max() < 2e-2
         assert res[r]["tokens"] == [int(t) for t in ref["tokens"]]
         assert res[r]["batch"] == res[0]["batch"]
+        assert res[r]["logits"] == res[0]["logits"]  # every rank holds the same residual
     for s in range(1, 4):
         p = lrs.prompt_tokens(50 + s, 20 + s, cfg.vocab_size)
         want = orc.OracleModel(sm.desc(), 256).benchmark_tokens(p, 17)["tokens"]
