@@ -345,6 +345,10 @@ namespace {
 
 struct Layer {
   DevTensor q, k, v, o, gate, up, down;
+  // tensor parallelism: column windows of the row-split o / down shards.  A
+  // shard holds whole blocks [c0 - lo, c0 - lo + cols); when that is wider
+  // than the rank's columns, x is zero-padded to it (launch_pad_copy).
+  int o_lo = 0, d_lo = 0;
   float *in_norm = nullptr, *post_norm = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr;
   void *kpool = nullptr, *vpool = nullptr;
 };
@@ -380,6 +384,7 @@ struct lrs_model {
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
   int* attn_cnt = nullptr;  // [max_items][kv heads] split counters of the attention combine
+  float *att_pad = nullptr, *act_pad = nullptr;  // zero-padded x of windowed o / down shards
   // tensor parallelism over peer memory (LRS_TP_P2P=1): exchange buffers
   // [2][max_items * hidden], signal words [world], a launch counter, and the
   // device arrays of every rank's (IPC-mapped) pointers
@@ -633,6 +638,11 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     p.error_flag = m->be->d_err;
     p.x = m->att;
     p.x_ld = qw;
+    if (L.o.cols != qw) {  // a windowed column shard: x zero-padded to its blocks
+      LRS_CUDA(launch_pad_copy(m->att, qw, m->att_pad, L.o.cols, L.o_lo, B, st));
+      p.x = m->att_pad;
+      p.x_ld = L.o.cols;
+    }
     LRS_CUDA(model_gemv(m, p, st, sms));
     if ((rc = allreduce_residual())) return rc;
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
@@ -670,6 +680,11 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     p.error_flag = m->be->d_err;
     p.x = m->act;
     p.x_ld = I;
+    if (L.down.cols != I) {
+      LRS_CUDA(launch_pad_copy(m->act, I, m->act_pad, L.down.cols, L.d_lo, B, st));
+      p.x = m->act_pad;
+      p.x_ld = L.down.cols;
+    }
     LRS_CUDA(model_gemv(m, p, st, sms));
     if ((rc = allreduce_residual())) return rc;
   }
@@ -743,17 +758,20 @@ lrs_tensor_desc rows_of(const lrs_tensor_desc& d, size_t r0, size_t n) {
   return o;
 }
 
-// Column window [c0, c0 + n) of a tensor, copied into `buf` (whole blocks).
+// Column window [c0, c0 + n) of a tensor, copied into `buf` as the whole
+// blocks that cover it: columns [c0 - *lo, c0 - *lo + out->cols).  The
+// blocks' values outside the window meet zeros in x, so the shard's dot
+// equals the window's (blocks are never re-encoded: the bytes stay the
+// reference's).
 int32_t cols_of(const lrs_tensor_desc& d, size_t c0, size_t n, const char* what,
-                std::vector<uint8_t>* buf, lrs_tensor_desc* out) {
+                std::vector<uint8_t>* buf, lrs_tensor_desc* out, int* lo) {
   uint32_t bv = 0, bb = 0;
-  if (!type_geometry(d.ggml_type, &bv, &bb)) return fail(LRS_ERR_UNSUPPORTED, "unknown ggml type");
-  if (c0 % bv || n % bv)
-    return fail(LRS_ERR_UNSUPPORTED, std::string("tensor-parallel split of ") + what +
-                                         " at column " + std::to_string(c0) +
-                                         " is not aligned to its " + std::to_string(bv) +
-                                         "-value blocks");
-  const size_t rb = d.rows ? d.nbytes / d.rows : 0, off = c0 / bv * bb, len = n / bv * bb;
+  if (!type_geometry(d.ggml_type, &bv, &bb))
+    return fail(LRS_ERR_UNSUPPORTED, std::string("unknown ggml type of ") + what);
+  const size_t a0 = c0 / bv * bv, a1 = (c0 + n + bv - 1) / bv * bv;
+  *lo = (int)(c0 - a0);
+  n = a1 - a0;
+  const size_t rb = d.rows ? d.nbytes / d.rows : 0, off = a0 / bv * bb, len = n / bv * bb;
   buf->resize(d.rows * len);
   for (size_t r = 0; r < d.rows; r++)
     memcpy(buf->data() + r * len, static_cast<const uint8_t*>(d.data) + r * rb + off, len);
@@ -863,16 +881,16 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         (rc = check_shape(s.up_proj, (size_t)c.intermediate_size, h, "up_proj")) ||
         (rc = check_shape(s.down_proj, h, (size_t)c.intermediate_size, "down_proj")))
       return cleanup(rc);
-    if (world > 1 && ((rc = cols_of(s.o_proj, rank * qw, qw, "o_proj", &obuf, &o_loc)) ||
-                      (rc = cols_of(s.down_proj, rank * I, I, "down_proj", &dbuf, &d_loc))))
+    if (world > 1 && ((rc = cols_of(s.o_proj, rank * qw, qw, "o_proj", &obuf, &o_loc, &L.o_lo)) ||
+                      (rc = cols_of(s.down_proj, rank * I, I, "down_proj", &dbuf, &d_loc, &L.d_lo))))
       return cleanup(rc);
     if ((rc = upload_mat(rows_of(s.q_proj, rank * qw, qw), qw, h, "q_proj", &L.q)) ||
         (rc = upload_mat(rows_of(s.k_proj, rank * kvw, kvw), kvw, h, "k_proj", &L.k)) ||
         (rc = upload_mat(rows_of(s.v_proj, rank * kvw, kvw), kvw, h, "v_proj", &L.v)) ||
-        (rc = upload_mat(o_loc, h, qw, "o_proj", &L.o)) ||
+        (rc = upload_mat(o_loc, h, o_loc.cols, "o_proj", &L.o)) ||
         (rc = upload_mat(rows_of(s.gate_proj, rank * I, I), I, h, "gate_proj", &L.gate)) ||
         (rc = upload_mat(rows_of(s.up_proj, rank * I, I), I, h, "up_proj", &L.up)) ||
-        (rc = upload_mat(d_loc, h, I, "down_proj", &L.down)))
+        (rc = upload_mat(d_loc, h, d_loc.cols, "down_proj", &L.down)))
       return cleanup(rc);
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
@@ -938,6 +956,16 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->attn_cnt, B * cl.num_key_value_heads * 4)))
     return cleanup(rc);
   LRS_CUDA(cudaMemset(m->attn_cnt, 0, B * cl.num_key_value_heads * 4));
+  {
+    size_t ow = 0, dw = 0;
+    for (const auto& L : m->layers) {
+      if (L.o.cols != (int)(cl.num_attention_heads * c.head_dim)) ow = std::max(ow, (size_t)L.o.cols);
+      if (L.down.cols != (int)cl.intermediate_size) dw = std::max(dw, (size_t)L.down.cols);
+    }
+    if ((ow && (rc = model_alloc(m.get(), (void**)&m->att_pad, B * ow * 4))) ||
+        (dw && (rc = model_alloc(m.get(), (void**)&m->act_pad, B * dw * 4))))
+      return cleanup(rc);
+  }
   for (const auto& L : m->layers)
     if (L.gate.type != L.up.type && !m->act2 &&
         (rc = model_alloc(m.get(), (void**)&m->act2, B * I * 4)))

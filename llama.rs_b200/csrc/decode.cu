@@ -726,6 +726,15 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
   return cudaGetLastError();
 }
 
+// dst[b][j] = src[b][j - lo] for lo <= j < lo + n, else 0 (j < width): the
+// rank's x of a windowed column shard, zero outside its columns.
+__global__ void pad_copy_kernel(const float* src, int n, float* dst, int width, int lo, int batch) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)batch * width) return;
+  const int b = (int)(i / width), j = (int)(i % width) - lo;
+  dst[i] = j >= 0 && j < n ? src[(size_t)b * n + j] : 0.0f;
+}
+
 // g[i] = silu(g[i]) * u[i] (src/model.rs:251-254), for gate and up
 // projections of different GGML types that ran as two launches.
 __global__ void swiglu_kernel(float* g, const float* u, size_t n) {
@@ -739,6 +748,14 @@ __global__ void swiglu_kernel(float* g, const float* u, size_t n) {
 __global__ void key_offset_kernel(unsigned long long* keys, int n, uint32_t offset) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n && keys[i]) keys[i] += offset;
+}
+
+cudaError_t launch_pad_copy(const float* src, int n, float* dst, int width, int lo, int batch,
+                            cudaStream_t st) {
+  const size_t total = (size_t)batch * width;
+  if (total == 0) return cudaSuccess;
+  pad_copy_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, n, dst, width, lo, batch);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_swiglu(float* g, const float* u, size_t n, cudaStream_t st) {

@@ -49,6 +49,10 @@ cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int n
                              cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
+// x of a windowed tensor-parallel column shard: dst[b][0..width) holds
+// src[b][0..n) at offset lo and zeros elsewhere.
+cudaError_t launch_pad_copy(const float* src, int n, float* dst, int width, int lo, int batch,
+                            cudaStream_t st);
 // g[i] = silu(g[i]) * u[i] over n floats (SwiGLU of separately computed gate / up).
 cudaError_t launch_swiglu(float* g, const float* u, size_t n, cudaStream_t st);
 // keys[i] += offset (the packed argmax keys of a vocabulary shard; 0 stays 0).

@@ -19,12 +19,13 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 WORKER = r"""
 import importlib.util, json, os, sys
 root, rank, world, tp_id, out = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), bytes.fromhex(sys.argv[4]), sys.argv[5]
+shape, recipe = json.loads(sys.argv[6]), sys.argv[7]
 pkg = os.path.join(root, "llama.rs_b200")
 spec = importlib.util.spec_from_file_location("llamars_b200", os.path.join(pkg, "__init__.py"),
                                               submodule_search_locations=[pkg])
 lrs = importlib.util.module_from_spec(spec); sys.modules["llamars_b200"] = lrs; spec.loader.exec_module(lrs)
-cfg = lrs.LlamaConfig(512, 1024, 8, 4, 2, 2048, 1e-6, 1e6, 4096, 64, False)
-sm = lrs.SynthModel(cfg, 11, lrs.LoadQuantization.Q4KM)
+cfg = lrs.LlamaConfig(*shape)
+sm = lrs.SynthModel(cfg, 11, lrs.LoadQuantization[recipe])
 be = lrs.CudaBackend(rank)
 m = lrs.CudaQwen2Model(be, sm.desc(), max_seq_len=256, max_sequences=4, tp_rank=rank,
                        tp_world=world, tp_id=tp_id)
@@ -43,15 +44,26 @@ json.dump(res, open(out, "w"))
 """
 
 
+SHAPES = {
+    # hidden, intermediate, heads, kv heads, layers, vocab, eps, theta, ctx, head_dim, tied
+    "aligned": ([512, 1024, 8, 4, 2, 2048, 1e-6, 1e6, 4096, 64, False], "Q4KM"),
+    # o's and down's column shards are 2.5 and 5.5 Q4_K super-blocks wide: the
+    # ranks hold the covering blocks and zero-pad x (the c4 layout at TP8)
+    "windowed": ([1280, 2816, 10, 2, 2, 2048, 1e-6, 1e6, 4096, 128, False], "Q4K"),
+}
+
+
+@pytest.mark.parametrize("shape", ["aligned", "windowed"])
 @pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
-def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce):
+def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
     """allreduce="p2p": the row-split projections are summed by the peer-memory
     all-reduce (LRS_TP_P2P=1, tp_p2p.cu) instead of NCCL."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    if allreduce == "p2p" and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
-        pytest.skip("the peer-memory all-reduce runs with LRS_TEST_NEW_KERNELS=1")
+    if (allreduce == "p2p" or shape == "windowed") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
+        pytest.skip("the peer-memory all-reduce and windowed shards run with LRS_TEST_NEW_KERNELS=1")
+    dims, recipe = SHAPES[shape]
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0"}
     if allreduce == "p2p":
         env["LRS_TP_P2P"] = "1"
@@ -62,7 +74,7 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce):
         out = str(tmp_path / f"rank{r}.json")
         outs.append(out)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER, ROOT, str(r), str(world), tp_id,
-                                       out], env=env))
+                                       out, json.dumps(dims), recipe], env=env))
     try:
         codes = [p.wait(timeout=600) for p in procs]
     finally:
@@ -71,8 +83,8 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce):
                 p.kill()
     assert codes == [0] * world
     res = [json.load(open(o)) for o in outs]
-    cfg = lrs.LlamaConfig(512, 1024, 8, 4, 2, 2048, 1e-6, 1e6, 4096, 64, False)
-    sm = lrs.SynthModel(cfg, 11, lrs.LoadQuantization.Q4KM)
+    cfg = lrs.LlamaConfig(*dims)
+    sm = lrs.SynthModel(cfg, 11, lrs.LoadQuantization[recipe])
     prompt = lrs.prompt_tokens(11, 40, cfg.vocab_size)
     ref = orc.OracleModel(sm.desc(), 256).benchmark_tokens(prompt, 25, keep_logits=True)
     for r in range(world):
