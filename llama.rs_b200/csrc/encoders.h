@@ -488,13 +488,13 @@ LRS_ENC uint32_t effective_type(uint32_t t, size_t cols) {
       if (cols % 256 == 0) return t;
       return cols % 32 == 0 ? LRS_GGML_Q8_0 : LRS_GGML_F32;
     case LRS_GGML_Q5_K:
-      return cols % 256 == 0 ? t : LRS_GGML_F32;
+      return cols % 256 == 0 ? t : (uint32_t)LRS_GGML_F32;
     case LRS_GGML_Q4_0:
     case LRS_GGML_Q4_1:
     case LRS_GGML_Q5_0:
     case LRS_GGML_Q5_1:
     case LRS_GGML_Q8_0:
-      return cols % 32 == 0 ? t : LRS_GGML_F32;
+      return cols % 32 == 0 ? t : (uint32_t)LRS_GGML_F32;
     default:
       return t;
   }
