@@ -627,10 +627,15 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       m->prof_attn->push_back(a1);
       cudaEventRecord(a0, st);
     }
-    LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
-                               L.kpool, L.vpool, kv_bf16, st));
+    // decode steps (every item one new position of its own sequence) with the
+    // v3 attention: RoPE and the KV store happen inside the attention kernel
+    const bool fuse_rope = lm_item == -1 && attention_v3_enabled();
+    const AttnRope rope{m->k, m->v, m->rope_cos, m->rope_sin};
+    if (!fuse_rope)
+      LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
+                                 L.kpool, L.vpool, kv_bf16, st));
     LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
-                              m->att, m->attn_cnt, m->be->d_err, st));
+                              m->att, m->attn_cnt, m->be->d_err, fuse_rope ? &rope : nullptr, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
     GemvMat om = mat_of(L.o, res_out(), h);
@@ -1264,6 +1269,8 @@ lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* s
     if (seqs[i] >= m->opt.max_sequences || tokens[i] >= m->vocab_full ||
         pos[i] >= m->opt.max_seq_len)
       return fail(LRS_ERR_INVALID, "profile_step: item out of range");
+    for (size_t j = 0; j < i; j++)
+      if (seqs[j] == seqs[i]) return fail(LRS_ERR_INVALID, "duplicate sequence slot in batch");
     tok[i] = (int)tokens[i];
     ps[i] = (int)pos[i];
     sq[i] = (int)seqs[i];

@@ -366,7 +366,8 @@ struct A3Shape {
   static constexpr int kPsOff = kQOff + kMaxGroup * HD * 4;      // ps [warps][2][32]
   static constexpr int kBarOff = kPsOff + kA3Warps * 2 * 32 * 4;  // full[kA3Stages]
   static constexpr int kFlagOff = kBarOff + kA3Stages * 8;        // abort, last
-  static constexpr int kSmem = kFlagOff + 16;
+  static constexpr int kNewOff = kFlagOff + 16;                   // rotated k, v of the new position
+  static constexpr int kSmem = kNewOff + 2 * HD * 4;
 };
 
 // DPL consecutive K or V values of a row in shared memory, as f32.
@@ -408,10 +409,22 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
   return v[0];
 }
 
+// Decode steps fuse RoPE and the KV store (rope_store_kernel's work) when
+// rope != null: q is rotated as it is loaded, and the CTA whose split holds the
+// new position rotates its k, stores k and v into the cache and uses them in
+// place of that row of its block (the copy may predate the store).
+struct A3Rope {
+  const float* k;  // [B][nkv][HD] this step's k (not rotated)
+  const float* v;  // [B][nkv][HD]
+  const float* cos_t;
+  const float* sin_t;
+};
+
 template <int HD, bool BF16>
 __global__ void __launch_bounds__(kA3Warps * 32)
-    attn3_kernel(const float* q, StepIO io, int nh, int nkv, const void* kpool, const void* vpool,
-                 int nsplit, float scale, float* part, float* att, int* counters, int* error_flag) {
+    attn3_kernel(const float* q, StepIO io, int nh, int nkv, void* kpool, void* vpool,
+                 int nsplit, float scale, float* part, float* att, int* counters, int* error_flag,
+                 const A3Rope rope, int fuse) {
   using S = A3Shape<HD, BF16>;
   constexpr int DPL = HD / 32;
   constexpr int ES = BF16 ? 2 : 4;
@@ -449,9 +462,68 @@ __global__ void __launch_bounds__(kA3Warps * 32)
     flags[0] = 0;
     flags[1] = 0;
   }
-  for (int i = tid; i < kMaxGroup * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    qs[i] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + d] * scale : 0.0f;
+  // the copies above read old positions only (or a row replaced below): the
+  // rest waits for the previous kernel (programmatic dependent launch)
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pnew = L - 1;  // this step's position
+  float* knew = reinterpret_cast<float*>(smem + S::kNewOff);
+  float* vnew = knew + HD;
+  if (!fuse) {
+    for (int i = tid; i < kMaxGroup * HD; i += blockDim.x) {
+      const int g = i / HD, d = i % HD;
+      qs[i] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + d] * scale : 0.0f;
+    }
+  } else {
+    // apply_rope_inplace (src/model.rs:86-95), unfused like rope_store_kernel
+    constexpr int half = HD / 2;
+    const float* c = rope.cos_t + (size_t)pnew * half;
+    const float* sn = rope.sin_t + (size_t)pnew * half;
+    for (int i = tid; i < kMaxGroup * half; i += blockDim.x) {
+      const int g = i / half, d = i % half;
+      float r0 = 0.0f, r1 = 0.0f;
+      if (g < G) {
+        const float* qh = q + ((size_t)b * nh + kvh * G + g) * HD;
+        const float re = qh[d], im = qh[d + half];
+        r0 = __fsub_rn(__fmul_rn(re, c[d]), __fmul_rn(im, sn[d]));
+        r1 = __fadd_rn(__fmul_rn(re, sn[d]), __fmul_rn(im, c[d]));
+      }
+      qs[g * HD + d] = r0 * scale;
+      qs[g * HD + d + half] = r1 * scale;
+    }
+    if (s0 <= pnew && pnew < s1) {  // this split holds the new position
+      const float* kh = rope.k + ((size_t)b * nkv + kvh) * HD;
+      const float* vh = rope.v + ((size_t)b * nkv + kvh) * HD;
+      const size_t o = kv_offset(io, b, pnew, nkv, kvh, HD);
+      for (int d = tid; d < half; d += blockDim.x) {
+        const float re = kh[d], im = kh[d + half];
+        float k0 = __fsub_rn(__fmul_rn(re, c[d]), __fmul_rn(im, sn[d]));
+        float k1 = __fadd_rn(__fmul_rn(re, sn[d]), __fmul_rn(im, c[d]));
+        float v0 = vh[d], v1 = vh[d + half];
+        if constexpr (BF16) {
+          __nv_bfloat16* kp = reinterpret_cast<__nv_bfloat16*>(kpool) + o;
+          __nv_bfloat16* vp = reinterpret_cast<__nv_bfloat16*>(vpool) + o;
+          kp[d] = __float2bfloat16_rn(k0);
+          kp[d + half] = __float2bfloat16_rn(k1);
+          vp[d] = __float2bfloat16_rn(v0);
+          vp[d + half] = __float2bfloat16_rn(v1);
+          // what a later read of the cache returns
+          k0 = __bfloat162float(kp[d]), k1 = __bfloat162float(kp[d + half]);
+          v0 = __bfloat162float(vp[d]), v1 = __bfloat162float(vp[d + half]);
+        } else {
+          float* kp = reinterpret_cast<float*>(kpool) + o;
+          float* vp = reinterpret_cast<float*>(vpool) + o;
+          kp[d] = k0;
+          kp[d + half] = k1;
+          vp[d] = v0;
+          vp[d + half] = v1;
+        }
+        knew[d] = k0;
+        knew[d + half] = k1;
+        vnew[d] = v0;
+        vnew[d + half] = v1;
+      }
+    }
   }
   __syncthreads();
 
@@ -480,12 +552,19 @@ __global__ void __launch_bounds__(kA3Warps * 32)
       const uint8_t* kb = smem + st * S::kStageBytes;
       const uint8_t* vb = kb + S::kBlockBytes;
       const int nv = min(32, s1 - blk);
+      // the row of the new position comes from knew / vnew when fused
+      const int jn = fuse && pnew >= blk && pnew < blk + 32 ? pnew - blk : -1;
       // scores: lane j ends with q . k_j for its heads
       float p0[32], p1[32];
 #pragma unroll
       for (int j = 0; j < 32; j++) {
         float kv[DPL];
-        lds_row<DPL, BF16>(kb + j * S::kRowBytes + lane * DPL * ES, kv);
+        if (j == jn) {
+#pragma unroll
+          for (int k = 0; k < DPL; k++) kv[k] = knew[lane * DPL + k];
+        } else {
+          lds_row<DPL, BF16>(kb + j * S::kRowBytes + lane * DPL * ES, kv);
+        }
         float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
         for (int k = 0; k < DPL; k++) {
@@ -520,7 +599,12 @@ __global__ void __launch_bounds__(kA3Warps * 32)
       __syncwarp();
       for (int j = 0; j < nv; j++) {
         float vv[DPL];
-        lds_row<DPL, BF16>(vb + j * S::kRowBytes + lane * DPL * ES, vv);
+        if (j == jn) {
+#pragma unroll
+          for (int k = 0; k < DPL; k++) vv[k] = vnew[lane * DPL + k];
+        } else {
+          lds_row<DPL, BF16>(vb + j * S::kRowBytes + lane * DPL * ES, vv);
+        }
         const float pj0 = ps[(warp * 2) * 32 + j];
         const float pj1 = ps[(warp * 2 + 1) * 32 + j];
 #pragma unroll
@@ -669,39 +753,53 @@ int attention_ctas_per_sm(int hd, int kv_bf16) {
   return n < 1 ? 1 : n;
 }
 
+template <int HD, bool BF>
+cudaError_t launch_attn3(dim3 grid, cudaStream_t st, const float* q, StepIO io, int nh, int nkv,
+                         void* kpool, void* vpool, int nsplit, float scale, float* part, float* att,
+                         int* counters, int* error_flag, const A3Rope& rope, int fuse) {
+  const void* k = attn3_prepare<HD, BF>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kA3Warps * 32);
+  cfg.dynamicSmemBytes = A3Shape<HD, BF>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&q, &io, &nh, &nkv, &kpool, &vpool, &nsplit, &scale, &part, &att, &counters,
+                  &error_flag, const_cast<A3Rope*>(&rope), &fuse};
+  return cudaLaunchKernelExC(&cfg, k, args);
+}
+
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
-                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
+                             void* kpool, void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, int* counters, int* error_flag,
-                             cudaStream_t st) {
+                             const AttnRope* rope, cudaStream_t st) {
   if (nh / nkv > kMaxGroup || nsplit > 64) return cudaErrorInvalidValue;
   const float scale = 1.0f / sqrtf((float)hd);
   if (counters && attention_v3_enabled()) {
-    dim3 g3(nsplit, nkv, batch);
-#define LRS_ATTN3(HD, BF)                                                                    \
-  attn3_kernel<HD, BF><<<g3, kA3Warps * 32, A3Shape<HD, BF>::kSmem, st>>>(                  \
-      q, io, nh, nkv, kpool, vpool, nsplit, scale, part, att, counters, error_flag);
-    if (hd == 128) {
-      if (kv_bf16) {
-        attn3_prepare<128, true>();
-        LRS_ATTN3(128, true)
-      } else {
-        attn3_prepare<128, false>();
-        LRS_ATTN3(128, false)
-      }
-    } else if (hd == 64) {
-      if (kv_bf16) {
-        attn3_prepare<64, true>();
-        LRS_ATTN3(64, true)
-      } else {
-        attn3_prepare<64, false>();
-        LRS_ATTN3(64, false)
-      }
-    } else {
-      return cudaErrorInvalidValue;
+    const dim3 g3(nsplit, nkv, batch);
+    A3Rope r{};
+    int fuse = 0;
+    if (rope) {
+      r = A3Rope{rope->k, rope->v, rope->cos_t, rope->sin_t};
+      fuse = 1;
     }
-#undef LRS_ATTN3
-    return cudaGetLastError();
+    if (hd == 128)
+      return kv_bf16 ? launch_attn3<128, true>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
+                                                part, att, counters, error_flag, r, fuse)
+                     : launch_attn3<128, false>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
+                                                 part, att, counters, error_flag, r, fuse);
+    if (hd == 64)
+      return kv_bf16 ? launch_attn3<64, true>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
+                                               part, att, counters, error_flag, r, fuse)
+                     : launch_attn3<64, false>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
+                                                part, att, counters, error_flag, r, fuse);
+    return cudaErrorInvalidValue;
   }
+  if (rope) return cudaErrorInvalidValue;  // only the v3 kernel fuses RoPE
   dim3 g(nsplit, nkv, batch);
 #define LRS_ATTN(HD, BF)                                                                         \
   attn_split_kernel<HD, BF><<<g, kAttnWarps * 32, 0, st>>>(q, io, nh, nkv, kpool, vpool, nsplit, \

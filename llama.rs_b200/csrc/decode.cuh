@@ -43,10 +43,19 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
 bool attention_v3_enabled();
 // Resident attention CTAs per SM (occupancy of the split kernel in use).
 int attention_ctas_per_sm(int hd, int kv_bf16);
+// With v3 and `rope` non-null (decode steps: every item one new position of
+// its own sequence) the kernel also does launch_rope_store's work, which the
+// caller then skips.
+struct AttnRope {
+  const float* k;
+  const float* v;
+  const float* cos_t;
+  const float* sin_t;
+};
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
-                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
+                             void* kpool, void* vpool, int kv_bf16, int nsplit,
                              float* part, float* att, int* counters, int* error_flag,
-                             cudaStream_t st);
+                             const AttnRope* rope, cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
 // x of a windowed tensor-parallel column shard: dst[b][0..width) holds
