@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Decode throughput of llama.rs's Qwen2 token loop on B200.
+"""Decode throughput of llama.rs's Qwen2 token loop on B200 (benchmark config 3).
 
 Workload (default --config c3): the Qwen2.5-7B-shape model (seed 2, q4km),
 64 independent sequences, each a 1024-token uniform prompt followed by greedy
@@ -438,7 +438,7 @@ SWEEP_TYPES = ["F16", "BF16", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0", "Q4_K", "Q
 
 
 def run_gemv_sweep(args):
-    """GB/s of the quantized GEMV per type, shape and batch.
+    """benchmark config 1: GB/s of the quantized GEMV per type, shape and batch.
 
     W ~ N(0, 0.02) quantized on the host, x ~ N(0, 1); each cell times `iters`
     back-to-back launches with CUDA events after 3 warm-up launches.  Shapes
@@ -506,7 +506,7 @@ def main():
                     help="one tensor-parallel model over the ranks instead of data parallel")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
-    ap.add_argument("--gemv-sweep", action="store_true", help="BASELINE config 1 GEMV sweep")
+    ap.add_argument("--gemv-sweep", action="store_true", help="benchmark config 1 GEMV sweep")
     ap.add_argument("--types", default="")
     ap.add_argument("--shapes", default="")
     ap.add_argument("--batches", default="1,8,64")

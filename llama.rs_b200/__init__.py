@@ -1135,22 +1135,22 @@ def tp_unique_id() -> bytes:
 
 
 def config_c0() -> LlamaConfig:
-    """Qwen2.5-0.5B shape."""
+    """Qwen2.5-0.5B shape (benchmark config 0)."""
     return LlamaConfig(896, 4864, 14, 2, 24, 151936, 1e-6, 1e6, 32768, 64, True)
 
 
 def config_c2() -> LlamaConfig:
-    """Qwen2.5-1.5B shape."""
+    """Qwen2.5-1.5B shape (benchmark config 2)."""
     return LlamaConfig(1536, 8960, 12, 2, 28, 151936, 1e-6, 1e6, 32768, 128, True)
 
 
 def config_c3() -> LlamaConfig:
-    """Qwen2.5-7B shape."""
+    """Qwen2.5-7B shape (benchmark config 3)."""
     return LlamaConfig(3584, 18944, 28, 4, 28, 152064, 1e-6, 1e6, 32768, 128, False)
 
 
 def config_c4() -> LlamaConfig:
-    """Qwen2.5-32B shape."""
+    """Qwen2.5-32B shape (benchmark config 4)."""
     return LlamaConfig(5120, 27648, 40, 8, 64, 152064, 1e-6, 1e6, 32768, 128, False)
 
 

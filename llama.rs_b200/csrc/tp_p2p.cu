@@ -17,7 +17,7 @@
 //     with plain loads, in rank order, so every rank gets the same bits.
 // A rank overwrites an exchange buffer two launches later, after every peer
 // has signalled the launch in between, i.e. after the peers finished reading
-// it.  No multicast and no TMA touch peer memory.
+// it.  Peer memory is only read with plain loads and written with plain stores.
 #include <cuda_runtime.h>
 
 #include "../../include/llamars.h"

@@ -107,7 +107,7 @@ def test_matvec_validates_like_reference(lrs, backend):
     backend.release(t)
 
 
-# The GEMV sweep shapes.  K-quants with 896 columns are
+# The GEMV sweep shapes (benchmark config 1).  K-quants with 896 columns are
 # invalid in the reference (896 % 256 != 0) and skipped.
 SWEEP_SHAPES = [(4864, 896), (896, 4864), (18944, 3584), (3584, 18944), (152064, 3584)]
 

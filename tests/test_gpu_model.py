@@ -99,7 +99,7 @@ def test_errors_like_reference(lrs, backend):
 
 
 def test_c0_shape_benchmark_workload(lrs, orc, backend):
-    """Qwen2.5-0.5B shape, seed 0, q4km, prompt 128 + 32 greedy tokens."""
+    """benchmark config 0: Qwen2.5-0.5B shape, seed 0, q4km, prompt 128 + 32 greedy tokens."""
     sm, model, prompt, ref, logits, first, toks = _run_pair(
         lrs, orc, backend, lrs.config_c0(), lrs.LoadQuantization.Q4KM, 0, 128, 32, max_seq=4096)
     assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
