@@ -392,6 +392,7 @@ struct lrs_model {
   float* xbuf = nullptr;
   int* tp_sig = nullptr;
   unsigned* tp_tickets = nullptr;
+  unsigned* tp_counters = nullptr;  // [kTpMaxGrid] launches per CTA index of the fused path
   const float** d_parts = nullptr;  // [2][world]
   int** d_peer_sig = nullptr;       // [world]
   std::vector<void*> ipc_opened;
@@ -428,18 +429,24 @@ int32_t model_alloc(lrs_model* m, void** p, size_t bytes) {
   return LRS_OK;
 }
 
-cudaError_t model_gemv(lrs_model* m, const GemvParams& p0, cudaStream_t st, int sms) {
+// One projection; with `tp` the batch-1 stream GEMV fused with the
+// tensor-parallel all-reduce (p.x and the plan as for the unfused launch).
+cudaError_t model_gemv(lrs_model* m, const GemvParams& p0, cudaStream_t st, int sms,
+                       const StreamTp* tp = nullptr) {
   GemvParams p = p0;
   p.scratch = m->gemm_scratch;
   p.scratch_bytes = m->gemm_scratch_bytes;
-  if (!m->prof) return gemv_launch(p, st, sms, true);
+  auto run = [&](bool pdl) {
+    return tp ? gemv_stream_launch(p, st, sms, pdl, tp) : gemv_launch(p, st, sms, pdl);
+  };
+  if (!m->prof) return run(true);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
   m->prof->push_back(a);
   m->prof->push_back(b);
   cudaEventRecord(a, st);
-  cudaError_t e = gemv_launch(p, st, sms, false);
+  cudaError_t e = run(false);
   cudaEventRecord(b, st);
   return e;
 }
@@ -480,12 +487,20 @@ int32_t setup_tp_p2p(lrs_model* m, int h) {
   // own cudaMalloc allocations: an IPC handle names the base of an allocation
   LRS_CUDA(cudaMalloc((void**)&m->xbuf, xcount * 4));
   m->allocs.push_back(m->xbuf);
-  LRS_CUDA(cudaMalloc((void**)&m->tp_sig, 256));
+  // signal words: [0, world) for tp_allreduce_add_kernel, then
+  // [kTpSigFused + src * kTpMaxGrid + cta] for the fused stream GEMV
+  const size_t sig_bytes = (kTpSigFused + (size_t)world * kTpMaxGrid) * 4;
+  LRS_CUDA(cudaMalloc((void**)&m->tp_sig, sig_bytes));
   m->allocs.push_back(m->tp_sig);
-  LRS_CUDA(cudaMemset(m->tp_sig, 0, 256));
+  LRS_CUDA(cudaMemset(m->tp_sig, 0, sig_bytes));
   int32_t rc;
-  if ((rc = model_alloc(m, (void**)&m->tp_tickets, 4))) return rc;
+  if ((rc = model_alloc(m, (void**)&m->tp_tickets, 4)) ||
+      (rc = model_alloc(m, (void**)&m->tp_counters, kTpMaxGrid * 4)))
+    return rc;
   LRS_CUDA(cudaMemset(m->tp_tickets, 0, 4));
+  LRS_CUDA(cudaMemset(m->tp_counters, 0, kTpMaxGrid * 4));
+  if ((size_t)world > (size_t)m->max_items)
+    return fail(LRS_ERR_UNSUPPORTED, "peer-memory all-reduce: more ranks than item slots");
   cudaIpcMemHandle_t mine[2];
   LRS_CUDA(cudaIpcGetMemHandle(&mine[0], m->xbuf));
   LRS_CUDA(cudaIpcGetMemHandle(&mine[1], m->tp_sig));
@@ -573,6 +588,21 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   auto res_out = [&]() -> float* {
     return m->tp_p2p ? m->xbuf + (size_t)(ar_calls & 1) * m->max_items * h : m->residual;
   };
+  // batch-1 decode with the stream GEMV: the o / down projections push their
+  // partials to the peers themselves and reduce in the same kernel
+  const bool fused_tp = tp && m->tp_p2p && B == 1 && gemv_stream_enabled();
+  auto fused_tp_args = [&]() {
+    StreamTp t;
+    t.peer_x = const_cast<float* const*>(m->d_parts + (size_t)(ar_calls & 1) * m->tp_world);
+    t.local_sig = m->tp_sig + kTpSigFused;
+    t.peer_sig = m->d_peer_sig;
+    t.counters = m->tp_counters;
+    t.rank = m->tp_rank;
+    t.world = m->tp_world;
+    t.rows = h;
+    t.error_flag = m->be->d_err;
+    return t;
+  };
   auto allreduce_residual = [&]() -> int32_t {
     if (tp && m->tp_p2p) {
       TpArgs a;
@@ -638,7 +668,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
                               m->att, m->attn_cnt, m->be->d_err, fuse_rope ? &rope : nullptr, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
-    GemvMat om = mat_of(L.o, res_out(), h);
+    GemvMat om = mat_of(L.o, fused_tp ? m->residual : res_out(), h);
     if ((rc = gemv_plan(&p, &om, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->att;
@@ -648,8 +678,14 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->att_pad;
       p.x_ld = L.o.cols;
     }
-    LRS_CUDA(model_gemv(m, p, st, sms));
-    if ((rc = allreduce_residual())) return rc;
+    if (fused_tp) {
+      const StreamTp t = fused_tp_args();
+      LRS_CUDA(model_gemv(m, p, st, sms, &t));
+      ar_calls++;
+    } else {
+      LRS_CUDA(model_gemv(m, p, st, sms));
+      if ((rc = allreduce_residual())) return rc;
+    }
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
     bool xn_ready = false;
     auto ffn_input = [&](GemvParams& q) -> int32_t {
@@ -680,7 +716,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       LRS_CUDA(launch_swiglu(m->act, m->act2, (size_t)B * I, st));
     }
     // down_proj + residual (src/model.rs:255-260)
-    GemvMat dm = mat_of(L.down, res_out(), h);
+    GemvMat dm = mat_of(L.down, fused_tp ? m->residual : res_out(), h);
     if ((rc = gemv_plan(&p, &dm, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->act;
@@ -690,8 +726,14 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->act_pad;
       p.x_ld = L.down.cols;
     }
-    LRS_CUDA(model_gemv(m, p, st, sms));
-    if ((rc = allreduce_residual())) return rc;
+    if (fused_tp) {
+      const StreamTp t = fused_tp_args();
+      LRS_CUDA(model_gemv(m, p, st, sms, &t));
+      ar_calls++;
+    } else {
+      LRS_CUDA(model_gemv(m, p, st, sms));
+      if ((rc = allreduce_residual())) return rc;
+    }
   }
   if (lm_item == -2) return LRS_OK;
   // final norm + lm_head (src/model.rs:263-268) fused with the greedy argmax

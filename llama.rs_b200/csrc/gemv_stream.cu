@@ -84,9 +84,19 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
   return ((unsigned long long)hi << 32) | lo;
 }
 
-template <int T, bool PAIR>
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int T, bool PAIR, bool TPX>
 __global__ void __launch_bounds__(kStreamThreads)
-    gemv_stream_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ StreamShape sh) {
+    gemv_stream_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ StreamShape sh,
+                       const __grid_constant__ StreamTp tp) {
   using BT = BlockTraits<T>;
   using P = fast::Piece<T>;
   using XL = XLayout<T>;
@@ -160,6 +170,12 @@ __global__ void __launch_bounds__(kStreamThreads)
     };
     auto apply = [&](const Rows& e) {
       if (!e.live) return;
+      if constexpr (TPX) {
+        // this rank's partial of the row, into every rank's exchange buffer
+        // (peers' over NVLink): x_q[rank][row]
+        for (int q = 0; q < tp.world; q++) tp.peer_x[q][(size_t)tp.rank * tp.rows + e.row] = e.y[0];
+        return;
+      }
       switch (p.epi) {
         case EPI_STORE:
           *e.out = e.has_bias ? e.y[0] + e.bias : e.y[0];
@@ -238,6 +254,41 @@ __global__ void __launch_bounds__(kStreamThreads)
       if (lane == 0)
         for (int i = max(0, issued - NS); i < issued; i++)
           mbar_wait_bounded(&full[i % NS], (uint32_t)((i / NS) & 1));
+      return;
+    }
+    if constexpr (TPX) {
+      // every partial of this CTA's rows is stored: make them visible to the
+      // peers, signal the same CTA index there, wait for theirs, reduce
+      __threadfence_system();
+      __syncwarp();
+      const int b = blockIdx.x;
+      int epoch = 0;
+      if (lane == 0) epoch = (int)(++tp.counters[b]);
+      epoch = __shfl_sync(0xffffffffu, epoch, 0);
+      if (lane < tp.world && lane != tp.rank)
+        st_release_sys(tp.peer_sig[lane] + kTpSigFused + tp.rank * kTpMaxGrid + b, epoch);
+      bool got = true;
+      if (lane < tp.world && lane != tp.rank) {
+        got = false;
+        for (uint32_t it = 0; it < kSpinLimit; it++)
+          if (ld_acquire_sys(tp.local_sig + lane * kTpMaxGrid + b) >= epoch) {
+            got = true;
+            break;
+          }
+      }
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0 && tp.error_flag) atomicExch(tp.error_flag, LRS_ERR_DEVICE_TIMEOUT);
+        return;
+      }
+      // rows of this CTA's tiles (one segment): out[row] += sum over ranks in rank order
+      const GemvSeg sg = p.seg[0];
+      const int rA = (tA - sg.tile0) * sh.rt, rB = min(sg.rows, (tB - sg.tile0) * sh.rt);
+      const float* mine = tp.peer_x[tp.rank];
+      for (int row = rA + lane; row < rB; row += 32) {
+        float acc = sg.out[row];
+        for (int q = 0; q < tp.world; q++) acc += mine[(size_t)q * tp.rows + row];
+        sg.out[row] = acc;
+      }
       return;
     }
     if (p.epi == EPI_ARGMAX) {
@@ -373,23 +424,25 @@ __global__ void __launch_bounds__(kStreamThreads)
 }
 
 template <int T>
-const void* stream_kernel_of(bool pair) {
-  return pair ? (const void*)gemv_stream_kernel<T, true> : (const void*)gemv_stream_kernel<T, false>;
+const void* stream_kernel_of(bool pair, bool tpx) {
+  if (tpx) return pair ? nullptr : (const void*)gemv_stream_kernel<T, false, true>;
+  return pair ? (const void*)gemv_stream_kernel<T, true, false>
+              : (const void*)gemv_stream_kernel<T, false, false>;
 }
 
-const void* stream_kernel(int type, bool pair) {
+const void* stream_kernel(int type, bool pair, bool tpx) {
   switch (type) {
-    case LRS_GGML_F32: return stream_kernel_of<LRS_GGML_F32>(pair);
-    case LRS_GGML_F16: return stream_kernel_of<LRS_GGML_F16>(pair);
-    case LRS_GGML_BF16: return stream_kernel_of<LRS_GGML_BF16>(pair);
-    case LRS_GGML_Q4_0: return stream_kernel_of<LRS_GGML_Q4_0>(pair);
-    case LRS_GGML_Q4_1: return stream_kernel_of<LRS_GGML_Q4_1>(pair);
-    case LRS_GGML_Q5_0: return stream_kernel_of<LRS_GGML_Q5_0>(pair);
-    case LRS_GGML_Q5_1: return stream_kernel_of<LRS_GGML_Q5_1>(pair);
-    case LRS_GGML_Q8_0: return stream_kernel_of<LRS_GGML_Q8_0>(pair);
-    case LRS_GGML_Q4_K: return stream_kernel_of<LRS_GGML_Q4_K>(pair);
-    case LRS_GGML_Q5_K: return stream_kernel_of<LRS_GGML_Q5_K>(pair);
-    case LRS_GGML_Q6_K: return stream_kernel_of<LRS_GGML_Q6_K>(pair);
+    case LRS_GGML_F32: return stream_kernel_of<LRS_GGML_F32>(pair, tpx);
+    case LRS_GGML_F16: return stream_kernel_of<LRS_GGML_F16>(pair, tpx);
+    case LRS_GGML_BF16: return stream_kernel_of<LRS_GGML_BF16>(pair, tpx);
+    case LRS_GGML_Q4_0: return stream_kernel_of<LRS_GGML_Q4_0>(pair, tpx);
+    case LRS_GGML_Q4_1: return stream_kernel_of<LRS_GGML_Q4_1>(pair, tpx);
+    case LRS_GGML_Q5_0: return stream_kernel_of<LRS_GGML_Q5_0>(pair, tpx);
+    case LRS_GGML_Q5_1: return stream_kernel_of<LRS_GGML_Q5_1>(pair, tpx);
+    case LRS_GGML_Q8_0: return stream_kernel_of<LRS_GGML_Q8_0>(pair, tpx);
+    case LRS_GGML_Q4_K: return stream_kernel_of<LRS_GGML_Q4_K>(pair, tpx);
+    case LRS_GGML_Q5_K: return stream_kernel_of<LRS_GGML_Q5_K>(pair, tpx);
+    case LRS_GGML_Q6_K: return stream_kernel_of<LRS_GGML_Q6_K>(pair, tpx);
   }
   return nullptr;
 }
@@ -454,7 +507,8 @@ bool gemv_stream_enabled() {
   return e && e[0] == '1';
 }
 
-cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int num_sms, bool pdl) {
+cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int num_sms, bool pdl,
+                               const StreamTp* tp) {
   const bool pair = p0.epi == EPI_SWIGLU;
   const int nm = pair ? 2 : 1, R = pair ? 2 : 4;
   const int type = p0.seg[0].type;
@@ -465,7 +519,8 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
   const int ub = dense ? (int)(bb * 32) : (int)bb;
   const int uv = dense ? 32 : (int)bv;
   const int units = p0.cols / uv;
-  const void* kernel = stream_kernel(type, pair);
+  if (tp && (pair || p0.nseg != 1 || p0.batch != 1)) return cudaErrorInvalidValue;
+  const void* kernel = stream_kernel(type, pair, tp != nullptr);
   const size_t xbytes = x_bytes_of(type, p0.cols);
   if (!kernel || units < 1) return cudaErrorInvalidValue;
 
@@ -517,6 +572,7 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
   q.total_tiles = tile0;
   const int grid = std::min(q.total_tiles, num_sms * occ);
   if (grid < 1) return cudaSuccess;
+  if (grid > kTpMaxGrid) return cudaErrorInvalidValue;
   stream_occupancy(kernel, smem);  // sets the dynamic shared-memory limit
 
   cudaLaunchConfig_t cfg = {};
@@ -529,7 +585,8 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[] = {&q, &sh};
+  StreamTp none = {};
+  void* args[] = {&q, &sh, tp ? const_cast<StreamTp*>(tp) : &none};
   return cudaLaunchKernelExC(&cfg, kernel, args);
 }
 

@@ -54,19 +54,24 @@ SHAPES = {
 
 
 @pytest.mark.parametrize("shape", ["aligned", "windowed"])
-@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p", "fused"])
 def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
     """allreduce="p2p": the row-split projections are summed by the peer-memory
-    all-reduce (LRS_TP_P2P=1, tp_p2p.cu) instead of NCCL."""
+    all-reduce (LRS_TP_P2P=1, tp_p2p.cu) instead of NCCL; "fused": in addition
+    the batch-1 decode steps run the stream GEMV that pushes its partials to
+    the peers and reduces in the same kernel (LRS_GEMV_STREAM=1), while the
+    prefill and the batch of three keep the separate all-reduce."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    if (allreduce == "p2p" or shape == "windowed") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
+    if (allreduce != "nccl" or shape == "windowed") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
         pytest.skip("the peer-memory all-reduce and windowed shards run with LRS_TEST_NEW_KERNELS=1")
     dims, recipe = SHAPES[shape]
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0"}
-    if allreduce == "p2p":
+    if allreduce != "nccl":
         env["LRS_TP_P2P"] = "1"
+    if allreduce == "fused":
+        env["LRS_GEMV_STREAM"] = "1"
     world = 2
     tp_id = lrs.tp_unique_id().hex()
     procs, outs = [], []
