@@ -770,9 +770,11 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
       q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
       if (stream_on) {
         cudaError_t e = gemv_stream_launch(q, stream, num_sms, pdl);
-        if (e != cudaSuccess) return e;
-        i = j;
-        continue;
+        if (e == cudaSuccess) {
+          i = j;
+          continue;
+        }
+        if (e != cudaErrorNotSupported) return e;  // else: this run on gemv5_kernel
       }
       const void* kernel = fast_kernel(q.seg[0].type, pair);
       const size_t smem = 256 + fast_x_bytes(q.seg[0].type, q.cols);

@@ -98,7 +98,8 @@ struct StreamTp {
 // Batch-1 GEMV through a shared-memory ring of bulk copies (gemv_stream.cu),
 // for one run of same-type segments planned by gemv_plan (p.fast).  Used
 // instead of gemv5_kernel when LRS_GEMV_STREAM=1; with `tp` (one segment, not
-// a pair) the fused tensor-parallel variant.
+// a pair) the fused tensor-parallel variant.  cudaErrorNotSupported: the plan
+// does not fit (the caller uses gemv5_kernel).
 bool gemv_stream_enabled();
 cudaError_t gemv_stream_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl,
                                const StreamTp* tp = nullptr);

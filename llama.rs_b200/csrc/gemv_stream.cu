@@ -558,7 +558,7 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
     }
   }
   const int smem = stream_layout(sh, xbytes);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 227 * 1024) return cudaErrorNotSupported;  // x too wide for this kernel
 
   GemvParams q = p0;
   int tile0 = 0;
