@@ -281,3 +281,32 @@ def test_safetensors_model_decodes_like_oracle(lrs, orc, backend, tmp_path):
     assert np.abs(logits - ref["logits"][0]).max() < 2e-2
     produced = model.decode_greedy([first], [len(prompt)], 16)[:, 0]
     assert np.array_equal(ref["tokens"], np.concatenate([[first], produced[:-1]]))
+
+
+def test_config_json_forms(lrs, tmp_path):
+    """config.json as Hugging Face writes it: unknown and nested fields are
+    ignored (serde), numbers in any JSON form, escapes in strings."""
+    cfg = _cfg(lrs, True)
+    src = lrs.SynthModel(cfg, 12, lrs.LoadQuantization.NONE)
+    lrs.write_qwen2_safetensors(str(tmp_path), src.desc())
+    text = r"""{
+      "architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2",
+      "name_or_path": "café 😀 \"quoted\" \\ \/",
+      "rope_scaling": {"type": "yarn", "factor": 4.0, "nested": [1, [2, {"x": null}]]},
+      "hidden_size": 512, "intermediate_size": 1024, "num_attention_heads": 4,
+      "num_key_value_heads": 2, "num_hidden_layers": 2, "vocab_size": 1000,
+      "rms_norm_eps": 1E-06, "rope_theta": 1.0e6, "max_position_embeddings": 32768,
+      "head_dim": null, "tie_word_embeddings": true, "use_cache": false
+    }"""
+    (tmp_path / "config.json").write_text(text)
+    d = lrs.SafetensorsFile(str(tmp_path)).qwen2_desc().contents
+    assert d.config.head_dim == 128 and d.config.rms_norm_eps == np.float32(1e-6)
+    assert d.config.rope_theta == np.float32(1e6) and d.config.max_position_embeddings == 32768
+    for bad, msg in [('{"model_type": "qwen2", "hidden_size": 5.5}', "model_type|invalid type"),
+                     ('{"model_type": "qwen2",}', "invalid config.json"),
+                     ('{"model_type": "qwen2" "x": 1}', "invalid config.json"),
+                     ('{"model_type": "\\ud800"}', "invalid config.json"),
+                     ('[1, 2]', "missing model_type")]:
+        (tmp_path / "config.json").write_text(bad)
+        with pytest.raises(lrs.LrsError, match=msg):
+            lrs.SafetensorsFile(str(tmp_path)).qwen2_desc()
