@@ -183,6 +183,8 @@ typedef struct lrs_model_options {
   uint32_t max_sequences; /* concurrent sequences (slots) */
   uint32_t kv_dtype;      /* LRS_KV_F32 (default, parity) or LRS_KV_BF16 */
   uint32_t use_graph;     /* capture decode steps in a CUDA graph (1 = yes) */
+  uint32_t device_recipe; /* LRS_RECIPE_* (llamars_synth.h): F32/F16/BF16 matrices are encoded
+                             on the GPU at creation (maybe_quantize, src/loader.rs:406-447); 0 = as given */
 } lrs_model_options;
 
 typedef struct lrs_model lrs_model;

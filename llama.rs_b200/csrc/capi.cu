@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "../../include/llamars.h"
+#include "../../include/llamars_synth.h"
 #include "common.h"
 #include "decode.cuh"
 #include "gemv.cuh"
@@ -829,6 +830,88 @@ int32_t cols_of(const lrs_tensor_desc& d, size_t c0, size_t n, const char* what,
   return LRS_OK;
 }
 
+// maybe_quantize on the device (src/loader.rs:406-447): a float matrix of the
+// description (full shape) is uploaded, widened to f32 and encoded with the
+// recipe's type for `name` (lrs_quantize_matrix_device: the host encoders'
+// bytes); then rows [r0, r0 + nr) and the whole blocks covering columns
+// [c0, c0 + nc) (*lo as in cols_of) become `out`.  Encoding the full matrix
+// first keeps the reference's per-matrix choices (fallbacks on cols) and bytes
+// under tensor parallelism.  *done = false for other types (host path).
+int32_t device_encode_mat(lrs_model* m, uint32_t recipe, const lrs_tensor_desc& d,
+                          const std::string& name, size_t r0, size_t nr, size_t c0, size_t nc,
+                          DevTensor* out, int* lo, bool* done) {
+  *done = false;
+  const uint32_t t = d.ggml_type;
+  if (recipe == LRS_RECIPE_NONE || (t != LRS_GGML_F32 && t != LRS_GGML_F16 && t != LRS_GGML_BF16))
+    return LRS_OK;
+  const size_t R = d.rows, C = d.cols, n = R * C;
+  cudaStream_t st = m->be->stream;
+  uint8_t* raw = nullptr;
+  float* f32 = nullptr;
+  uint8_t* enc = nullptr;
+  auto release = [&]() {
+    cudaFree(raw);
+    if ((void*)f32 != (void*)raw) cudaFree(f32);
+    cudaFree(enc);
+  };
+  if (cudaMalloc(&raw, d.nbytes) != cudaSuccess) return fail(LRS_ERR_OOM, "upload of " + name);
+  if (cudaMemcpy(raw, d.data, d.nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    release();
+    return fail(LRS_ERR_CUDA, "upload copy of " + name + " failed");
+  }
+  if (t == LRS_GGML_F32) {
+    f32 = reinterpret_cast<float*>(raw);
+  } else if (cudaMalloc(&f32, n * 4) != cudaSuccess || launch_widen(raw, t, n, f32, st) != cudaSuccess) {
+    release();
+    return fail(LRS_ERR_OOM, "widening " + name);
+  }
+  const uint32_t qt = lrs_recipe_type(recipe, name.c_str(), R, C);
+  const size_t cap = lrs_quantized_size(qt, R, C);
+  if (cudaMalloc(&enc, cap + 256) != cudaSuccess) {
+    release();
+    return fail(LRS_ERR_OOM, "encoded buffer of " + name);
+  }
+  uint32_t made;
+  size_t len;
+  int32_t rc = lrs_quantize_matrix_device(m->be, qt, f32, R, C, enc, cap, &made, &len);
+  if (rc) {
+    release();
+    return rc;
+  }
+  uint32_t bv, bb;
+  type_geometry(made, &bv, &bb);
+  const size_t rb = len / R, a0 = c0 / bv * bv, a1 = (c0 + nc + bv - 1) / bv * bv;
+  const size_t off = a0 / bv * bb, w = (a1 - a0) / bv * bb;
+  *lo = (int)(c0 - a0);
+  uint8_t* dst = nullptr;
+  if (r0 == 0 && nr == R && a0 == 0 && a1 == C) {  // the whole matrix: keep the buffer
+    dst = enc;
+    enc = nullptr;
+    cudaMemsetAsync(dst + len, 0, 256, st);
+  } else {
+    if (cudaMalloc(&dst, nr * w + 256) != cudaSuccess) {
+      release();
+      return fail(LRS_ERR_OOM, "shard of " + name);
+    }
+    cudaMemsetAsync(dst + nr * w, 0, 256, st);
+    if (cudaMemcpy2DAsync(dst, w, enc + r0 * rb + off, rb, w, nr, cudaMemcpyDeviceToDevice, st) !=
+        cudaSuccess) {
+      cudaFree(dst);
+      release();
+      return fail(LRS_ERR_CUDA, "shard copy of " + name);
+    }
+  }
+  cudaStreamSynchronize(st);
+  release();
+  out->d = dst;
+  out->nbytes = nr * w;
+  out->rows = (int)nr;
+  out->cols = (int)(a1 - a0);
+  out->type = made;
+  *done = true;
+  return LRS_OK;
+}
+
 int32_t check_shape(const lrs_tensor_desc& d, size_t rows, size_t cols, const char* what) {
   if (d.rows != rows || d.cols != cols)
     return fail(LRS_ERR_INVALID, std::string("tensor ") + what + " has shape [" +
@@ -870,6 +953,7 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
                                      " exceeds model limit " +
                                      std::to_string(c.max_position_embeddings));
   if (opt.max_sequences == 0) opt.max_sequences = 1;
+  if (opt.device_recipe > LRS_RECIPE_Q4KM) return fail(LRS_ERR_INVALID, "unknown device recipe");
   LRS_CUDA(cudaSetDevice(be->device));
 
   // Tensor parallelism (world > 1): heads, the MLP width and the LM-head rows
@@ -902,24 +986,44 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
     lrs_model_destroy(m.release());
     return code;
   };
-  if ((rc = upload_mat(d->embed_tokens, c.vocab_size, h, "model.embed_tokens.weight", &m->embed)))
+  // a matrix: encoded on the device when opt.device_recipe asks for it (float
+  // types), else uploaded as given; rows [r0, r0 + nr), columns [c0, c0 + nc)
+  // of the full tensor (column windows: whole blocks, *lo as cols_of)
+  const uint32_t drec = opt.device_recipe;
+  std::vector<uint8_t> colbuf;
+  auto load_mat = [&](const lrs_tensor_desc& full, const std::string& name, size_t r0, size_t nr,
+                      size_t c0, size_t nc, DevTensor* dt, int* lo) -> int32_t {
+    bool done = false;
+    int32_t r2 = device_encode_mat(m.get(), drec, full, name, r0, nr, c0, nc, dt, lo, &done);
+    if (r2 || done) return r2;
+    *lo = 0;
+    lrs_tensor_desc part = rows_of(full, r0, nr);
+    if (c0 != 0 || nc != full.cols) {
+      if ((r2 = cols_of(part, c0, nc, name.c_str(), &colbuf, &part, lo))) return r2;
+    }
+    return upload_mat(part, nr, part.cols, name.c_str(), dt);
+  };
+  int lo_unused = 0;
+  if ((rc = check_shape(d->embed_tokens, c.vocab_size, h, "model.embed_tokens.weight")) ||
+      (rc = load_mat(d->embed_tokens, "model.embed_tokens.weight", 0, c.vocab_size, 0, h,
+                     &m->embed, &lo_unused)))
     return cleanup(rc);
-  if (d->lm_head.data == d->embed_tokens.data && world == 1) {
+  const bool head_is_embed = d->lm_head.data == d->embed_tokens.data;
+  if (head_is_embed && world == 1) {
     m->tied = true;
     m->lm = m->embed;
   } else if ((rc = check_shape(d->lm_head, c.vocab_size, h, "lm_head.weight")) ||
-             (rc = upload_mat(rows_of(d->lm_head, m->vocab0, V), V, h, "lm_head.weight", &m->lm))) {
+             (rc = load_mat(d->lm_head, head_is_embed ? "model.embed_tokens.weight" : "lm_head.weight",
+                            m->vocab0, V, 0, h, &m->lm, &lo_unused))) {
     return cleanup(rc);
   }
   if ((rc = upload_vec(m.get(), d->final_norm, h, &m->final_norm))) return cleanup(rc);
   if (!m->final_norm) return cleanup(fail(LRS_ERR_INVALID, "missing model.norm.weight"));
   m->weight_bytes = m->lm.nbytes + m->embed.nbytes / c.vocab_size;
   m->layers.resize(c.num_hidden_layers);
-  std::vector<uint8_t> obuf, dbuf;
   for (uint32_t i = 0; i < c.num_hidden_layers; i++) {
     const lrs_layer_desc& s = d->layers[i];
     Layer& L = m->layers[i];
-    lrs_tensor_desc o_loc = s.o_proj, d_loc = s.down_proj;
     if ((rc = check_shape(s.q_proj, h, h, "q_proj")) ||
         (rc = check_shape(s.k_proj, kvw_full, h, "k_proj")) ||
         (rc = check_shape(s.v_proj, kvw_full, h, "v_proj")) ||
@@ -928,16 +1032,14 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         (rc = check_shape(s.up_proj, (size_t)c.intermediate_size, h, "up_proj")) ||
         (rc = check_shape(s.down_proj, h, (size_t)c.intermediate_size, "down_proj")))
       return cleanup(rc);
-    if (world > 1 && ((rc = cols_of(s.o_proj, rank * qw, qw, "o_proj", &obuf, &o_loc, &L.o_lo)) ||
-                      (rc = cols_of(s.down_proj, rank * I, I, "down_proj", &dbuf, &d_loc, &L.d_lo))))
-      return cleanup(rc);
-    if ((rc = upload_mat(rows_of(s.q_proj, rank * qw, qw), qw, h, "q_proj", &L.q)) ||
-        (rc = upload_mat(rows_of(s.k_proj, rank * kvw, kvw), kvw, h, "k_proj", &L.k)) ||
-        (rc = upload_mat(rows_of(s.v_proj, rank * kvw, kvw), kvw, h, "v_proj", &L.v)) ||
-        (rc = upload_mat(o_loc, h, o_loc.cols, "o_proj", &L.o)) ||
-        (rc = upload_mat(rows_of(s.gate_proj, rank * I, I), I, h, "gate_proj", &L.gate)) ||
-        (rc = upload_mat(rows_of(s.up_proj, rank * I, I), I, h, "up_proj", &L.up)) ||
-        (rc = upload_mat(d_loc, h, d_loc.cols, "down_proj", &L.down)))
+    const std::string pre = "model.layers." + std::to_string(i);
+    if ((rc = load_mat(s.q_proj, pre + ".self_attn.q_proj.weight", rank * qw, qw, 0, h, &L.q, &lo_unused)) ||
+        (rc = load_mat(s.k_proj, pre + ".self_attn.k_proj.weight", rank * kvw, kvw, 0, h, &L.k, &lo_unused)) ||
+        (rc = load_mat(s.v_proj, pre + ".self_attn.v_proj.weight", rank * kvw, kvw, 0, h, &L.v, &lo_unused)) ||
+        (rc = load_mat(s.o_proj, pre + ".self_attn.o_proj.weight", 0, h, rank * qw, qw, &L.o, &L.o_lo)) ||
+        (rc = load_mat(s.gate_proj, pre + ".mlp.gate_proj.weight", rank * I, I, 0, h, &L.gate, &lo_unused)) ||
+        (rc = load_mat(s.up_proj, pre + ".mlp.up_proj.weight", rank * I, I, 0, h, &L.up, &lo_unused)) ||
+        (rc = load_mat(s.down_proj, pre + ".mlp.down_proj.weight", 0, h, rank * I, I, &L.down, &L.d_lo)))
       return cleanup(rc);
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||

@@ -30,3 +30,8 @@ struct lrs_tensor {
   lrs_backend* be = nullptr;
   DevTensor t;
 };
+
+namespace lrs {
+// F16 / BF16 (type) values at src to f32 (exact), on stream st (quantize_dev.cu).
+cudaError_t launch_widen(const void* src, uint32_t type, size_t n, float* dst, cudaStream_t st);
+}  // namespace lrs

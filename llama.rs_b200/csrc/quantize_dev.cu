@@ -38,7 +38,23 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// F16 / BF16 values to f32 (exact widening: QuantTensor::to_vec_f32).
+__global__ void widen_kernel(const uint16_t* src, uint32_t t, size_t n, float* dst) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint16_t h = src[i];
+  dst[i] = t == LRS_GGML_BF16 ? __uint_as_float((uint32_t)h << 16) : enc::f16_bits_to_f32(h);
+}
+
 }  // namespace
+
+cudaError_t launch_widen(const void* src, uint32_t type, size_t n, float* dst, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  widen_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint16_t*>(src), type,
+                                                              n, dst);
+  return cudaGetLastError();
+}
+
 }  // namespace lrs
 
 using namespace lrs;

@@ -310,3 +310,26 @@ def test_config_json_forms(lrs, tmp_path):
         (tmp_path / "config.json").write_text(bad)
         with pytest.raises(lrs.LrsError, match=msg):
             lrs.SafetensorsFile(str(tmp_path)).qwen2_desc()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
+                    reason="device-encoded loading runs with LRS_TEST_NEW_KERNELS=1")
+@pytest.mark.parametrize("dtype", ["F32", "BF16"])
+def test_device_recipe_equals_host_recipe(lrs, backend, tmp_path, dtype):
+    """maybe_quantize on the GPU (lrs_model_options.device_recipe): the float
+    checkpoint encoded at model creation gives bit-identical logits to the
+    host-encoded description."""
+    cfg = _cfg(lrs, False)
+    src = lrs.SynthModel(cfg, 13, lrs.LoadQuantization.NONE)
+    lrs.write_qwen2_safetensors(str(tmp_path), src.desc(), dtype=dtype)
+    raw = lrs.LoadedModel(str(tmp_path), lrs.LoadQuantization.NONE)
+    host = lrs.LoadedModel(str(tmp_path), lrs.LoadQuantization.Q4KM)
+    prompt = lrs.prompt_tokens(13, 24, cfg.vocab_size)
+    a = lrs.CudaQwen2Model(backend, raw.desc(), max_seq_len=128,
+                           device_recipe=lrs.LoadQuantization.Q4KM)
+    b = lrs.CudaQwen2Model(backend, host.desc(), max_seq_len=128)
+    la, fa = a.prefill(prompt, 0)
+    lb, fb = b.prefill(prompt, 0)
+    assert np.array_equal(la, lb) and fa == fb
+    assert np.array_equal(a.decode_greedy([fa], [24], 12), b.decode_greedy([fb], [24], 12))
