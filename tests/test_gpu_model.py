@@ -149,3 +149,40 @@ def test_model_from_gguf_file(lrs, orc, backend, tmp_path):
     assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
     _assert_tokens(ref, np.concatenate([[first], produced[:-1]]))
     model.close()
+
+
+new_shape = pytest.mark.skipif(__import__("os").environ.get("LRS_TEST_NEW_KERNELS") != "1",
+                               reason="runs with LRS_TEST_NEW_KERNELS=1 until run on a B200")
+
+
+@new_shape
+def test_c2_width_two_layers(lrs, orc, backend):
+    """Qwen2.5-1.5B widths under q4k: every matrix Q4_K, including the tied
+    151936-row head (benchmark config 2), 2 layers, batch 1."""
+    cfg = lrs.config_c2()
+    cfg.num_hidden_layers = 2
+    sm, model, prompt, ref, logits, first, toks = _run_pair(
+        lrs, orc, backend, cfg, lrs.LoadQuantization.Q4K, 1, 24, 32, max_seq=512)
+    assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
+    _assert_tokens(ref, toks)
+
+
+@new_shape
+def test_c4_width_batch16(lrs, orc, backend):
+    """Qwen2.5-32B widths (hidden 5120, 40/8 heads, intermediate 27648, q4k),
+    2 layers: batch 1 and 16 sequences (the tcgen05 path at 16 items)."""
+    cfg = lrs.config_c4()
+    cfg.num_hidden_layers = 2
+    sm, model, prompt, ref, logits, first, toks = _run_pair(
+        lrs, orc, backend, cfg, lrs.LoadQuantization.Q4K, 3, 20, 12, max_seq=256)
+    assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
+    _assert_tokens(ref, toks)
+    B, n_dec = 16, 8
+    m = lrs.CudaQwen2Model(backend, sm.desc(), max_seq_len=256, max_sequences=B)
+    prompts = [lrs.prompt_tokens(600 + s, 10 + s, cfg.vocab_size) for s in range(B)]
+    firsts = [m.prefill(p, 0, seq=s)[1] for s, p in enumerate(prompts)]
+    produced = m.decode_greedy(firsts, [len(p) for p in prompts], n_dec, list(range(B)))
+    fed = np.concatenate([np.array(firsts, np.uint32)[None, :], produced[:-1]], axis=0)
+    for s in (0, B - 1):
+        r = orc.OracleModel(sm.desc(), 256).benchmark_tokens(prompts[s], n_dec)
+        _assert_tokens(r, fed[:, s])
