@@ -38,10 +38,16 @@ def _check_rows(got, ref):
     assert bad[0].size == 0, f"{bad[0].size} rows off; worst err {err.max():.3e}"
 
 
+_MATS = {}
+
+
 def _matrix(lrs, qt, rows, cols, seed):
-    rng = np.random.default_rng(seed)
-    v = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
-    return lrs.QuantTensor.quantize(v, rows, cols, lrs.QuantType[qt])
+    """Quantized once per module (the host encoders are the slow part)."""
+    key = (qt, rows, cols, seed)
+    if key not in _MATS:
+        v = (np.random.default_rng(seed).standard_normal(rows * cols) * 0.02).astype(np.float32)
+        _MATS[key] = lrs.QuantTensor.quantize(v, rows, cols, lrs.QuantType[qt])
+    return _MATS[key]
 
 
 def _matvec_case(lrs, orc, backend, qt, rows, cols, seed):

@@ -44,23 +44,32 @@ def _check_rows(got, ref):
     assert bad[0].size == 0, f"{bad[0].size} rows off; worst err {err.max():.3e}"
 
 
+_MATS = {}
+
+
+def _matrix(lrs, qt, rows, cols):
+    """Quantized once per module (the host encoders are the slow part)."""
+    key = (qt, rows, cols)
+    if key not in _MATS:
+        v = (np.random.default_rng(31).standard_normal(rows * cols) * 0.02).astype(np.float32)
+        _MATS[key] = lrs.QuantTensor.quantize(v, rows, cols, lrs.QuantType[qt])
+    return _MATS[key]
+
+
 @pytest.mark.parametrize("shape", [(1000, 512), (300, 3584), (4864, 896 * 2), (18944, 3584)],
                          ids=str)
 @pytest.mark.parametrize("batch", [5, 17, 33, 64])
 @pytest.mark.parametrize("qt", ["Q4_K", "Q6_K"])
 def test_fused_tc_matvec_batched(lrs, orc, backend, qt, shape, batch):
     rows, cols = shape
-    rng = np.random.default_rng(31)
-    v = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
-    t = lrs.QuantTensor.quantize(v, rows, cols, lrs.QuantType[qt])
-    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    t = _matrix(lrs, qt, rows, cols)
+    x = np.random.default_rng(32).standard_normal((batch, cols)).astype(np.float32)
     got = backend.matvec_batched(t, x)
     for b in sorted({0, batch // 2, batch - 1}):
         ref = orc.matvec(orc.SCALAR, t.data, int(t.quant_type), rows, cols, x[b])
         _check_rows(got[b], ref)
     again = backend.matvec_batched(t, x)  # counters were left at zero
     assert np.array_equal(got, again)
-    backend.release(t)
 
 
 def _cfg(lrs, hidden, inter, heads, kv, layers, vocab, hd, tied):
