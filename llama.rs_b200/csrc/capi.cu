@@ -350,6 +350,8 @@ struct Layer {
   // shard holds whole blocks [c0 - lo, c0 - lo + cols); when that is wider
   // than the rank's columns, x is zero-padded to it (launch_pad_copy).
   int o_lo = 0, d_lo = 0;
+  // the widest o / down shard over all ranks (the fused TP GEMV plans from it)
+  int o_plan = 0, d_plan = 0;
   float *in_norm = nullptr, *post_norm = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr;
   void *kpool = nullptr, *vpool = nullptr;
 };
@@ -592,8 +594,9 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   // batch-1 decode with the stream GEMV: the o / down projections push their
   // partials to the peers themselves and reduce in the same kernel
   const bool fused_tp = tp && m->tp_p2p && B == 1 && gemv_stream_enabled();
-  auto fused_tp_args = [&]() {
+  auto fused_tp_args = [&](int plan_cols) {
     StreamTp t;
+    t.plan_cols = plan_cols;
     t.peer_x = const_cast<float* const*>(m->d_parts + (size_t)(ar_calls & 1) * m->tp_world);
     t.local_sig = m->tp_sig + kTpSigFused;
     t.peer_sig = m->d_peer_sig;
@@ -680,7 +683,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x_ld = L.o.cols;
     }
     if (fused_tp) {
-      const StreamTp t = fused_tp_args();
+      const StreamTp t = fused_tp_args(L.o_plan);
       LRS_CUDA(model_gemv(m, p, st, sms, &t));
       ar_calls++;
     } else {
@@ -728,7 +731,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x_ld = L.down.cols;
     }
     if (fused_tp) {
-      const StreamTp t = fused_tp_args();
+      const StreamTp t = fused_tp_args(L.d_plan);
       LRS_CUDA(model_gemv(m, p, st, sms, &t));
       ar_calls++;
     } else {
@@ -811,6 +814,19 @@ lrs_tensor_desc rows_of(const lrs_tensor_desc& d, size_t r0, size_t n) {
 // blocks' values outside the window meet zeros in x, so the shard's dot
 // equals the window's (blocks are never re-encoded: the bytes stay the
 // reference's).
+// The widest column window (whole blocks of `type`, as cols_of takes them)
+// over the shards [q * n, q * n + n) of ranks q < world.
+int widest_window(uint32_t type, size_t n, int world) {
+  uint32_t bv = 0, bb = 0;
+  if (!type_geometry(type, &bv, &bb)) return (int)n;
+  size_t w = 0;
+  for (int q = 0; q < world; q++) {
+    const size_t c0 = (size_t)q * n, a0 = c0 / bv * bv, a1 = (c0 + n + bv - 1) / bv * bv;
+    w = std::max(w, a1 - a0);
+  }
+  return (int)w;
+}
+
 int32_t cols_of(const lrs_tensor_desc& d, size_t c0, size_t n, const char* what,
                 std::vector<uint8_t>* buf, lrs_tensor_desc* out, int* lo) {
   uint32_t bv = 0, bb = 0;
@@ -1041,6 +1057,8 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         (rc = load_mat(s.up_proj, pre + ".mlp.up_proj.weight", rank * I, I, 0, h, &L.up, &lo_unused)) ||
         (rc = load_mat(s.down_proj, pre + ".mlp.down_proj.weight", 0, h, rank * I, I, &L.down, &L.d_lo)))
       return cleanup(rc);
+    L.o_plan = widest_window(L.o.type, qw, world);
+    L.d_plan = widest_window(L.down.type, I, world);
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
         (rc = upload_vec(m.get(), s.q_bias ? s.q_bias + rank * qw : nullptr, qw, &L.qb)) ||

@@ -92,6 +92,7 @@ struct StreamTp {
   int* const* peer_sig;   // [world] every rank's signal words (bases)
   unsigned* counters;     // [kTpMaxGrid] this rank's launches per CTA index (zero at creation)
   int rank, world, rows;
+  int plan_cols;          // the widest shard of this projection over all ranks (>= cols)
   int* error_flag;
 };
 

@@ -519,18 +519,28 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
   const int ub = dense ? (int)(bb * 32) : (int)bb;
   const int uv = dense ? 32 : (int)bv;
   const int units = p0.cols / uv;
-  if (tp && (pair || p0.nseg != 1 || p0.batch != 1)) return cudaErrorInvalidValue;
+  if (tp && (pair || p0.nseg != 1 || p0.batch != 1 || tp->plan_cols < p0.cols))
+    return cudaErrorInvalidValue;
   const void* kernel = stream_kernel(type, pair, tp != nullptr);
-  const size_t xbytes = x_bytes_of(type, p0.cols);
+  // The tensor-parallel variant reduces CTA b's rows after CTA b of every
+  // peer signalled, so all ranks need the same tiles and grid: those are
+  // planned from plan_cols, the same on every rank (windowed shards of one
+  // projection may cover different numbers of blocks).
+  const int plan_cols = tp ? tp->plan_cols : p0.cols;
+  const int plan_units = plan_cols / uv;
+  const size_t xbytes = x_bytes_of(type, plan_cols);
   if (!kernel || units < 1) return cudaErrorInvalidValue;
 
   StreamShape sh = {};
-  sh.units = units;
   // K-chunks: whole rows while R rows of every matrix fit one item.
-  sh.kc = std::max(1, std::min(units, kItemMaxBytes / (nm * R * ub)));
-  sh.nchunk = (units + sh.kc - 1) / sh.kc;
-  sh.kc = (units + sh.nchunk - 1) / sh.nchunk;  // even chunks
-  sh.mreg = ((sh.kc * ub + 15) & ~15) + 32;
+  auto chunk = [&](int n, int cap) {
+    sh.units = n;
+    sh.kc = std::max(1, std::min(n, cap));
+    sh.nchunk = (n + sh.kc - 1) / sh.kc;
+    sh.kc = (n + sh.nchunk - 1) / sh.nchunk;  // even chunks
+    sh.mreg = ((sh.kc * ub + 15) & ~15) + 32;
+  };
+  chunk(plan_units, kItemMaxBytes / (nm * R * ub));
 
   int total_rows = 0;
   for (int i = 0; i < p0.nseg; i++) total_rows += p0.seg[i].rows;
@@ -557,8 +567,14 @@ cudaError_t gemv_stream_launch(const GemvParams& p0, cudaStream_t stream, int nu
       break;
     }
   }
-  const int smem = stream_layout(sh, xbytes);
-  if (smem > 227 * 1024) return cudaErrorNotSupported;  // x too wide for this kernel
+  if (stream_layout(sh, xbytes) > 227 * 1024) return cudaErrorNotSupported;  // x too wide
+  if (units != plan_units) {
+    // this rank's shard: chunks no longer than the plan's, so the item and
+    // the staged x stay within the planned layout (same stages and tiles)
+    chunk(units, sh.kc);
+    sh.item_bytes = nm * sh.rt * sh.mreg;
+  }
+  const int smem = stream_layout(sh, x_bytes_of(type, p0.cols));
 
   GemvParams q = p0;
   int tile0 = 0;

@@ -1,4 +1,5 @@
-"""Tensor-parallel decode (the c4 layout) on 2 GPUs against the oracle.
+"""Tensor-parallel decode (the c4 layout) on 2 GPUs (4 for the uneven shards)
+against the oracle.
 
 Each rank is a separate process with its own GPU; rank 0 makes the NCCL id
 and every rank passes the full model.  Bars: final logits within 2e-2 of the
@@ -50,10 +51,14 @@ SHAPES = {
     # o's and down's column shards are 2.5 and 5.5 Q4_K super-blocks wide: the
     # ranks hold the covering blocks and zero-pad x (the c4 layout at TP8)
     "windowed": ([1280, 2816, 10, 2, 2, 2048, 1e-6, 1e6, 4096, 128, False], "Q4K"),
+    # at TP=4, o's shards are 1.75 super-blocks (the ranks cover 2 or 3) and
+    # down's 2.75 (3 or 4): shards of one projection differ in width
+    "uneven4": ([1792, 2816, 28, 4, 2, 2048, 1e-6, 1e6, 4096, 64, False], "Q4K"),
 }
+WORLD = {"uneven4": 4}
 
 
-@pytest.mark.parametrize("shape", ["aligned", "windowed"])
+@pytest.mark.parametrize("shape", ["aligned", "windowed", "uneven4"])
 @pytest.mark.parametrize("allreduce", ["nccl", "p2p", "fused"])
 def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
     """allreduce="p2p": the row-split projections are summed by the peer-memory
@@ -62,9 +67,10 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
     the peers and reduces in the same kernel (LRS_GEMV_STREAM=1), while the
     prefill and the batch of three keep the separate all-reduce."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    if (allreduce != "nccl" or shape == "windowed") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
+    world = WORLD.get(shape, 2)
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if (allreduce != "nccl" or shape != "aligned") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
         pytest.skip("the peer-memory all-reduce and windowed shards run with LRS_TEST_NEW_KERNELS=1")
     dims, recipe = SHAPES[shape]
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0"}
@@ -72,7 +78,6 @@ def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
         env["LRS_TP_P2P"] = "1"
     if allreduce == "fused":
         env["LRS_GEMV_STREAM"] = "1"
-    world = 2
     tp_id = lrs.tp_unique_id().hex()
     procs, outs = [], []
     for r in range(world):
