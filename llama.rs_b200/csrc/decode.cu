@@ -458,13 +458,19 @@ __global__ void __launch_bounds__(kA3Warps * 32)
     policy = evict_first_policy();
     for (int st = 0; st < kA3Stages; st++) mbar_init(&full[st], 1);
     fence_barrier_init();
-    for (; issued < kA3Stages && issued < nblk; issued++) issue(issued, policy);
+    // A fused decode step reads rows of earlier steps only (its own new row
+    // is replaced below), so the first copies may start before the previous
+    // kernel (programmatic dependent launch) has finished.  Unfused,
+    // rope_store_kernel just wrote rows of this step (a prefill chunk's
+    // positions): those copies wait for it.
+    if (fuse)
+      for (; issued < kA3Stages && issued < nblk; issued++) issue(issued, policy);
     flags[0] = 0;
     flags[1] = 0;
   }
-  // the copies above read old positions only (or a row replaced below): the
-  // rest waits for the previous kernel (programmatic dependent launch)
   pdl_wait();
+  if (tid == 0)
+    for (; issued < kA3Stages && issued < nblk; issued++) issue(issued, policy);
   pdl_launch_dependents();
   const int pnew = L - 1;  // this step's position
   float* knew = reinterpret_cast<float*>(smem + S::kNewOff);
