@@ -17,7 +17,9 @@
  * Device limit: 1 <= top_k <= LRS_SAMPLE_MAX_TOP_K (or top_k >= vocab when the
  * vocabulary itself is that small); top_k = 0 (off) and larger values return
  * LRS_ERR_UNSUPPORTED, and the shim keeps the reference's host sampler for
- * them.  temperature <= 0 is the greedy argmax whatever top_k is.
+ * them, as for vocabularies above about 1.39 million tokens (the device's
+ * seen-token bitmap must fit in shared memory).  temperature <= 0 is the
+ * greedy argmax whatever top_k is.
  */
 #ifndef LLAMARS_SAMPLE_H
 #define LLAMARS_SAMPLE_H
@@ -38,7 +40,7 @@ typedef struct lrs_sampler {
 } lrs_sampler;
 
 /* validate_sampling (src/engine.rs:327-339), with its messages; plus the
- * device limit on top_k (LRS_ERR_UNSUPPORTED).  No CUDA call. */
+ * device limits on top_k and the vocabulary (LRS_ERR_UNSUPPORTED).  No CUDA call. */
 lrs_status lrs_sampler_check(const lrs_sampler* params, size_t vocab);
 
 /* Samples from `vocab` logits in device memory (d_logits) on the backend

@@ -29,6 +29,7 @@ namespace {
 
 constexpr int kSampleThreads = 1024;
 constexpr int kBins = 2048;
+constexpr size_t kSampleMaxSmem = 227 * 1024;  // dynamic shared memory of one CTA
 
 struct SampleArgs {
   const float* logits;
@@ -314,6 +315,8 @@ extern "C" lrs_status lrs_sampler_check(const lrs_sampler* p, size_t vocab) {
   if (!std::isfinite(p->repetition_penalty) || p->repetition_penalty <= 0.0f)
     return fail(LRS_ERR_INVALID, "repetition_penalty must be finite and positive");
   if (vocab == 0 || vocab > (1u << 24)) return fail(LRS_ERR_INVALID, "vocabulary size out of range");
+  if (sample_smem(vocab) > kSampleMaxSmem)  // the seen bitmap lives in shared memory
+    return fail(LRS_ERR_UNSUPPORTED, "device sampler: vocabulary too large (the host sampler applies)");
   const size_t k = p->top_k == 0 || p->top_k >= vocab ? vocab : p->top_k;
   if (p->temperature > 0.0f && k > LRS_SAMPLE_MAX_TOP_K)
     return fail(LRS_ERR_UNSUPPORTED, "device sampler: top_k must be in 1.." +

@@ -126,6 +126,11 @@ def test_validation_messages(lrs):
     assert e.value.code == 2  # LRS_ERR_UNSUPPORTED
     lrs.sampler_check(S(top_k=0), 3000)      # the vocabulary itself is small enough
     lrs.sampler_check(S(temperature=0.0, top_k=0), 151936)  # greedy: top_k unused
+    # the seen bitmap of the device sampler is in shared memory
+    lrs.sampler_check(S(temperature=0.0), 1 << 20)
+    with pytest.raises(lrs.LrsError, match="vocabulary too large") as e:
+        lrs.sampler_check(S(temperature=0.0), 1 << 22)
+    assert e.value.code == 2
 
 
 gpu_gate = pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
