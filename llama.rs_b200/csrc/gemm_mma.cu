@@ -622,14 +622,9 @@ constexpr size_t smem_for() {
 
 template <int T, bool PAIR, int NT>
 cudaError_t launch_t(const GemmArgs& a, dim3 grid, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_mma_kernel<T, PAIR, NT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem_for<NT>());
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  cudaError_t e = set_smem_once(attr, (const void*)gemm_mma_kernel<T, PAIR, NT>, (int)smem_for<NT>());
+  if (e != cudaSuccess) return e;
   gemm_mma_kernel<T, PAIR, NT><<<grid, Shape<PAIR>::kThreads, smem_for<NT>(), st>>>(a);
   return cudaGetLastError();
 }

@@ -727,13 +727,9 @@ int tc_kgroups(const GemvParams& p, int sms) {
 template <int T, int NI, bool FUSED, bool RAW = false>
 cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
   using S = TcShape<T, NI, RAW>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, NI, FUSED, RAW>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  cudaError_t e = set_smem_once(attr, (const void*)gemm_tc_kernel<T, NI, FUSED, RAW>, S::kSmem);
+  if (e != cudaSuccess) return e;
   if constexpr (!FUSED) {
     gemm_tc_kernel<T, NI, false, RAW><<<grid, S::kThreads, S::kSmem, st>>>(a);
     return cudaGetLastError();

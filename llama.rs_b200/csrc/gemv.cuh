@@ -3,7 +3,23 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace lrs {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `kernel`, once per
+// device: the attribute belongs to the current device's context.  `done`
+// holds one bit per device ordinal (static per kernel at the call site).
+inline cudaError_t set_smem_once(std::atomic<uint64_t>& done, const void* kernel, int smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 enum GemvEpilogue : int {
   EPI_STORE = 0,   // out[b][r] = y (+ bias[r])           LinearLayer::forward, src/model.rs:33-46
