@@ -70,9 +70,12 @@ constexpr uint32_t kTmemCols = 512;
 // f16, accumulated into the same TMEM columns; two A and two x buffers.
 //
 // RAW (Q4_K only, opt-in): a loader warp copies each super-block's 128 raw
-// rows (144 bytes each, 16-byte aligned) into a two-stage shared-memory ring
-// with cp.async.bulk, and the producers decode from there instead of holding
-// the next super-block in registers; two x buffers make the room.
+// rows (144 bytes each, 16-byte aligned) into a shared-memory ring with
+// cp.async.bulk, and the producers decode from there instead of holding the
+// next super-block in registers; two x buffers and two A buffers make the
+// room.  The ring takes what shared memory is left, up to 5 stages (4 at 64
+// items): at the weight-streaming rate an SM consumes a super-block every
+// ~0.4 us, against 1-2 us of DRAM latency under load.
 template <int T, int NI, bool RAW = false>
 struct TcShape {
   static constexpr int kN = 2 * NI;
@@ -80,15 +83,20 @@ struct TcShape {
   static constexpr int kTileBmin = tile_bmin(NI);
   static constexpr bool kMins = T == LRS_GGML_Q4_K;
   static constexpr int kAParts = T == LRS_GGML_Q6_K ? 2 : 1;  // A tiles per half step
-  static constexpr int kAB = T == LRS_GGML_Q6_K ? 2 : 3;      // A buffers
+  // A buffers: RAW producers decode from shared memory, so two suffice and
+  // the third goes to the raw ring
+  static constexpr int kAB = T == LRS_GGML_Q6_K || RAW ? 2 : 3;
   static constexpr int kBB = T == LRS_GGML_Q6_K || RAW ? 2 : 3;  // x buffers
-  static constexpr int kRawStages = RAW ? 2 : 0;
   static constexpr int kRawStage = kRows * 144;  // one super-block of 128 Q4_K rows
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kAB * kAParts * kTileA;
   static constexpr int kOffAmin = kOffB + kBB * kTileB;
   static constexpr int kOffBmin = kOffAmin + (kMins ? 2 * kTileMin : 0);
   static constexpr int kOffRaw = kOffBmin + (kMins ? 2 * kTileBmin : 0);
+  static constexpr int kRawFit = (227 * 1024 - 256 - kOffRaw) / kRawStage;
+  static constexpr int kRawStages = RAW ? (kRawFit < 5 ? kRawFit : 5) : 0;
+  static_assert(!RAW || kRawStages >= 2, "the raw ring needs two stages");
+  static constexpr int kRawRing = RAW ? kRawStages : 1;  // divisor in code only RAW runs
   static constexpr int kOffBar = kOffRaw + kRawStages * kRawStage;
   static constexpr int kSmem = kOffBar + (RAW ? 256 : 128);
   static constexpr int kBytes = T == LRS_GGML_Q6_K ? 210 : 144;
@@ -355,8 +363,9 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
   uint64_t* mma_done = bars + 6;    // [kAB] MMAs of a half step finished (A, x buffers free)
   uint64_t* acc_full = bars + 9;    // [2] super-block accumulator ready
   uint64_t* acc_empty = bars + 11;  // [2] epilogue finished reading it
-  uint64_t* raw_full = bars + 13;   // [2] RAW: a super-block's rows landed
-  uint64_t* raw_empty = bars + 15;  // [2] RAW: the producers finished with them
+  uint64_t* raw_full = bars + 13;                   // [kRawStages] RAW: a super-block's rows landed
+  uint64_t* raw_empty = bars + 13 + S::kRawStages;  // [kRawStages] RAW: the producers finished with them
+  static_assert(13 + 2 * S::kRawStages <= (RAW ? 32 : 16), "barrier area");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = smem_u32(smem);
 
@@ -369,10 +378,10 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
-      if (RAW) {
-        mbar_init(&raw_full[i], 1);
-        mbar_init(&raw_empty[i], 256);
-      }
+    }
+    for (int i = 0; i < S::kRawStages; i++) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 256);
     }
     fence_barrier_init();
   }
@@ -406,8 +415,8 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     for (int sb = 0; sb < nsb && ok; sb++) {
       if constexpr (RAW) {
         // this super-block's rows from the ring (row r at r * 144: conflict-free)
-        const int rs = sb & 1;
-        ok = mbar_wait_bounded(&raw_full[rs], (uint32_t)((sb >> 1) & 1));
+        const int rs = sb % S::kRawRing;
+        ok = mbar_wait_bounded(&raw_full[rs], (uint32_t)((sb / S::kRawRing) & 1));
         if (!ok) break;
         const uint8_t* u = smem + S::kOffRaw + rs * S::kRawStage + r * 144;
         cur.v[0] = *reinterpret_cast<const uint4*>(u);
@@ -625,9 +634,10 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     // ---------------- raw loader: super-block rows into the ring ----------------
     const uint64_t pol = evict_first_policy();
     for (int sb = 0; sb < nsb && ok; sb++) {
-      const int rs = sb & 1;
-      if (sb >= 2) {
-        if (lane == 0) ok = mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((sb - 2) >> 1) & 1));
+      const int rs = sb % S::kRawRing;
+      if (sb >= S::kRawRing) {
+        if (lane == 0)
+          ok = mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((sb - S::kRawRing) / S::kRawRing) & 1));
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
       }
