@@ -116,7 +116,9 @@ lrs_status lrs_matvec_batched(lrs_backend* backend, const lrs_tensor* weight, co
  * held by every GPU that loads the library until exit) and allocates nothing.
  * Limits: cols <= 65536, rows <= 262144 (larger matrices: LRS_ERR_INVALID).
  * The first call on a device looks up the array's address there; make it
- * before any stream capture.  All calls on a device share the array: calls
+ * before any stream capture.  That address is cached for the life of the
+ * process: it assumes the device's primary context is never reset
+ * (cudaDeviceReset) while the library is loaded.  All calls on a device share the array: calls
  * whose GPU work overlaps race, so callers on several threads must serialize
  * them.  Synchronous; same validation and results as lrs_matvec. */
 lrs_status lrs_matvec_noalloc(lrs_backend* backend, const lrs_tensor* weight, const float* in,

@@ -13,7 +13,9 @@
 // Properties a caller must know:
 // * The first call on a device looks up that device's address of the array
 //   (cudaGetSymbolAddress, with the device current) and caches it.  Make that
-//   first call before any stream capture is started.
+//   first call before any stream capture is started.  The cached address
+//   assumes the device's primary context lives as long as the process (no
+//   cudaDeviceReset while the library is loaded).
 // * Every call on a device shares the one array, which keeps the previous
 //   call's contents; calls whose GPU work overlaps in time race with each
 //   other.  The call is synchronous, so calls from one host thread never
