@@ -31,15 +31,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
 
-# Opt-in kernels (read by the library at launch time): the bulk-copy batch-1
-# GEMV, the streamed decode attention, the tcgen05 matmul's fused output step
-# and its raw-row ring.
-STREAM_GEMV = os.environ.get("LRS_GEMV_STREAM") == "1"
-ATTN_V3 = os.environ.get("LRS_ATTN_V3") == "1"
-TC_FUSED = os.environ.get("LRS_TC_FUSED") == "1"
-TC_RAW = os.environ.get("LRS_TC_RAW") == "1"
-TP_P2P = os.environ.get("LRS_TP_P2P") == "1"
-
 def load_pkg():
     import importlib.util
     if "llamars_b200" in sys.modules:
@@ -188,12 +179,7 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
                          f"data-parallel over {world} GPU(s)"),
             "parallelism": f"tp{world}" if tp else f"dp{world}",
             "sequences_per_gpu": total_seqs if tp else total_seqs // max(world, 1), "prompt": P,
-            "kv_cache": "bf16" if kv_bf16 else "f32",
-            "kernels": {"gemv_b1": "stream" if STREAM_GEMV else "direct",
-                        "attention": "v3" if ATTN_V3 else "v2",
-                        "matmul_tc": "+".join(["tcgen05"] + (["fused"] if TC_FUSED else []) +
-                                              (["raw"] if TC_RAW else [])),
-                        "tp_allreduce": "p2p" if TP_P2P else "nccl"}}
+            "kv_cache": "bf16" if kv_bf16 else "f32"}
 
 
 def run_reference(args, wl):
@@ -403,14 +389,11 @@ def run_ours(args, wl):
                          "frac": achieved / hbm, "traffic": None,
                          "kernel": ("gemm_tc_kernel (tcgen05, Q4_K/Q6_K) + gemm_mma_kernel (Q8_0): batched quantized matmul (x split, matmul, "
                                     "K-split epilogue) of every projection and the LM head"
-                                    if B > 1 else
-                                    ("gemv_stream_kernel: batch-1 quantized GEMV, bulk-copy ring"
-                                     if STREAM_GEMV else "gemv5_kernel: batch-1 quantized GEMV")),
+                                    if B > 1 else "gemv5_kernel: batch-1 quantized GEMV"),
                          "bytes_per_launch": wbytes / gemv_n, "ms_per_launch": gemv_ms / gemv_n,
                          "launches": gemv_n, "peak_kind": peak_kind,
                          "share_of_step": gemv_ms / prof_step_ms},
-            "attention": {"kernel": ("rope_store + attn3 (bulk-copy ring, combine in the last CTA), all layers"
-                                     if ATTN_V3 else "rope_store + attn_split + attn_combine, all layers"),
+            "attention": {"kernel": "rope_store + attn_split + attn_combine, all layers",
                           "kv_bytes_per_step": kv_bytes, "ms": attn_ms,
                           "achieved_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
                           "frac": kv_bytes / (attn_ms / 1e3) / 1e9 / hbm,

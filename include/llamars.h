@@ -187,7 +187,11 @@ typedef struct lrs_model_options {
   uint32_t use_graph;     /* capture decode steps in a CUDA graph (1 = yes) */
   uint32_t device_recipe; /* LRS_RECIPE_* (llamars_synth.h): F32/F16/BF16 matrices are encoded
                              on the GPU at creation (maybe_quantize, src/loader.rs:406-447); 0 = as given */
+  uint32_t tp_allreduce;  /* tensor-parallel models: LRS_TP_ALLREDUCE_NCCL (default) or
+                             LRS_TP_ALLREDUCE_P2P (one kernel over peer memory) */
 } lrs_model_options;
+
+enum { LRS_TP_ALLREDUCE_NCCL = 0, LRS_TP_ALLREDUCE_P2P = 1 };
 
 typedef struct lrs_model lrs_model;
 

@@ -20,6 +20,7 @@ from __future__ import annotations
 import ctypes as C
 import enum
 import os
+import weakref
 from dataclasses import dataclass, field
 from typing import Optional, Sequence
 
@@ -131,7 +132,7 @@ class _ModelDesc(C.Structure):
 class _ModelOptions(C.Structure):
     _fields_ = [("max_seq_len", C.c_uint32), ("max_sequences", C.c_uint32),
                 ("kv_dtype", C.c_uint32), ("use_graph", C.c_uint32),
-                ("device_recipe", C.c_uint32)]
+                ("device_recipe", C.c_uint32), ("tp_allreduce", C.c_uint32)]
 
 
 class _SynthSpec(C.Structure):
@@ -381,8 +382,11 @@ class CudaBackend:
         self._h = h
         self.device = device
         self._cache = {}
+        self._models = weakref.WeakSet()  # models on this backend: destroyed first
 
     def close(self):
+        for m in list(self._models):
+            m.close()
         for _, (t, _keep) in list(self._cache.items()):
             _lib.lrs_tensor_free(t)
         self._cache.clear()
@@ -671,13 +675,14 @@ class CudaQwen2Model:
     def __init__(self, backend: CudaBackend, desc, max_seq_len: int = 4096,
                  max_sequences: int = 1, kv_bf16: bool = False, use_graph: bool = True,
                  keepalive=None, tp_rank: int = 0, tp_world: int = 1, tp_id: bytes = b"",
-                 device_recipe: LoadQuantization = LoadQuantization.NONE):
+                 device_recipe: LoadQuantization = LoadQuantization.NONE,
+                 tp_p2p: bool = False):
         """tp_world > 1 makes this process shard tp_rank of a tensor-parallel
         model (every rank passes the full desc and the same tp_id, made once by
         tp_unique_id() and shared out of band).  device_recipe encodes the
         desc's F32/F16/BF16 matrices on the GPU (the load-time recipe)."""
         opts = _ModelOptions(max_seq_len, max_sequences, 1 if kv_bf16 else 0,
-                             1 if use_graph else 0, int(device_recipe))
+                             1 if use_graph else 0, int(device_recipe), 1 if tp_p2p else 0)
         h = _P()
         if tp_world > 1:
             if len(tp_id) != 128:
@@ -688,6 +693,7 @@ class CudaQwen2Model:
             _check(_lib.lrs_model_create(backend.handle, desc, C.byref(opts), C.byref(h)))
         self._h = h
         self.backend = backend
+        backend._models.add(self)
         self.keepalive = keepalive
         cfg = desc.contents.config
         self.vocab_size = cfg.vocab_size
@@ -695,9 +701,10 @@ class CudaQwen2Model:
         self.max_sequences = max_sequences
 
     def close(self):
-        if self._h:
+        # a model must go before its backend; the backend's close() closes it first
+        if self._h and self.backend._h:
             _lib.lrs_model_destroy(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:

@@ -291,7 +291,7 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
   p.x_ld = w->t.cols;
   p.error_flag = be->d_err;
   if (batch > 1 && gemm_supported(p)) {
-    const size_t need = gemm_scratch_bytes((int)batch, w->t.cols, be->sms) + kScratchCounterBytes;
+    const size_t need = gemm_scratch_bytes((int)batch, w->t.cols, be->sms);
     if (be->scratch_cap < need) {
       cudaFree(be->d_scratch);  // synchronizes with work that may still use it
       be->d_scratch = nullptr;
@@ -350,8 +350,6 @@ struct Layer {
   // shard holds whole blocks [c0 - lo, c0 - lo + cols); when that is wider
   // than the rank's columns, x is zero-padded to it (launch_pad_copy).
   int o_lo = 0, d_lo = 0;
-  // the widest o / down shard over all ranks (the fused TP GEMV plans from it)
-  int o_plan = 0, d_plan = 0;
   float *in_norm = nullptr, *post_norm = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr;
   void *kpool = nullptr, *vpool = nullptr;
 };
@@ -386,7 +384,6 @@ struct lrs_model {
   int max_items = 0, max_split = 64;
   float *residual = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
         *att = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
-  int* attn_cnt = nullptr;  // [max_items][kv heads] split counters of the attention combine
   float *att_pad = nullptr, *act_pad = nullptr;  // zero-padded x of windowed o / down shards
   // tensor parallelism over peer memory (LRS_TP_P2P=1): exchange buffers
   // [2][max_items * hidden], signal words [world], a launch counter, and the
@@ -395,7 +392,6 @@ struct lrs_model {
   float* xbuf = nullptr;
   int* tp_sig = nullptr;
   unsigned* tp_tickets = nullptr;
-  unsigned* tp_counters = nullptr;  // [kTpMaxGrid] launches per CTA index of the fused path
   const float** d_parts = nullptr;  // [2][world]
   int** d_peer_sig = nullptr;       // [world]
   std::vector<void*> ipc_opened;
@@ -432,16 +428,12 @@ int32_t model_alloc(lrs_model* m, void** p, size_t bytes) {
   return LRS_OK;
 }
 
-// One projection; with `tp` the batch-1 stream GEMV fused with the
-// tensor-parallel all-reduce (p.x and the plan as for the unfused launch).
-cudaError_t model_gemv(lrs_model* m, const GemvParams& p0, cudaStream_t st, int sms,
-                       const StreamTp* tp = nullptr) {
+// One projection (with per-launch events when profiling).
+cudaError_t model_gemv(lrs_model* m, const GemvParams& p0, cudaStream_t st, int sms) {
   GemvParams p = p0;
   p.scratch = m->gemm_scratch;
   p.scratch_bytes = m->gemm_scratch_bytes;
-  auto run = [&](bool pdl) {
-    return tp ? gemv_stream_launch(p, st, sms, pdl, tp) : gemv_launch(p, st, sms, pdl);
-  };
+  auto run = [&](bool pdl) { return gemv_launch(p, st, sms, pdl); };
   if (!m->prof) return run(true);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
@@ -475,11 +467,6 @@ int32_t upload_mat(const lrs_tensor_desc& d, size_t rows, size_t cols, const cha
   return upload(d.data, d.nbytes, rows, cols, d.ggml_type, out);
 }
 
-bool tp_p2p_requested() {
-  const char* e = getenv("LRS_TP_P2P");
-  return e && e[0] == '1';
-}
-
 // The peer-memory all-reduce: every rank allocates its exchange buffers and
 // signal words, the ranks swap CUDA IPC handles with one NCCL all-gather, and
 // each rank maps its peers' allocations (collective: all ranks call it).
@@ -490,18 +477,14 @@ int32_t setup_tp_p2p(lrs_model* m, int h) {
   // own cudaMalloc allocations: an IPC handle names the base of an allocation
   LRS_CUDA(cudaMalloc((void**)&m->xbuf, xcount * 4));
   m->allocs.push_back(m->xbuf);
-  // signal words: [0, world) for tp_allreduce_add_kernel, then
-  // [kTpSigFused + src * kTpMaxGrid + cta] for the fused stream GEMV
-  const size_t sig_bytes = (kTpSigFused + (size_t)world * kTpMaxGrid) * 4;
+  // signal words [0, world) of tp_allreduce_add_kernel
+  const size_t sig_bytes = (size_t)world * 4;
   LRS_CUDA(cudaMalloc((void**)&m->tp_sig, sig_bytes));
   m->allocs.push_back(m->tp_sig);
   LRS_CUDA(cudaMemset(m->tp_sig, 0, sig_bytes));
   int32_t rc;
-  if ((rc = model_alloc(m, (void**)&m->tp_tickets, 4)) ||
-      (rc = model_alloc(m, (void**)&m->tp_counters, kTpMaxGrid * 4)))
-    return rc;
+  if ((rc = model_alloc(m, (void**)&m->tp_tickets, 4))) return rc;
   LRS_CUDA(cudaMemset(m->tp_tickets, 0, 4));
-  LRS_CUDA(cudaMemset(m->tp_counters, 0, kTpMaxGrid * 4));
   if ((size_t)world > (size_t)m->max_items)
     return fail(LRS_ERR_UNSUPPORTED, "peer-memory all-reduce: more ranks than item slots");
   cudaIpcMemHandle_t mine[2];
@@ -591,22 +574,6 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   auto res_out = [&]() -> float* {
     return m->tp_p2p ? m->xbuf + (size_t)(ar_calls & 1) * m->max_items * h : m->residual;
   };
-  // batch-1 decode with the stream GEMV: the o / down projections push their
-  // partials to the peers themselves and reduce in the same kernel
-  const bool fused_tp = tp && m->tp_p2p && B == 1 && gemv_stream_enabled();
-  auto fused_tp_args = [&](int plan_cols) {
-    StreamTp t;
-    t.plan_cols = plan_cols;
-    t.peer_x = const_cast<float* const*>(m->d_parts + (size_t)(ar_calls & 1) * m->tp_world);
-    t.local_sig = m->tp_sig + kTpSigFused;
-    t.peer_sig = m->d_peer_sig;
-    t.counters = m->tp_counters;
-    t.rank = m->tp_rank;
-    t.world = m->tp_world;
-    t.rows = h;
-    t.error_flag = m->be->d_err;
-    return t;
-  };
   auto allreduce_residual = [&]() -> int32_t {
     if (tp && m->tp_p2p) {
       TpArgs a;
@@ -661,18 +628,13 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       m->prof_attn->push_back(a1);
       cudaEventRecord(a0, st);
     }
-    // decode steps (every item one new position of its own sequence) with the
-    // v3 attention: RoPE and the KV store happen inside the attention kernel
-    const bool fuse_rope = lm_item == -1 && attention_v3_enabled();
-    const AttnRope rope{m->k, m->v, m->rope_cos, m->rope_sin};
-    if (!fuse_rope)
-      LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
-                                 L.kpool, L.vpool, kv_bf16, st));
+    LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
+                               L.kpool, L.vpool, kv_bf16, st));
     LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
-                              m->att, m->attn_cnt, m->be->d_err, fuse_rope ? &rope : nullptr, st));
+                              m->att, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
-    GemvMat om = mat_of(L.o, fused_tp ? m->residual : res_out(), h);
+    GemvMat om = mat_of(L.o, res_out(), h);
     if ((rc = gemv_plan(&p, &om, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->att;
@@ -682,14 +644,8 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->att_pad;
       p.x_ld = L.o.cols;
     }
-    if (fused_tp) {
-      const StreamTp t = fused_tp_args(L.o_plan);
-      LRS_CUDA(model_gemv(m, p, st, sms, &t));
-      ar_calls++;
-    } else {
-      LRS_CUDA(model_gemv(m, p, st, sms));
-      if ((rc = allreduce_residual())) return rc;
-    }
+    LRS_CUDA(model_gemv(m, p, st, sms));
+    if ((rc = allreduce_residual())) return rc;
     // post_attention_layernorm + gate/up + SwiGLU (src/model.rs:241-254)
     bool xn_ready = false;
     auto ffn_input = [&](GemvParams& q) -> int32_t {
@@ -720,7 +676,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       LRS_CUDA(launch_swiglu(m->act, m->act2, (size_t)B * I, st));
     }
     // down_proj + residual (src/model.rs:255-260)
-    GemvMat dm = mat_of(L.down, fused_tp ? m->residual : res_out(), h);
+    GemvMat dm = mat_of(L.down, res_out(), h);
     if ((rc = gemv_plan(&p, &dm, 1, res_epi, B))) return rc;
     p.error_flag = m->be->d_err;
     p.x = m->act;
@@ -730,14 +686,8 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       p.x = m->act_pad;
       p.x_ld = L.down.cols;
     }
-    if (fused_tp) {
-      const StreamTp t = fused_tp_args(L.d_plan);
-      LRS_CUDA(model_gemv(m, p, st, sms, &t));
-      ar_calls++;
-    } else {
-      LRS_CUDA(model_gemv(m, p, st, sms));
-      if ((rc = allreduce_residual())) return rc;
-    }
+    LRS_CUDA(model_gemv(m, p, st, sms));
+    if ((rc = allreduce_residual())) return rc;
   }
   if (lm_item == -2) return LRS_OK;
   // final norm + lm_head (src/model.rs:263-268) fused with the greedy argmax
@@ -814,19 +764,6 @@ lrs_tensor_desc rows_of(const lrs_tensor_desc& d, size_t r0, size_t n) {
 // blocks' values outside the window meet zeros in x, so the shard's dot
 // equals the window's (blocks are never re-encoded: the bytes stay the
 // reference's).
-// The widest column window (whole blocks of `type`, as cols_of takes them)
-// over the shards [q * n, q * n + n) of ranks q < world.
-int widest_window(uint32_t type, size_t n, int world) {
-  uint32_t bv = 0, bb = 0;
-  if (!type_geometry(type, &bv, &bb)) return (int)n;
-  size_t w = 0;
-  for (int q = 0; q < world; q++) {
-    const size_t c0 = (size_t)q * n, a0 = c0 / bv * bv, a1 = (c0 + n + bv - 1) / bv * bv;
-    w = std::max(w, a1 - a0);
-  }
-  return (int)w;
-}
-
 int32_t cols_of(const lrs_tensor_desc& d, size_t c0, size_t n, const char* what,
                 std::vector<uint8_t>* buf, lrs_tensor_desc* out, int* lo) {
   uint32_t bv = 0, bb = 0;
@@ -1057,8 +994,6 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         (rc = load_mat(s.up_proj, pre + ".mlp.up_proj.weight", rank * I, I, 0, h, &L.up, &lo_unused)) ||
         (rc = load_mat(s.down_proj, pre + ".mlp.down_proj.weight", 0, h, rank * I, I, &L.down, &L.d_lo)))
       return cleanup(rc);
-    L.o_plan = widest_window(L.o.type, qw, world);
-    L.d_plan = widest_window(L.down.type, I, world);
     if ((rc = upload_vec(m.get(), s.input_layernorm, h, &L.in_norm)) ||
         (rc = upload_vec(m.get(), s.post_attention_layernorm, h, &L.post_norm)) ||
         (rc = upload_vec(m.get(), s.q_bias ? s.q_bias + rank * qw : nullptr, qw, &L.qb)) ||
@@ -1119,10 +1054,8 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->d_pos, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_seq, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_step, 4)) ||
-      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)) ||
-      (rc = model_alloc(m.get(), (void**)&m->attn_cnt, B * cl.num_key_value_heads * 4)))
+      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
     return cleanup(rc);
-  LRS_CUDA(cudaMemset(m->attn_cnt, 0, B * cl.num_key_value_heads * 4));
   {
     size_t ow = 0, dw = 0;
     for (const auto& L : m->layers) {
@@ -1154,10 +1087,9 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
         m->gemm_scratch_bytes = std::max(m->gemm_scratch_bytes, gemm_tc_scratch_bytes(p, m->be->sms));
     }
   }
-  m->gemm_scratch_bytes += kScratchCounterBytes;
   if ((rc = model_alloc(m.get(), &m->gemm_scratch, m->gemm_scratch_bytes))) return cleanup(rc);
-  LRS_CUDA(cudaMemset(m->gemm_scratch, 0, m->gemm_scratch_bytes));  // the tail counters start at zero
-  if (world > 1 && tp_p2p_requested() && (rc = setup_tp_p2p(m.get(), h))) return cleanup(rc);
+  if (world > 1 && opt.tp_allreduce == LRS_TP_ALLREDUCE_P2P && (rc = setup_tp_p2p(m.get(), h)))
+    return cleanup(rc);
   if (world > 1 &&
       (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))
     return cleanup(rc);

@@ -341,347 +341,6 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* part, con
   att[((size_t)b * nh + h) * HD + d] = O / Lsum;
 }
 
-// ---- split-K GQA decode attention, v3: K/V blocks streamed by bulk copies ----
-// One CTA per (split, kv head, item), 4 warps, as attn_split_kernel, but:
-// * the 32-position K and V blocks of the split (each contiguous in its page)
-//   arrive by cp.async.bulk into a ring of kA3Stages stages, issued by one
-//   thread as soon as a stage is free, so two blocks are in flight while one
-//   is consumed;
-// * warp w owns query heads w and w + 4 of the GQA group; lanes span the head
-//   dimension, so K and V rows are read from shared memory contiguously.  The
-//   32 per-lane partial dots of a block are transpose-reduced (31 shuffles) so
-//   that lane j holds the score of position j; the online softmax and the PV
-//   product follow per head, with no cross-warp merge;
-// * the cross-split combine runs in the CTA that finishes last for its
-//   (item, kv head) (a counter, reset by that CTA), in a fixed split order.
-constexpr int kA3Warps = 4;
-constexpr int kA3Stages = 3;
-
-template <int HD, bool BF16>
-struct A3Shape {
-  static constexpr int kRowBytes = HD * (BF16 ? 2 : 4);
-  static constexpr int kBlockBytes = 32 * kRowBytes;  // K or V block of 32 positions
-  static constexpr int kStageBytes = 2 * kBlockBytes;
-  static constexpr int kQOff = kA3Stages * kStageBytes;          // q [kMaxGroup][HD] f32
-  static constexpr int kPsOff = kQOff + kMaxGroup * HD * 4;      // ps [warps][2][32]
-  static constexpr int kBarOff = kPsOff + kA3Warps * 2 * 32 * 4;  // full[kA3Stages]
-  static constexpr int kFlagOff = kBarOff + kA3Stages * 8;        // abort, last
-  static constexpr int kNewOff = kFlagOff + 16;                   // rotated k, v of the new position
-  static constexpr int kSmem = kNewOff + 2 * HD * 4;
-};
-
-// DPL consecutive K or V values of a row in shared memory, as f32.
-template <int DPL, bool BF16>
-__device__ __forceinline__ void lds_row(const uint8_t* p, float* v) {
-  if constexpr (BF16) {
-    if constexpr (DPL == 4) {
-      const uint2 u = *reinterpret_cast<const uint2*>(p);
-      v[0] = __uint_as_float(u.x << 16), v[1] = __uint_as_float(u.x & 0xffff0000u);
-      v[2] = __uint_as_float(u.y << 16), v[3] = __uint_as_float(u.y & 0xffff0000u);
-    } else {
-      const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
-      v[0] = __uint_as_float(u << 16), v[1] = __uint_as_float(u & 0xffff0000u);
-    }
-  } else {
-    if constexpr (DPL == 4) {
-      const float4 t = *reinterpret_cast<const float4*>(p);
-      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
-    } else {
-      const float2 t = *reinterpret_cast<const float2*>(p);
-      v[0] = t.x, v[1] = t.y;
-    }
-  }
-}
-
-// v[0..2^k) across the warp -> lane l holds the warp sum of v[l] (for 32
-// values: 16 + 8 + 4 + 2 + 1 shuffles).
-__device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int k = 0; k < off; k++) {
-      const float send = upper ? v[k] : v[k + off];
-      const float keep = upper ? v[k + off] : v[k];
-      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
-
-// Decode steps fuse RoPE and the KV store (rope_store_kernel's work) when
-// rope != null: q is rotated as it is loaded, and the CTA whose split holds the
-// new position rotates its k, stores k and v into the cache and uses them in
-// place of that row of its block (the copy may predate the store).
-struct A3Rope {
-  const float* k;  // [B][nkv][HD] this step's k (not rotated)
-  const float* v;  // [B][nkv][HD]
-  const float* cos_t;
-  const float* sin_t;
-};
-
-template <int HD, bool BF16>
-__global__ void __launch_bounds__(kA3Warps * 32)
-    attn3_kernel(const float* q, StepIO io, int nh, int nkv, void* kpool, void* vpool,
-                 int nsplit, float scale, float* part, float* att, int* counters, int* error_flag,
-                 const A3Rope rope, int fuse) {
-  using S = A3Shape<HD, BF16>;
-  constexpr int DPL = HD / 32;
-  constexpr int ES = BF16 ? 2 : 4;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int G = nh / nkv;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int L = io.pos[b] + 1;
-  const int chunk = split_chunk(L, nsplit);
-  const int s0 = split * chunk, s1 = min(L, s0 + chunk);
-  if (s0 >= s1) return;  // a split past the context: not counted by the combine
-  const int nblk = (s1 - s0 + 31) / 32;
-  const int nact = min(nsplit, (L + chunk - 1) / chunk);
-  float* qs = reinterpret_cast<float*>(smem + S::kQOff);
-  float* ps = reinterpret_cast<float*>(smem + S::kPsOff);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-  int* flags = reinterpret_cast<int*>(smem + S::kFlagOff);  // [0] abort, [1] last CTA
-
-  auto issue = [&](int i, uint64_t policy) {
-    const int st = i % kA3Stages;
-    const size_t off = kv_offset(io, b, s0 + 32 * i, nkv, kvh, HD) * ES;
-    uint8_t* dst = smem + st * S::kStageBytes;
-    mbar_expect_tx(&full[st], 2 * S::kBlockBytes);
-    tma_load_1d(dst, reinterpret_cast<const uint8_t*>(kpool) + off, S::kBlockBytes, &full[st], policy);
-    tma_load_1d(dst + S::kBlockBytes, reinterpret_cast<const uint8_t*>(vpool) + off, S::kBlockBytes,
-                &full[st], policy);
-  };
-  uint64_t policy = 0;
-  int issued = 0;  // blocks whose copies thread 0 has issued
-  if (tid == 0) {
-    policy = evict_first_policy();
-    for (int st = 0; st < kA3Stages; st++) mbar_init(&full[st], 1);
-    fence_barrier_init();
-    // A fused decode step reads rows of earlier steps only (its own new row
-    // is replaced below), so the first copies may start before the previous
-    // kernel (programmatic dependent launch) has finished.  Unfused,
-    // rope_store_kernel just wrote rows of this step (a prefill chunk's
-    // positions): those copies wait for it.
-    if (fuse)
-      for (; issued < kA3Stages && issued < nblk; issued++) issue(issued, policy);
-    flags[0] = 0;
-    flags[1] = 0;
-  }
-  pdl_wait();
-  if (tid == 0)
-    for (; issued < kA3Stages && issued < nblk; issued++) issue(issued, policy);
-  pdl_launch_dependents();
-  const int pnew = L - 1;  // this step's position
-  float* knew = reinterpret_cast<float*>(smem + S::kNewOff);
-  float* vnew = knew + HD;
-  if (!fuse) {
-    for (int i = tid; i < kMaxGroup * HD; i += blockDim.x) {
-      const int g = i / HD, d = i % HD;
-      qs[i] = g < G ? q[((size_t)b * nh + kvh * G + g) * HD + d] * scale : 0.0f;
-    }
-  } else {
-    // apply_rope_inplace (src/model.rs:86-95), unfused like rope_store_kernel
-    constexpr int half = HD / 2;
-    const float* c = rope.cos_t + (size_t)pnew * half;
-    const float* sn = rope.sin_t + (size_t)pnew * half;
-    for (int i = tid; i < kMaxGroup * half; i += blockDim.x) {
-      const int g = i / half, d = i % half;
-      float r0 = 0.0f, r1 = 0.0f;
-      if (g < G) {
-        const float* qh = q + ((size_t)b * nh + kvh * G + g) * HD;
-        const float re = qh[d], im = qh[d + half];
-        r0 = __fsub_rn(__fmul_rn(re, c[d]), __fmul_rn(im, sn[d]));
-        r1 = __fadd_rn(__fmul_rn(re, sn[d]), __fmul_rn(im, c[d]));
-      }
-      qs[g * HD + d] = r0 * scale;
-      qs[g * HD + d + half] = r1 * scale;
-    }
-    if (s0 <= pnew && pnew < s1) {  // this split holds the new position
-      const float* kh = rope.k + ((size_t)b * nkv + kvh) * HD;
-      const float* vh = rope.v + ((size_t)b * nkv + kvh) * HD;
-      const size_t o = kv_offset(io, b, pnew, nkv, kvh, HD);
-      for (int d = tid; d < half; d += blockDim.x) {
-        const float re = kh[d], im = kh[d + half];
-        float k0 = __fsub_rn(__fmul_rn(re, c[d]), __fmul_rn(im, sn[d]));
-        float k1 = __fadd_rn(__fmul_rn(re, sn[d]), __fmul_rn(im, c[d]));
-        float v0 = vh[d], v1 = vh[d + half];
-        if constexpr (BF16) {
-          __nv_bfloat16* kp = reinterpret_cast<__nv_bfloat16*>(kpool) + o;
-          __nv_bfloat16* vp = reinterpret_cast<__nv_bfloat16*>(vpool) + o;
-          kp[d] = __float2bfloat16_rn(k0);
-          kp[d + half] = __float2bfloat16_rn(k1);
-          vp[d] = __float2bfloat16_rn(v0);
-          vp[d + half] = __float2bfloat16_rn(v1);
-          // what a later read of the cache returns
-          k0 = __bfloat162float(kp[d]), k1 = __bfloat162float(kp[d + half]);
-          v0 = __bfloat162float(vp[d]), v1 = __bfloat162float(vp[d + half]);
-        } else {
-          float* kp = reinterpret_cast<float*>(kpool) + o;
-          float* vp = reinterpret_cast<float*>(vpool) + o;
-          kp[d] = k0;
-          kp[d + half] = k1;
-          vp[d] = v0;
-          vp[d + half] = v1;
-        }
-        knew[d] = k0;
-        knew[d + half] = k1;
-        vnew[d] = v0;
-        vnew[d + half] = v1;
-      }
-    }
-  }
-  __syncthreads();
-
-  const int h0 = warp, h1 = warp + kA3Warps;  // this warp's heads of the group
-  const bool has0 = h0 < G, has1 = h1 < G;
-  float qa[2][DPL], o[2][DPL], m[2], l[2];
-#pragma unroll
-  for (int k = 0; k < DPL; k++) {
-    qa[0][k] = qs[(has0 ? h0 : 0) * HD + lane * DPL + k];
-    qa[1][k] = qs[(has1 ? h1 : 0) * HD + lane * DPL + k];
-    o[0][k] = o[1][k] = 0.0f;
-  }
-  m[0] = m[1] = -INFINITY;
-  l[0] = l[1] = 0.0f;
-
-  for (int i = 0; i < nblk; i++) {
-    const int st = i % kA3Stages, blk = s0 + 32 * i;
-    bool ok = true;
-    if (lane == 0) ok = mbar_wait_bounded(&full[st], (uint32_t)((i / kA3Stages) & 1));
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (!ok && lane == 0) {
-      flags[0] = 1;
-      if (error_flag) atomicExch(error_flag, LRS_ERR_DEVICE_TIMEOUT);
-    }
-    if (ok && has0) {
-      const uint8_t* kb = smem + st * S::kStageBytes;
-      const uint8_t* vb = kb + S::kBlockBytes;
-      const int nv = min(32, s1 - blk);
-      // the row of the new position comes from knew / vnew when fused
-      const int jn = fuse && pnew >= blk && pnew < blk + 32 ? pnew - blk : -1;
-      // scores: lane j ends with q . k_j for its heads
-      float p0[32], p1[32];
-#pragma unroll
-      for (int j = 0; j < 32; j++) {
-        float kv[DPL];
-        if (j == jn) {
-#pragma unroll
-          for (int k = 0; k < DPL; k++) kv[k] = knew[lane * DPL + k];
-        } else {
-          lds_row<DPL, BF16>(kb + j * S::kRowBytes + lane * DPL * ES, kv);
-        }
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-        for (int k = 0; k < DPL; k++) {
-          a0 = fmaf(qa[0][k], kv[k], a0);
-          a1 = fmaf(qa[1][k], kv[k], a1);
-        }
-        p0[j] = a0;
-        p1[j] = a1;
-      }
-      float sc[2];
-      sc[0] = transpose_reduce32(p0, lane);
-      sc[1] = has1 ? transpose_reduce32(p1, lane) : 0.0f;
-      const bool valid = lane < nv;
-      // online softmax per head (softmax_inplace, src/model.rs:298-313, streamed)
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        if (hh == 1 && !has1) break;
-        const float s = valid ? sc[hh] : -INFINITY;
-        float bm = s;
-        for (int w = 16; w >= 1; w >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, w));
-        const float mn = fmaxf(m[hh], bm);  // finite: position blk is valid
-        const float corr = m[hh] == -INFINITY ? 0.0f : expf(m[hh] - mn);
-        const float e = valid ? expf(s - mn) : 0.0f;
-        float es = e;
-        for (int w = 16; w >= 1; w >>= 1) es += __shfl_xor_sync(0xffffffffu, es, w);
-        l[hh] = l[hh] * corr + es;
-        m[hh] = mn;
-        ps[(warp * 2 + hh) * 32 + lane] = e;
-#pragma unroll
-        for (int k = 0; k < DPL; k++) o[hh][k] *= corr;
-      }
-      __syncwarp();
-      for (int j = 0; j < nv; j++) {
-        float vv[DPL];
-        if (j == jn) {
-#pragma unroll
-          for (int k = 0; k < DPL; k++) vv[k] = vnew[lane * DPL + k];
-        } else {
-          lds_row<DPL, BF16>(vb + j * S::kRowBytes + lane * DPL * ES, vv);
-        }
-        const float pj0 = ps[(warp * 2) * 32 + j];
-        const float pj1 = ps[(warp * 2 + 1) * 32 + j];
-#pragma unroll
-        for (int k = 0; k < DPL; k++) {
-          o[0][k] = fmaf(pj0, vv[k], o[0][k]);
-          o[1][k] = fmaf(pj1, vv[k], o[1][k]);
-        }
-      }
-      __syncwarp();
-    }
-    __syncthreads();  // every warp is done with stage st
-    if (flags[0]) {
-      // let the copies still in flight (blocks i + 1 .. issued - 1) land before leaving
-      if (tid == 0)
-        for (int j = i + 1; j < issued; j++)
-          mbar_wait_bounded(&full[j % kA3Stages], (uint32_t)((j / kA3Stages) & 1));
-      return;
-    }
-    if (tid == 0 && issued < nblk) {
-      fence_proxy_async();
-      issue(issued++, policy);
-    }
-  }
-
-  // this split's (m, l, o) per head; a single split writes the output directly
-#pragma unroll
-  for (int hh = 0; hh < 2; hh++) {
-    if (!(hh == 0 ? has0 : has1)) continue;
-    const int head = kvh * G + (hh == 0 ? h0 : h1);
-    if (nsplit == 1) {
-      const float inv = 1.0f / l[hh];
-#pragma unroll
-      for (int k = 0; k < DPL; k++)
-        att[((size_t)b * nh + head) * HD + lane * DPL + k] = o[hh][k] * inv;
-    } else {
-      float* pp = part + (((size_t)b * nh + head) * nsplit + split) * (HD + 2);
-      if (lane == 0) {
-        pp[0] = m[hh];
-        pp[1] = l[hh];
-      }
-#pragma unroll
-      for (int k = 0; k < DPL; k++) pp[2 + lane * DPL + k] = o[hh][k];
-    }
-  }
-  if (nsplit == 1) return;
-  __threadfence();
-  __syncthreads();
-  int* cnt = counters + (size_t)b * nkv + kvh;
-  if (tid == 0) flags[1] = atomicAdd(cnt, 1) == nact - 1;
-  __syncthreads();
-  if (!flags[1]) return;
-  __threadfence();
-  // combine (attn_combine_kernel's arithmetic): splits in order 0..nact-1
-  for (int idx = tid; idx < G * HD; idx += blockDim.x) {
-    const int g = idx / HD, d = idx % HD;
-    const int head = kvh * G + g;
-    const float* pp = part + ((size_t)b * nh + head) * nsplit * (HD + 2);
-    float M = -INFINITY;
-    for (int sp = 0; sp < nact; sp++) M = fmaxf(M, __ldcg(pp + sp * (HD + 2)));
-    float Ls = 0.0f, O = 0.0f;
-    for (int sp = 0; sp < nact; sp++) {
-      const float ms = __ldcg(pp + sp * (HD + 2));
-      const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
-      Ls += __ldcg(pp + sp * (HD + 2) + 1) * w;
-      O += __ldcg(pp + sp * (HD + 2) + 2 + d) * w;
-    }
-    att[((size_t)b * nh + head) * HD + d] = O / Ls;
-  }
-  if (tid == 0) *cnt = 0;  // ready for the next launch
-}
-
 __global__ void advance_kernel(const unsigned long long* keys, int* tok, int* pos, int batch,
                                int* step, int n_steps, uint32_t* tokens_out, uint32_t* last) {
   const int s = *step;
@@ -722,34 +381,8 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
   return cudaGetLastError();
 }
 
-bool attention_v3_enabled() {
-  const char* e = getenv("LRS_ATTN_V3");
-  return e && e[0] == '1';
-}
-
-template <int HD, bool BF16>
-const void* attn3_prepare() {
-  const void* k = (const void*)attn3_kernel<HD, BF16>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, A3Shape<HD, BF16>::kSmem);
-  return k;
-}
-
 int attention_ctas_per_sm(int hd, int kv_bf16) {
   int n = 1;
-  if (attention_v3_enabled()) {
-    const void* k3 = nullptr;
-    int smem = 0;
-    if (hd == 128) {
-      k3 = kv_bf16 ? attn3_prepare<128, true>() : attn3_prepare<128, false>();
-      smem = kv_bf16 ? A3Shape<128, true>::kSmem : A3Shape<128, false>::kSmem;
-    } else {
-      k3 = kv_bf16 ? attn3_prepare<64, true>() : attn3_prepare<64, false>();
-      smem = kv_bf16 ? A3Shape<64, true>::kSmem : A3Shape<64, false>::kSmem;
-    }
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k3, kA3Warps * 32, smem) != cudaSuccess)
-      return 1;
-    return n < 1 ? 1 : n;
-  }
   const void* k = hd == 128 ? (kv_bf16 ? (const void*)attn_split_kernel<128, true>
                                        : (const void*)attn_split_kernel<128, false>)
                             : (kv_bf16 ? (const void*)attn_split_kernel<64, true>
@@ -759,53 +392,11 @@ int attention_ctas_per_sm(int hd, int kv_bf16) {
   return n < 1 ? 1 : n;
 }
 
-template <int HD, bool BF>
-cudaError_t launch_attn3(dim3 grid, cudaStream_t st, const float* q, StepIO io, int nh, int nkv,
-                         void* kpool, void* vpool, int nsplit, float scale, float* part, float* att,
-                         int* counters, int* error_flag, const A3Rope& rope, int fuse) {
-  const void* k = attn3_prepare<HD, BF>();
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kA3Warps * 32);
-  cfg.dynamicSmemBytes = A3Shape<HD, BF>::kSmem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  void* args[] = {&q, &io, &nh, &nkv, &kpool, &vpool, &nsplit, &scale, &part, &att, &counters,
-                  &error_flag, const_cast<A3Rope*>(&rope), &fuse};
-  return cudaLaunchKernelExC(&cfg, k, args);
-}
-
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
-                             void* kpool, void* vpool, int kv_bf16, int nsplit,
-                             float* part, float* att, int* counters, int* error_flag,
-                             const AttnRope* rope, cudaStream_t st) {
+                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
+                             float* part, float* att, cudaStream_t st) {
   if (nh / nkv > kMaxGroup || nsplit > 64) return cudaErrorInvalidValue;
   const float scale = 1.0f / sqrtf((float)hd);
-  if (counters && attention_v3_enabled()) {
-    const dim3 g3(nsplit, nkv, batch);
-    A3Rope r{};
-    int fuse = 0;
-    if (rope) {
-      r = A3Rope{rope->k, rope->v, rope->cos_t, rope->sin_t};
-      fuse = 1;
-    }
-    if (hd == 128)
-      return kv_bf16 ? launch_attn3<128, true>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
-                                                part, att, counters, error_flag, r, fuse)
-                     : launch_attn3<128, false>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
-                                                 part, att, counters, error_flag, r, fuse);
-    if (hd == 64)
-      return kv_bf16 ? launch_attn3<64, true>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
-                                               part, att, counters, error_flag, r, fuse)
-                     : launch_attn3<64, false>(g3, st, q, io, nh, nkv, kpool, vpool, nsplit, scale,
-                                                part, att, counters, error_flag, r, fuse);
-    return cudaErrorInvalidValue;
-  }
-  if (rope) return cudaErrorInvalidValue;  // only the v3 kernel fuses RoPE
   dim3 g(nsplit, nkv, batch);
 #define LRS_ATTN(HD, BF)                                                                         \
   attn_split_kernel<HD, BF><<<g, kAttnWarps * 32, 0, st>>>(q, io, nh, nkv, kpool, vpool, nsplit, \

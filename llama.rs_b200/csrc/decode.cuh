@@ -35,27 +35,11 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
                               void* kpool, void* vpool, int kv_bf16, cudaStream_t st);
 // Split-K GQA decode attention over the paged cache (src/model.rs:206-231 with
 // softmax_inplace :298-313), then the cross-split combine into att[b][nh*hd].
-// With LRS_ATTN_V3=1 (and `counters`, [batch][nkv] zeros, non-null) the split
-// kernel streams K/V blocks through a shared-memory ring (attn3_kernel) and
-// the last split of each (item, kv head) combines in place of the second
-// launch; a bounded wait that gives up writes LRS_ERR_DEVICE_TIMEOUT to
-// error_flag.
-bool attention_v3_enabled();
-// Resident attention CTAs per SM (occupancy of the split kernel in use).
+// Resident attention CTAs per SM (occupancy of the split kernel).
 int attention_ctas_per_sm(int hd, int kv_bf16);
-// With v3 and `rope` non-null (decode steps: every item one new position of
-// its own sequence) the kernel also does launch_rope_store's work, which the
-// caller then skips.
-struct AttnRope {
-  const float* k;
-  const float* v;
-  const float* cos_t;
-  const float* sin_t;
-};
 cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
-                             void* kpool, void* vpool, int kv_bf16, int nsplit,
-                             float* part, float* att, int* counters, int* error_flag,
-                             const AttnRope* rope, cudaStream_t st);
+                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
+                             float* part, float* att, cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
 // x of a windowed tensor-parallel column shard: dst[b][0..width) holds

@@ -43,7 +43,6 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cstdlib>
 
 #include "common.h"
 #include "device_common.cuh"
@@ -68,40 +67,23 @@ constexpr uint32_t kTmemCols = 512;
 // the A_min MMA; three A and three x buffers.  Q6_K: two A tiles per half
 // super-block, (q-32)*(sc & 15) and (q-32)*(sc - (sc & 15)), both exact in
 // f16, accumulated into the same TMEM columns; two A and two x buffers.
-//
-// RAW (Q4_K only, opt-in): a loader warp copies each super-block's 128 raw
-// rows (144 bytes each, 16-byte aligned) into a shared-memory ring with
-// cp.async.bulk, and the producers decode from there instead of holding the
-// next super-block in registers; two x buffers and two A buffers make the
-// room.  The ring takes what shared memory is left, up to 5 stages (4 at 64
-// items): at the weight-streaming rate an SM consumes a super-block every
-// ~0.4 us, against 1-2 us of DRAM latency under load.
-template <int T, int NI, bool RAW = false>
+template <int T, int NI>
 struct TcShape {
   static constexpr int kN = 2 * NI;
   static constexpr int kTileB = tile_b(NI);
   static constexpr int kTileBmin = tile_bmin(NI);
   static constexpr bool kMins = T == LRS_GGML_Q4_K;
   static constexpr int kAParts = T == LRS_GGML_Q6_K ? 2 : 1;  // A tiles per half step
-  // A buffers: RAW producers decode from shared memory, so two suffice and
-  // the third goes to the raw ring
-  static constexpr int kAB = T == LRS_GGML_Q6_K || RAW ? 2 : 3;
-  static constexpr int kBB = T == LRS_GGML_Q6_K || RAW ? 2 : 3;  // x buffers
-  static constexpr int kRawStage = kRows * 144;  // one super-block of 128 Q4_K rows
+  static constexpr int kAB = T == LRS_GGML_Q6_K ? 2 : 3;  // A buffers
+  static constexpr int kBB = T == LRS_GGML_Q6_K ? 2 : 3;  // x buffers
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kAB * kAParts * kTileA;
   static constexpr int kOffAmin = kOffB + kBB * kTileB;
   static constexpr int kOffBmin = kOffAmin + (kMins ? 2 * kTileMin : 0);
-  static constexpr int kOffRaw = kOffBmin + (kMins ? 2 * kTileBmin : 0);
-  static constexpr int kRawFit = (227 * 1024 - 256 - kOffRaw) / kRawStage;
-  static constexpr int kRawStages = RAW ? (kRawFit < 5 ? kRawFit : 5) : 0;
-  static_assert(!RAW || kRawStages >= 2, "the raw ring needs two stages");
-  static constexpr int kRawRing = RAW ? kRawStages : 1;  // divisor in code only RAW runs
-  static constexpr int kOffBar = kOffRaw + kRawStages * kRawStage;
-  static constexpr int kSmem = kOffBar + (RAW ? 256 : 128);
+  static constexpr int kOffBar = kOffBmin + (kMins ? 2 * kTileBmin : 0);
+  static constexpr int kSmem = kOffBar + 128;
   static constexpr int kBytes = T == LRS_GGML_Q6_K ? 210 : 144;
-  static constexpr int kThreads = RAW ? 448 : 416;  // + the raw loader warp
-  static_assert(!RAW || T == LRS_GGML_Q4_K, "the raw ring needs 16-byte aligned rows (Q4_K)");
+  static constexpr int kThreads = 416;
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
@@ -179,11 +161,7 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8
 // xscale: [64] item scales.
 __global__ void __launch_bounds__(256)
     xsplit_tc_kernel(const float* x, int x_ld, int cols, int batch, int ni, uint8_t* xt,
-                     uint8_t* xm, float* xscale, const float* norm_w, float norm_eps,
-                     int pdl_trigger) {
-  // lets a matmul launched with programmatic dependent launch start decoding
-  // its weights now; it reads what this kernel writes after griddepcontrol.wait
-  if (pdl_trigger) pdl_launch_dependents();
+                     uint8_t* xm, float* xscale, const float* norm_w, float norm_eps) {
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = x + (size_t)b * x_ld;
@@ -280,22 +258,6 @@ struct TcArgs {
   const float* xscale;
   float* part;  // [kgroups][batch][rows]
   int* error_flag;
-  // Fused-mode launch (the FUSED kernel variant, programmatic dependent
-  // launch): x tiles and scales are read only after griddepcontrol.wait, so the
-  // producers decode weights while x is prepared.
-  int pdl;
-  // Output step in the kernel (0: partials only, for gemm_partials_epilogue or
-  // a later fused launch).  With kgroups > 1 the CTA that finishes last for its
-  // row block adds the kgroups partials in order 0..kgroups-1 (the order of
-  // gemm_epilogue_kernel) and applies it; counters[row block] is zero between
-  // launches (reset by that CTA).
-  int fused;
-  int epi, out_ld, argmax_base;
-  float* out;
-  const float* bias;
-  const float* gate_part;  // EPI_SWIGLU (the up matrix): the gate launch's partials
-  unsigned long long* keys;
-  int* counters;
 };
 
 // Four bytes at a 2-byte aligned address (Q6_K blocks are 210 bytes).
@@ -315,9 +277,6 @@ __device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
 }
-
-// Barrier of the four epilogue warps only (named barrier 2, 128 threads).
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 // Raw bytes one producer thread (c, r) needs from one super-block.
 template <int T>
@@ -350,10 +309,10 @@ struct Raw<LRS_GGML_Q6_K> {
   }
 };
 
-template <int T, int NI, bool FUSED, bool RAW>
-__global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
+template <int T, int NI>
+__global__ void __launch_bounds__(TcShape<T, NI>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ TcArgs a) {
-  using S = TcShape<T, NI, RAW>;
+  using S = TcShape<T, NI>;
   constexpr int kN = S::kN, kTileB = S::kTileB;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
@@ -363,9 +322,6 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
   uint64_t* mma_done = bars + 6;    // [kAB] MMAs of a half step finished (A, x buffers free)
   uint64_t* acc_full = bars + 9;    // [2] super-block accumulator ready
   uint64_t* acc_empty = bars + 11;  // [2] epilogue finished reading it
-  uint64_t* raw_full = bars + 13;                   // [kRawStages] RAW: a super-block's rows landed
-  uint64_t* raw_empty = bars + 13 + S::kRawStages;  // [kRawStages] RAW: the producers finished with them
-  static_assert(13 + 2 * S::kRawStages <= (RAW ? 32 : 16), "barrier area");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sbase = smem_u32(smem);
 
@@ -378,10 +334,6 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
-    }
-    for (int i = 0; i < S::kRawStages; i++) {
-      mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 256);
     }
     fence_barrier_init();
   }
@@ -411,26 +363,12 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     const int r = tid & 127, c = tid >> 7;
     const uint8_t* rp = a.w + (size_t)min(row0 + r, a.rows - 1) * a.rb;
     Raw<T> cur, nxt;
-    if (!RAW && nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
+    if (nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
     for (int sb = 0; sb < nsb && ok; sb++) {
-      if constexpr (RAW) {
-        // this super-block's rows from the ring (row r at r * 144: conflict-free)
-        const int rs = sb % S::kRawRing;
-        ok = mbar_wait_bounded(&raw_full[rs], (uint32_t)((sb / S::kRawRing) & 1));
-        if (!ok) break;
-        const uint8_t* u = smem + S::kOffRaw + rs * S::kRawStage + r * 144;
-        cur.v[0] = *reinterpret_cast<const uint4*>(u);
-        cur.v[1] = *reinterpret_cast<const uint4*>(u + 16 + 32 * c);
-        cur.v[2] = *reinterpret_cast<const uint4*>(u + 32 + 32 * c);
-        cur.v[3] = *reinterpret_cast<const uint4*>(u + 80 + 32 * c);
-        cur.v[4] = *reinterpret_cast<const uint4*>(u + 96 + 32 * c);
-        mbar_arrive(&raw_empty[rs]);  // the values are in registers now
-      } else {
-        if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
-        if (sb + 2 < nsb) {  // two super-blocks ahead into L2
-          const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
-          if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
-        }
+      if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
+      if (sb + 2 < nsb) {  // two super-blocks ahead into L2
+        const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
+        if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
       }
 #pragma unroll
       for (int half = 0; half < 2; half++) {
@@ -523,7 +461,7 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
         fence_proxy_async();
         mbar_arrive(&a_full[ab]);
       }
-      if (!RAW) cur = nxt;
+      cur = nxt;
     }
   } else if (warp < 12) {
     // ---------------- epilogue: TMEM -> per-item sums ----------------
@@ -573,86 +511,13 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
     // partial sums, in units of the true x (item scales are powers of two)
     const int row = row0 + r;
     const bool live = row < a.rows;
-    if constexpr (FUSED) pdl_wait();  // xscale, and outputs the previous kernels may read
     if (ok && live) {
       float* pp = a.part + (size_t)blockIdx.y * a.batch * a.rows + row;
 #pragma unroll
       for (int i = 0; i < NI; i++)
         if (i < a.batch) pp[(size_t)i * a.rows] = acc[i] * a.xscale[i];
     }
-    if (FUSED && a.fused) {
-      // the CTA that finishes last for this row block (the only one when
-      // kgroups == 1) adds the partials in K-group order and applies the step
-      bool last = true;
-      if (a.kgroups > 1) {
-        __threadfence();
-        epilogue_sync();
-        __shared__ int last_sh;
-        if (r == 0) last_sh = atomicAdd(&a.counters[blockIdx.x], 1) == a.kgroups - 1;
-        epilogue_sync();
-        last = last_sh != 0;
-        if (last) __threadfence();
-      }
-      if (last) {
-        // LinearLayer::forward + bias / residual add / SwiGLU / greedy argmax
-        // (src/model.rs:33-46, 236-238, 251-254, 258-260; src/engine.rs:233-241)
-#pragma unroll 1
-        for (int i = 0; i < a.batch; i++) {
-          unsigned long long key = 0ull;
-          if (live) {
-            float y = 0.0f;
-            for (int k = 0; k < a.kgroups; k++)
-              y += __ldcg(a.part + ((size_t)k * a.batch + i) * a.rows + row);
-            float* o = a.out ? a.out + (size_t)i * a.out_ld + row : nullptr;
-            if (a.epi == EPI_STORE) {
-              *o = a.bias ? y + a.bias[row] : y;
-            } else if (a.epi == EPI_ADD) {
-              *o += y;
-            } else if (a.epi == EPI_SWIGLU) {
-              float g = 0.0f;
-              for (int k = 0; k < a.kgroups; k++)
-                g += __ldcg(a.gate_part + ((size_t)k * a.batch + i) * a.rows + row);
-              *o = (g / (1.0f + expf(-g))) * y;
-            } else {
-              if (o) *o = y;
-              key = argmax_pack(y, (uint32_t)(row + a.argmax_base));
-            }
-          }
-          if (a.epi == EPI_ARGMAX) {
-            for (int sh = 16; sh >= 1; sh >>= 1) {
-              const unsigned long long v2 = __shfl_xor_sync(0xffffffffu, key, sh);
-              key = v2 > key ? v2 : key;
-            }
-            if (lane == 0 && key) atomicMax(&a.keys[i], key);
-          }
-        }
-        if (a.kgroups > 1 && r == 0) a.counters[blockIdx.x] = 0;  // ready for the next launch
-      }
-    }
     if (!ok && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
-  } else if (RAW && warp == 13) {
-    // ---------------- raw loader: super-block rows into the ring ----------------
-    const uint64_t pol = evict_first_policy();
-    for (int sb = 0; sb < nsb && ok; sb++) {
-      const int rs = sb % S::kRawRing;
-      if (sb >= S::kRawRing) {
-        if (lane == 0)
-          ok = mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((sb - S::kRawRing) / S::kRawRing) & 1));
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-      }
-      if (lane == 0) mbar_expect_tx(&raw_full[rs], (uint32_t)S::kRawStage);
-      __syncwarp();
-      uint8_t* dst = smem + S::kOffRaw + rs * S::kRawStage;
-#pragma unroll
-      for (int k = 0; k < kRows / 32; k++) {
-        const int rr = lane + 32 * k;
-        const uint8_t* src =
-            a.w + (size_t)min(row0 + rr, a.rows - 1) * a.rb + (size_t)(s0 + sb) * 144;
-        tma_load_1d(dst + rr * 144, src, 144, &raw_full[rs], pol);
-      }
-    }
-    if (!ok && lane == 0 && a.error_flag) atomicExch(a.error_flag, LRS_ERR_DEVICE_TIMEOUT);
   } else if (warp == 12 && lane == 0) {
     // ---------------- issuer: x copies and MMAs ----------------
     const uint64_t pol = evict_first_policy();
@@ -668,7 +533,6 @@ __global__ void __launch_bounds__(TcShape<T, NI, RAW>::kThreads, 1)
         tma_load_1d(smem + S::kOffBmin + ((h >> 1) & 1) * S::kTileBmin,
                     a.xm + (size_t)sbg * S::kTileBmin, S::kTileBmin, &full_b[bi], pol);
     };
-    if constexpr (FUSED) pdl_wait();  // the x tiles come from xsplit_tc_kernel
     for (int h = 0; h < S::kBB - 1 && h < nhs; h++) issue_x(h);
     for (int hs = 0; hs < nhs && ok; hs++) {
       const int sb = hs >> 1, half = hs & 1, ab = hs % S::kAB, bb = hs % S::kBB, tb = sb & 1;
@@ -734,44 +598,20 @@ int tc_kgroups(const GemvParams& p, int sms) {
   return ctas >= sms ? 1 : std::max(1, std::min(nsb, sms / ctas));
 }
 
-template <int T, int NI, bool FUSED, bool RAW = false>
+template <int T, int NI>
 cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t st) {
-  using S = TcShape<T, NI, RAW>;
+  using S = TcShape<T, NI>;
   static std::atomic<uint64_t> attr{0};
-  cudaError_t e = set_smem_once(attr, (const void*)gemm_tc_kernel<T, NI, FUSED, RAW>, S::kSmem);
+  cudaError_t e = set_smem_once(attr, (const void*)gemm_tc_kernel<T, NI>, S::kSmem);
   if (e != cudaSuccess) return e;
-  if constexpr (!FUSED) {
-    gemm_tc_kernel<T, NI, false, RAW><<<grid, S::kThreads, S::kSmem, st>>>(a);
-    return cudaGetLastError();
-  }
-  // programmatic dependent launch: the producers start while xsplit_tc_kernel runs
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(S::kThreads);
-  cfg.dynamicSmemBytes = S::kSmem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr1[1];
-  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr1[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr1;
-  cfg.numAttrs = 1;
-  void* args[] = {const_cast<TcArgs*>(&a)};
-  return cudaLaunchKernelExC(&cfg, (const void*)gemm_tc_kernel<T, NI, FUSED, RAW>, args);
+  gemm_tc_kernel<T, NI><<<grid, S::kThreads, S::kSmem, st>>>(a);
+  return cudaGetLastError();
 }
 
 template <int NI>
 cudaError_t launch_tc_type(int type, const TcArgs& a, dim3 grid, cudaStream_t st) {
-  // LRS_TC_RAW=1: Q4_K through the raw-row ring
-  const char* rv = getenv("LRS_TC_RAW");
-  const bool raw = rv && rv[0] == '1';
-  if (type == LRS_GGML_Q6_K)
-    return a.pdl ? launch_tc<LRS_GGML_Q6_K, NI, true>(a, grid, st)
-                 : launch_tc<LRS_GGML_Q6_K, NI, false>(a, grid, st);
-  if (raw)
-    return a.pdl ? launch_tc<LRS_GGML_Q4_K, NI, true, true>(a, grid, st)
-                 : launch_tc<LRS_GGML_Q4_K, NI, false, true>(a, grid, st);
-  return a.pdl ? launch_tc<LRS_GGML_Q4_K, NI, true>(a, grid, st)
-               : launch_tc<LRS_GGML_Q4_K, NI, false>(a, grid, st);
+  if (type == LRS_GGML_Q6_K) return launch_tc<LRS_GGML_Q6_K, NI>(a, grid, st);
+  return launch_tc<LRS_GGML_Q4_K, NI>(a, grid, st);
 }
 }  // namespace
 
@@ -796,19 +636,8 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
   float* xscale = reinterpret_cast<float*>(xm + (size_t)(cols / 256) * tile_bmin(ni));
   float* part = xscale + kMaxItems;
   const int kgroups = tc_kgroups(p, sms);
-  // LRS_TC_FUSED=1: output step in the matmul (no epilogue launch) and the
-  // matmul overlapping the x preparation; needs the counters at the tail of
-  // the scratch (zero between launches)
-  int* counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(scratch) + p.scratch_bytes -
-                                         kScratchCounterBytes);
-  int max_blocks = 0;
-  for (int i = 0; i < p.nseg; i++) max_blocks = std::max(max_blocks, (p.seg[i].rows + kRows - 1) / kRows);
-  const bool fused = gemm_tc_fused_enabled() &&
-                     p.scratch_bytes >= gemm_tc_scratch_bytes(p, sms) + kScratchCounterBytes &&
-                     max_blocks <= (int)(kScratchCounterBytes / sizeof(int)) &&
-                     reinterpret_cast<uintptr_t>(counters) % 4 == 0;
   xsplit_tc_kernel<<<dim3(ni, 4), 256, 0, st>>>(p.x, p.x_ld, cols, B, ni, xt, xm, xscale,
-                                                p.norm_w, p.norm_eps, fused ? 1 : 0);
+                                                p.norm_w, p.norm_eps);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const float* parts[kGemvMaxSeg];
@@ -828,18 +657,6 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       a.xscale = xscale;
       a.part = cur;
       a.error_flag = p.error_flag;
-      if (fused) {
-        a.pdl = 1;
-        a.fused = !pair || m == 1;  // the gate launch of a pair only leaves partials
-        a.epi = p.epi;
-        a.out = p.seg[i].out;
-        a.out_ld = p.seg[i].out_ld;
-        a.bias = p.seg[i].bias;
-        a.argmax_base = p.argmax_base;
-        a.keys = p.argmax_keys;
-        a.gate_part = pair && m == 1 ? cur - (size_t)kgroups * B * a.rows : nullptr;
-        a.counters = counters;
-      }
       cur += (size_t)kgroups * B * a.rows;
       const dim3 grid((a.rows + kRows - 1) / kRows, kgroups);
       e = ni == 16 ? launch_tc_type<16>(p.seg[i].type, a, grid, st)
@@ -848,13 +665,7 @@ cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStre
       if (e != cudaSuccess) return e;
     }
   }
-  if (fused) return cudaSuccess;
   return gemm_partials_epilogue(p, parts, kgroups, st);
-}
-
-bool gemm_tc_fused_enabled() {
-  const char* v = getenv("LRS_TC_FUSED");
-  return v && v[0] == '1';
 }
 
 }  // namespace lrs

@@ -713,9 +713,7 @@ cudaError_t launch_cfg(const void* kernel, size_t smem, int grid, int threads,
 
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl) {
   const bool pair = p.epi == EPI_SWIGLU;
-  // LRS_NO_TCGEN05=1 keeps K-quant batches on the mma.sync kernel (comparison runs)
-  static const bool tc_off = getenv("LRS_NO_TCGEN05") != nullptr;
-  if (!tc_off && p.scratch && p.batch >= 4) {
+  if (p.scratch && p.batch >= 4) {
     if (gemm_tc_supported(p)) {
       if (p.scratch_bytes >= gemm_tc_scratch_bytes(p, num_sms))
         return gemm_tc_launch(p, p.scratch, num_sms, stream);
@@ -753,9 +751,7 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
       p.scratch_bytes >= gemm_scratch_bytes(p.batch, p.cols, num_sms))
     return gemm_launch(p, p.scratch, num_sms, stream);
   if (p.fast) {
-    // Direct-load batch-1 kernel (or, with LRS_GEMV_STREAM=1, the bulk-copy
-    // ring of gemv_stream.cu), one launch per run of same-type segments.
-    const bool stream_on = gemv_stream_enabled();
+    // Direct-load batch-1 kernel, one launch per run of same-type segments.
     int i = 0;
     while (i < p.nseg) {
       int j = i + 1;
@@ -768,14 +764,6 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, int num_sms, b
         q.seg[k].tile0 -= t0;
       }
       q.total_tiles = (j < p.nseg ? p.seg[j].tile0 : p.total_tiles) - t0;
-      if (stream_on) {
-        cudaError_t e = gemv_stream_launch(q, stream, num_sms, pdl);
-        if (e == cudaSuccess) {
-          i = j;
-          continue;
-        }
-        if (e != cudaErrorNotSupported) return e;  // else: this run on gemv5_kernel
-      }
       const void* kernel = fast_kernel(q.seg[0].type, pair);
       const size_t smem = 256 + fast_x_bytes(q.seg[0].type, q.cols);
       const int occ = std::max(1, occupancy(kernel, (int)smem, kGemvThreads));

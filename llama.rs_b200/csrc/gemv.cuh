@@ -83,42 +83,9 @@ cudaError_t gemm_launch(const GemvParams& p, void* scratch, int sms, cudaStream_
 cudaError_t gemm_partials_epilogue(const GemvParams& p, const float* const* parts, int kgroups,
                                    cudaStream_t stream);
 
-// The last kScratchCounterBytes of a matmul scratch buffer are counters that
-// must be zero when the buffer is allocated; kernels that use them leave them
-// zero.  Scratch sizes passed in GemvParams include them.
-constexpr size_t kScratchCounterBytes = 16384;
-
-// Batched Q4_K / Q6_K matmul on tcgen05 (gemm_tc.cu), 4..64 items.  With
-// LRS_TC_FUSED=1 the output step runs in the matmul kernel (gemm_tc_fused_enabled).
+// Batched Q4_K / Q6_K matmul on tcgen05 (gemm_tc.cu), 4..64 items.
 bool gemm_tc_supported(const GemvParams& p);
 size_t gemm_tc_scratch_bytes(const GemvParams& p, int sms);
 cudaError_t gemm_tc_launch(const GemvParams& p, void* scratch, int sms, cudaStream_t stream);
-bool gemm_tc_fused_enabled();
-
-// Tensor-parallel row-split projection fused with its all-reduce (the TPX
-// variant of gemv_stream_kernel): every CTA stores its rows' partial sums
-// into every rank's exchange buffer as its tiles finish, signals the same CTA
-// index on the peers, waits for theirs, and adds all ranks' partials of its
-// rows onto the output in rank order.
-constexpr int kTpSigFused = 64;    // first signal word of the fused path (per rank)
-constexpr int kTpMaxGrid = 1024;   // signal words per source rank
-struct StreamTp {
-  float* const* peer_x;   // [world] every rank's exchange buffer: [world][rows] of this call
-  int* local_sig;         // this rank's signal words + kTpSigFused: [world][kTpMaxGrid]
-  int* const* peer_sig;   // [world] every rank's signal words (bases)
-  unsigned* counters;     // [kTpMaxGrid] this rank's launches per CTA index (zero at creation)
-  int rank, world, rows;
-  int plan_cols;          // the widest shard of this projection over all ranks (>= cols)
-  int* error_flag;
-};
-
-// Batch-1 GEMV through a shared-memory ring of bulk copies (gemv_stream.cu),
-// for one run of same-type segments planned by gemv_plan (p.fast).  Used
-// instead of gemv5_kernel when LRS_GEMV_STREAM=1; with `tp` (one segment, not
-// a pair) the fused tensor-parallel variant.  cudaErrorNotSupported: the plan
-// does not fit (the caller uses gemv5_kernel).
-bool gemv_stream_enabled();
-cudaError_t gemv_stream_launch(const GemvParams& p, cudaStream_t stream, int num_sms, bool pdl,
-                               const StreamTp* tp = nullptr);
 
 }  // namespace lrs

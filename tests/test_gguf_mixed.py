@@ -9,7 +9,7 @@ tensor as stored.
 
 * CPU: every tensor of the loaded description has the mixed type and the
   bytes of the reference encoder for that type.
-* GPU (runs with LRS_TEST_NEW_KERNELS=1 until measured on a B200): the model
+* GPU: the model
   decodes like the oracle on the same description, batch 1 and batched.
 """
 import os
@@ -100,12 +100,9 @@ def test_mixed_gguf_oracle_runs(lrs, orc, tmp_path):
     assert np.abs(a["logits"][0] - b["logits"][0]).max() < 1e-3
 
 
-gpu_gate = pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
-                              reason="mixed-GGUF GPU parity runs with LRS_TEST_NEW_KERNELS=1")
 
 
 @pytest.mark.gpu
-@gpu_gate
 def test_mixed_gguf_decodes_like_oracle(lrs, orc, backend, tmp_path):
     path = str(tmp_path / "mixed.gguf")
     cfg, _ = _write_mixed(lrs, path)
@@ -122,7 +119,6 @@ def test_mixed_gguf_decodes_like_oracle(lrs, orc, backend, tmp_path):
 
 
 @pytest.mark.gpu
-@gpu_gate
 def test_mixed_gguf_batched_sequences(lrs, orc, backend, tmp_path):
     path = str(tmp_path / "mixed.gguf")
     cfg, _ = _write_mixed(lrs, path)

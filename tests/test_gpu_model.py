@@ -151,11 +151,6 @@ def test_model_from_gguf_file(lrs, orc, backend, tmp_path):
     model.close()
 
 
-new_shape = pytest.mark.skipif(__import__("os").environ.get("LRS_TEST_NEW_KERNELS") != "1",
-                               reason="runs with LRS_TEST_NEW_KERNELS=1 until run on a B200")
-
-
-@new_shape
 def test_c2_width_two_layers(lrs, orc, backend):
     """Qwen2.5-1.5B widths under q4k: every matrix Q4_K, including the tied
     151936-row head (benchmark config 2), 2 layers, batch 1."""
@@ -167,7 +162,6 @@ def test_c2_width_two_layers(lrs, orc, backend):
     _assert_tokens(ref, toks)
 
 
-@new_shape
 def test_c4_width_batch16(lrs, orc, backend):
     """Qwen2.5-32B widths (hidden 5120, 40/8 heads, intermediate 27648, q4k),
     2 layers: batch 1 and 16 sequences (the tcgen05 path at 16 items)."""

@@ -20,7 +20,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 WORKER = r"""
 import importlib.util, json, os, sys
 root, rank, world, tp_id, out = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), bytes.fromhex(sys.argv[4]), sys.argv[5]
-shape, recipe = json.loads(sys.argv[6]), sys.argv[7]
+shape, recipe, p2p = json.loads(sys.argv[6]), sys.argv[7], sys.argv[8] == "p2p"
 pkg = os.path.join(root, "llama.rs_b200")
 spec = importlib.util.spec_from_file_location("llamars_b200", os.path.join(pkg, "__init__.py"),
                                               submodule_search_locations=[pkg])
@@ -29,7 +29,7 @@ cfg = lrs.LlamaConfig(*shape)
 sm = lrs.SynthModel(cfg, 11, lrs.LoadQuantization[recipe])
 be = lrs.CudaBackend(rank)
 m = lrs.CudaQwen2Model(be, sm.desc(), max_seq_len=256, max_sequences=4, tp_rank=rank,
-                       tp_world=world, tp_id=tp_id)
+                       tp_world=world, tp_id=tp_id, tp_p2p=p2p)
 res = {}
 prompt = lrs.prompt_tokens(11, 40, cfg.vocab_size)
 logits, first = m.prefill(prompt, 0, seq=0)
@@ -59,32 +59,23 @@ WORLD = {"uneven4": 4}
 
 
 @pytest.mark.parametrize("shape", ["aligned", "windowed", "uneven4"])
-@pytest.mark.parametrize("allreduce", ["nccl", "p2p", "fused"])
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
 def test_tp2_matches_oracle(lrs, orc, tmp_path, allreduce, shape):
     """allreduce="p2p": the row-split projections are summed by the peer-memory
-    all-reduce (LRS_TP_P2P=1, tp_p2p.cu) instead of NCCL; "fused": in addition
-    the batch-1 decode steps run the stream GEMV that pushes its partials to
-    the peers and reduces in the same kernel (LRS_GEMV_STREAM=1), while the
-    prefill and the batch of three keep the separate all-reduce."""
+    all-reduce (the model option tp_p2p, tp_p2p.cu) instead of NCCL."""
     import torch
     world = WORLD.get(shape, 2)
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    if (allreduce != "nccl" or shape != "aligned") and os.environ.get("LRS_TEST_NEW_KERNELS") != "1":
-        pytest.skip("the peer-memory all-reduce and windowed shards run with LRS_TEST_NEW_KERNELS=1")
     dims, recipe = SHAPES[shape]
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0"}
-    if allreduce != "nccl":
-        env["LRS_TP_P2P"] = "1"
-    if allreduce == "fused":
-        env["LRS_GEMV_STREAM"] = "1"
     tp_id = lrs.tp_unique_id().hex()
     procs, outs = [], []
     for r in range(world):
         out = str(tmp_path / f"rank{r}.json")
         outs.append(out)
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER, ROOT, str(r), str(world), tp_id,
-                                       out, json.dumps(dims), recipe], env=env))
+                                       out, json.dumps(dims), recipe, allreduce], env=env))
     try:
         codes = [p.wait(timeout=600) for p in procs]
     finally:

@@ -267,8 +267,6 @@ def test_oracle_decodes_the_loaded_model(lrs, orc, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
-                    reason="SafeTensors-on-GPU parity runs with LRS_TEST_NEW_KERNELS=1")
 def test_safetensors_model_decodes_like_oracle(lrs, orc, backend, tmp_path):
     cfg = _cfg(lrs, False)
     src = lrs.SynthModel(cfg, 11, lrs.LoadQuantization.NONE)
@@ -313,8 +311,6 @@ def test_config_json_forms(lrs, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
-                    reason="device-encoded loading runs with LRS_TEST_NEW_KERNELS=1")
 @pytest.mark.parametrize("dtype", ["F32", "BF16"])
 def test_device_recipe_equals_host_recipe(lrs, backend, tmp_path, dtype):
     """maybe_quantize on the GPU (lrs_model_options.device_recipe): the float

@@ -11,7 +11,7 @@ oracle's decision lies within 1e-5 (probability units) of its boundary,
 where the last-ulp differences of the device expf may flip it.
 
 CPU: Python restatement vs oracle, edge cases, validate_sampling's messages.
-GPU (runs with LRS_TEST_NEW_KERNELS=1 until measured on a B200): device vs
+GPU: device vs
 oracle on full-vocabulary logits, and the model's forward_sample.
 """
 import math
@@ -133,12 +133,9 @@ def test_validation_messages(lrs):
     assert e.value.code == 2
 
 
-gpu_gate = pytest.mark.skipif(os.environ.get("LRS_TEST_NEW_KERNELS") != "1",
-                              reason="device sampler parity runs with LRS_TEST_NEW_KERNELS=1")
 
 
 @pytest.mark.gpu
-@gpu_gate
 @pytest.mark.parametrize("vocab", [151936, 4000, 37])
 def test_device_sampler_matches_oracle(lrs, orc, backend, vocab):
     import torch
@@ -161,7 +158,6 @@ def test_device_sampler_matches_oracle(lrs, orc, backend, vocab):
 
 
 @pytest.mark.gpu
-@gpu_gate
 def test_model_forward_sample_matches_oracle(lrs, orc, backend):
     cfg = lrs.LlamaConfig(512, 1024, 4, 2, 2, 3000, 1e-6, 1e6, 32768, 128, False)
     sm = lrs.SynthModel(cfg, 9, lrs.LoadQuantization.Q4KM)
