@@ -132,7 +132,10 @@ int32_t upload(const void* data, size_t nbytes, size_t rows, size_t cols, uint32
   if (cudaMalloc(&d, nbytes + 256) != cudaSuccess)
     return fail(LRS_ERR_OOM, "cudaMalloc of " + std::to_string(nbytes) + " bytes failed");
   cudaMemset(d + nbytes, 0, 256);
-  if (cudaMemcpy(d, data, nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+  // a copy from pageable memory may return before its DMA lands; kernels on
+  // other (non-blocking) streams must not start before it has
+  if (cudaMemcpy(d, data, nbytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess) {
     cudaFree(d);
     return fail(LRS_ERR_CUDA, "upload copy failed");
   }
@@ -808,7 +811,9 @@ int32_t device_encode_mat(lrs_model* m, uint32_t recipe, const lrs_tensor_desc& 
     cudaFree(enc);
   };
   if (cudaMalloc(&raw, d.nbytes) != cudaSuccess) return fail(LRS_ERR_OOM, "upload of " + name);
-  if (cudaMemcpy(raw, d.data, d.nbytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+  // on the stream the encoder runs on: a cudaMemcpy from pageable memory may
+  // return before its DMA lands, and the backend's stream does not wait for it
+  if (cudaMemcpyAsync(raw, d.data, d.nbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
     release();
     return fail(LRS_ERR_CUDA, "upload copy of " + name + " failed");
   }

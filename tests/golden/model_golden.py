@@ -30,7 +30,6 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 CASES = {
     "c3": ("config_c3", 2, "Q4KM", 1024, 128, 0),
     "c2": ("config_c2", 1, "Q4K", 512, 128, 0),
-    "c4l8": ("config_c4", 3, "Q4K", 2048, 64, 8),
 }
 N_TOP, N_RAND = 64, 1024
 
@@ -111,7 +110,7 @@ def make(name):
                                     "argmax": int(oracle.argmax(lg))}
     with open(fixture_path(name), "w") as f:
         json.dump(out, f)
-    print(f"{name}: {took:.0f} s, digest {digest[:16]}")
+    print(f"{name}: {took:.0f} s, digest {digest[:16]}", flush=True)
 
 
 if __name__ == "__main__":
