@@ -273,6 +273,12 @@ void* lrs_backend_stream(lrs_backend* backend);
 
 /* Bytes of weights the decode step streams per token (algorithmic). */
 uint64_t lrs_model_weight_bytes(const lrs_model* model);
+/* FNV-1a 64-bit digest of the weight bytes the model holds on the device
+ * (embedding, every layer's matrices in q, k, v, o, gate, up, down order, the
+ * LM head).  No counterpart in the reference: an integrity check that two
+ * models (for example one encoded on the host and one by device_recipe) hold
+ * the same bytes.  Synchronous; copies each tensor through host memory. */
+lrs_status lrs_model_weights_digest(lrs_model* model, uint64_t* digest_out);
 
 #ifdef __cplusplus
 }

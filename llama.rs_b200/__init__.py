@@ -210,6 +210,7 @@ _sig("lrs_model_decode_greedy", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c
 _sig("lrs_model_decode_enqueue", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, C.c_size_t)
 _sig("lrs_model_read_tokens", C.c_int32, _P, C.c_size_t, C.c_size_t, _U32)
 _sig("lrs_model_weight_bytes", C.c_uint64, _P)
+_sig("lrs_model_weights_digest", C.c_int32, _P, C.POINTER(C.c_uint64))
 _sig("lrs_model_profile_step", C.c_int32, _P, C.c_size_t, _U32, _U32, _U32, _F, _U32, _F, _F)
 _sig("lrs_model_step_kernels", C.c_uint32, _P)
 _sig("lrs_recipe_type", C.c_uint32, C.c_uint32, C.c_char_p, C.c_size_t, C.c_size_t)
@@ -243,7 +244,7 @@ EXPORTED_SYMBOLS = (
     "lrs_model_create",
     "lrs_model_destroy", "lrs_model_reset", "lrs_model_forward_token", "lrs_model_prefill",
     "lrs_model_decode_greedy", "lrs_model_decode_enqueue", "lrs_model_read_tokens",
-    "lrs_model_weight_bytes", "lrs_model_profile_step", "lrs_model_step_kernels",
+    "lrs_model_weight_bytes", "lrs_model_weights_digest", "lrs_model_profile_step", "lrs_model_step_kernels",
     "lrs_tp_unique_id", "lrs_model_create_tp", "lrs_model_tp_world",
     "lrs_quantize_matrix_device", "lrs_gguf_open", "lrs_gguf_close", "lrs_gguf_version", "lrs_gguf_tensor_count",
     "lrs_gguf_metadata_u64", "lrs_gguf_metadata_f32", "lrs_gguf_metadata_str", "lrs_gguf_tensor",
@@ -714,6 +715,12 @@ class CudaQwen2Model:
 
     def weight_bytes(self) -> int:
         return int(_lib.lrs_model_weight_bytes(self._h))
+
+    def weights_digest(self) -> int:
+        """FNV-1a digest of the weight bytes on the device (lrs_model_weights_digest)."""
+        d = C.c_uint64()
+        _check(_lib.lrs_model_weights_digest(self._h, C.byref(d)))
+        return int(d.value)
 
     def reset(self, seq: int = 0) -> None:
         _check(_lib.lrs_model_reset(self._h, seq))

@@ -24,6 +24,7 @@
 #include "gemv.cuh"
 #include "internal.h"
 #include "sample.cuh"
+#include "step1.cuh"
 #include "tp_p2p.cuh"
 
 namespace lrs {
@@ -286,6 +287,19 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
                              size_t batch, float* d_out, void* stream) {
   if (!be || !w || !d_in || !d_out) return fail(LRS_ERR_INVALID, "null argument");
   if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
+  cudaStream_t st0 = stream ? (cudaStream_t)stream : be->stream;
+  if (batch == 1) {  // the bulk-copy ring GEMV of the batch-1 decode step
+    S1Mat sm{};
+    sm.w = w->t.d;
+    sm.out = d_out;
+    sm.type = (int)w->t.type;
+    sm.rows = w->t.rows;
+    sm.cols = w->t.cols;
+    sm.epi = EPI_STORE;
+    const cudaError_t e = s1_launch_gemv(sm, d_in, be->d_err, be->sms, st0);
+    if (e != cudaSuccess) return fail(LRS_ERR_CUDA, std::string("batch-1 GEMV: ") + cudaGetErrorString(e));
+    return LRS_OK;
+  }
   GemvMat m = mat_of(w->t, d_out, w->t.rows);
   GemvParams p;
   int32_t rc = gemv_plan(&p, &m, 1, EPI_STORE, (int)batch);
@@ -399,6 +413,12 @@ struct lrs_model {
   int** d_peer_sig = nullptr;       // [world]
   std::vector<void*> ipc_opened;
   float* act2 = nullptr;    // up projection when a layer's gate and up differ in type
+  // the batch-1 decode step as one persistent kernel (step1.cu)
+  bool s1_ok = false;
+  S1Model s1{};
+  S1Model* d_s1 = nullptr;
+  const void* s1_tokens = nullptr;  // tokens_out the device copy holds
+  int s1_cap = -1;
   void* gemm_scratch = nullptr;  // batched tensor-core matmul scratch
   // tensor parallelism: this process holds shard tp_rank of tp_world
   int tp_rank = 0, tp_world = 1;
@@ -724,6 +744,127 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
   if (greedy_advance)
     LRS_CUDA(launch_advance(m->keys, m->d_tok, m->d_pos, B, m->d_step, n_steps_cap,
                             m->d_tokens_out, m->d_last, st));
+  return LRS_OK;
+}
+
+// The batch-1 decode step of step1.cu: the layer table, the chunk plans and
+// the shared-memory plan, uploaded once.  Models it cannot serve (tensor
+// parallel, head_dim other than 64/128, more than 8 query heads per KV head,
+// or x rows wider than shared memory) keep the per-kernel step.
+int32_t setup_step1(lrs_model* m) {
+  const lrs_config& c = m->c;
+  if (m->tp_world != 1) return LRS_OK;
+  if ((c.head_dim != 64 && c.head_dim != 128) || c.num_attention_heads / c.num_key_value_heads > 8)
+    return LRS_OK;
+  int coop = 0;
+  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->be->device) != cudaSuccess || !coop)
+    return LRS_OK;
+  const int G = m->be->sms;
+  S1Model& s = m->s1;
+  s = S1Model{};
+  s.L = (int)m->layers.size();
+  s.h = (int)c.hidden_size;
+  s.nh = (int)c.num_attention_heads;
+  s.nkv = (int)c.num_key_value_heads;
+  s.hd = (int)c.head_dim;
+  s.inter = (int)c.intermediate_size;
+  s.vocab = (int)c.vocab_size;
+  s.eps = c.rms_norm_eps;
+  s.attn_scale = 1.0f / sqrtf((float)c.head_dim);
+  s.kv_bf16 = m->opt.kv_dtype == LRS_KV_BF16;
+  int cols[3] = {0, 0, 0};
+  auto mat = [&](const DevTensor& t, const DevTensor* t2, const float* bias, float* out, int epi,
+                 S1Mat* o) -> bool {
+    *o = S1Mat{};
+    o->w = t.d;
+    o->w2 = t2 ? t2->d : nullptr;
+    o->bias = bias;
+    o->out = out;
+    o->type = (int)t.type;
+    o->rows = t.rows;
+    o->cols = t.cols;
+    o->epi = epi;
+    if (!s1_plan_mat(o, t2 ? 2 : 1, G)) return false;
+    int& w = cols[s1_xclass(o->type)];
+    w = std::max(w, o->cols);
+    return true;
+  };
+  std::vector<S1Layer> layers(s.L);
+  for (int l = 0; l < s.L; l++) {
+    const Layer& L = m->layers[l];
+    S1Layer& y = layers[l];
+    bool ok = mat(L.q, nullptr, L.qb, m->q, EPI_STORE, &y.qkv[0]) &&
+              mat(L.k, nullptr, L.kb, m->k, EPI_STORE, &y.qkv[1]) &&
+              mat(L.v, nullptr, L.vb, m->v, EPI_STORE, &y.qkv[2]) &&
+              mat(L.o, nullptr, nullptr, m->residual, EPI_ADD, &y.o) &&
+              mat(L.down, nullptr, nullptr, m->residual, EPI_ADD, &y.down);
+    if (L.gate.type == L.up.type) {
+      y.ngu = 1;
+      ok = ok && mat(L.gate, &L.up, nullptr, m->act, EPI_SWIGLU, &y.gu[0]);
+    } else {
+      y.ngu = 2;
+      ok = ok && mat(L.gate, nullptr, nullptr, m->act, EPI_STORE, &y.gu[0]) &&
+           mat(L.up, nullptr, nullptr, m->act2, EPI_STORE, &y.gu[1]);
+    }
+    if (!ok || L.o.cols != (int)(c.num_attention_heads * c.head_dim)) return LRS_OK;
+    y.in_norm = L.in_norm;
+    y.post_norm = L.post_norm;
+    y.kpool = L.kpool;
+    y.vpool = L.vpool;
+  }
+  if (!mat(m->lm, nullptr, nullptr, nullptr, EPI_ARGMAX, &s.lm)) return LRS_OK;
+  s.embed = m->embed.d;
+  s.embed_type = (int)m->embed.type;
+  s.final_norm = m->final_norm;
+  s.rope_cos = m->rope_cos;
+  s.rope_sin = m->rope_sin;
+  s.residual = m->residual;
+  s.q = m->q;
+  s.k = m->k;
+  s.v = m->v;
+  s.att = m->att;
+  s.act = m->act;
+  s.act2 = m->act2;
+  s.part = m->part;
+  s.max_split = std::max(1, std::min(G / s.nkv, m->max_split * (s.nh / s.nkv)));
+  s.split_cap = std::max(64, (int)((m->opt.max_seq_len + s.max_split - 1) / s.max_split));
+  const int work = std::max(s.h, kS1MaxGroup * s.hd + kS1MaxGroup * s.split_cap + 2 * s.hd + 2 * kS1MaxGroup);
+  if (!s1_plan_smem(&s.sm, cols[0], cols[1], cols[2], work)) return LRS_OK;
+  if (s1_occupancy(s.sm.total) < 1) return LRS_OK;
+  int32_t rc;
+  unsigned* sync = nullptr;
+  S1Layer* d_layers = nullptr;
+  if ((rc = model_alloc(m, (void**)&sync, (1 + (size_t)s.nkv) * 4)) ||
+      (rc = model_alloc(m, (void**)&d_layers, layers.size() * sizeof(S1Layer))) ||
+      (rc = model_alloc(m, (void**)&m->d_s1, sizeof(S1Model))))
+    return rc;
+  LRS_CUDA(cudaMemset(sync, 0, (1 + (size_t)s.nkv) * 4));
+  LRS_CUDA(cudaMemcpy(d_layers, layers.data(), layers.size() * sizeof(S1Layer), cudaMemcpyHostToDevice));
+  s.layers = d_layers;
+  s.bar_ctr = sync;
+  s.attn_cnt = sync + 1;
+  s.keys = m->keys;
+  s.tok = m->d_tok;
+  s.pos = m->d_pos;
+  s.seq = m->d_seq;
+  s.pages = m->d_pages;
+  s.max_pages = m->pages_per_seq;
+  s.step = m->d_step;
+  s.last = m->d_last;
+  s.error_flag = m->be->d_err;
+  s.tokens_out = nullptr;
+  s.n_steps_cap = 0;
+  LRS_CUDA(cudaMemcpy(m->d_s1, &s, sizeof(S1Model), cudaMemcpyHostToDevice));
+  m->s1_tokens = nullptr;
+  m->s1_cap = 0;
+  m->s1_ok = true;
+  return LRS_OK;
+}
+
+// Queues one greedy decode step of item 0 through the step kernel (the
+// device copy of the model table must name the current token buffer).
+int32_t enqueue_step1(lrs_model* m) {
+  LRS_CUDA(s1_launch_step(m->s1, m->d_s1, m->be->sms, m->be->stream));
   return LRS_OK;
 }
 
@@ -1098,6 +1239,7 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
   if (world > 1 &&
       (rc = model_alloc(m.get(), (void**)&m->logits_full, (size_t)c.vocab_size * 4)))
     return cleanup(rc);
+  if ((rc = setup_step1(m.get()))) return cleanup(rc);
   LRS_CUDA(cudaDeviceSynchronize());
   *out = m.release();
   return LRS_OK;
@@ -1176,6 +1318,28 @@ void lrs_model_destroy(lrs_model* m) {
 }
 
 uint64_t lrs_model_weight_bytes(const lrs_model* m) { return m ? m->weight_bytes : 0; }
+
+lrs_status lrs_model_weights_digest(lrs_model* m, uint64_t* out) {
+  if (!m || !out) return fail(LRS_ERR_INVALID, "null argument");
+  LRS_CUDA(cudaSetDevice(m->be->device));
+  LRS_CUDA(cudaStreamSynchronize(m->be->stream));
+  uint64_t h = 1469598103934665603ull;
+  std::vector<uint8_t> buf;
+  auto eat = [&](const DevTensor& t) -> int32_t {
+    buf.resize(t.nbytes);
+    if (t.nbytes) LRS_CUDA(cudaMemcpy(buf.data(), t.d, t.nbytes, cudaMemcpyDeviceToHost));
+    for (uint8_t b : buf) h = (h ^ b) * 1099511628211ull;
+    return LRS_OK;
+  };
+  int32_t rc;
+  if ((rc = eat(m->embed))) return rc;
+  for (const auto& L : m->layers)
+    for (const DevTensor* t : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+      if ((rc = eat(*t))) return rc;
+  if ((rc = eat(m->lm))) return rc;
+  *out = h;
+  return LRS_OK;
+}
 
 lrs_status lrs_model_reset(lrs_model* m, uint32_t seq) {
   if (!m) return fail(LRS_ERR_INVALID, "null model");
@@ -1306,6 +1470,15 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
   cudaStream_t st = m->be->stream;
   LRS_CUDA(cudaMemsetAsync(m->d_step, 0, 4, st));
   const int cap_steps = (int)(m->tokens_out_cap / B);
+  const bool step1 = B == 1 && m->s1_ok;
+  if (step1 && (m->s1_tokens != m->d_tokens_out || m->s1_cap != cap_steps)) {
+    m->s1.tokens_out = m->d_tokens_out;
+    m->s1.n_steps_cap = cap_steps;
+    LRS_CUDA(cudaMemcpyAsync(m->d_s1, &m->s1, sizeof(S1Model), cudaMemcpyHostToDevice, st));
+    LRS_CUDA(cudaStreamSynchronize(st));
+    m->s1_tokens = m->d_tokens_out;
+    m->s1_cap = cap_steps;
+  }
   if (m->opt.use_graph) {
     GraphKey key{B, m->d_tokens_out};
     auto it = m->graphs.find(key);
@@ -1313,7 +1486,7 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
     if (it == m->graphs.end()) {
       cudaGraph_t graph;
       LRS_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-      rc = enqueue_step(m, B, -1, false, true, cap_steps);
+      rc = step1 ? enqueue_step1(m) : enqueue_step(m, B, -1, false, true, cap_steps);
       cudaError_t e = cudaStreamEndCapture(st, &graph);
       if (rc) return rc;
       if (e != cudaSuccess) return fail(LRS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
@@ -1339,7 +1512,7 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
     for (size_t s = 0; s < n_steps; s++) LRS_CUDA(cudaGraphLaunch(exec, st));
   } else {
     for (size_t s = 0; s < n_steps; s++)
-      if ((rc = enqueue_step(m, B, -1, false, true, cap_steps))) return rc;
+      if ((rc = step1 ? enqueue_step1(m) : enqueue_step(m, B, -1, false, true, cap_steps))) return rc;
   }
   return LRS_OK;
 }
