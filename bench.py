@@ -157,17 +157,32 @@ def build_model(lrs, wl, threads=0, barrier=None, builder=True):
     return mf.config, mf
 
 
-def cpu_decode_rate(orc, lrs, sm, cfg, wl, threads, budget_s=15.0):
-    """Reference AVX2 path (oracle port) on the host: tokens/s of greedy decode for one
-    sequence after a 16-token prompt, on a bounded number of steps."""
-    om = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
-    prompt = lrs.prompt_tokens(wl["seed"], 16, cfg.vocab_size)
-    probe = om.benchmark_tokens(prompt, 2)
-    per_tok = max(probe["decode_s"] / 2, 1e-4)
-    n = int(max(2, min(128, budget_s / per_tok)))
-    om2 = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
-    r = om2.benchmark_tokens(prompt, n)
-    return n / r["decode_s"], n
+def cpu_decode_rate(orc, desc, vocab, wl, P, threads, budget_s=15.0, warmup=2):
+    """The reference AVX2 path (the oracle's restatement of src/simd.rs with
+    the row-parallel pool of src/backend.rs:143-162) on the host cores: greedy
+    decode steps of one sequence at the workload's context (positions P, P+1,
+    ...).  The prompt is not run through the CPU (it would take minutes): the
+    dense f32 KV cache of the restatement starts zeroed, and the cost of a
+    decode step depends on the context length only.  Returns (tok/s, steps)."""
+    om = orc.OracleModel(desc, P + 512, orc.AVX2, threads)
+    tok = int(prompt_ids(wl["seed"], 1, vocab)[0])
+    for i in range(warmup):
+        tok = int(orc.argmax(om.forward_token(tok, P + i)))
+    t0 = time.perf_counter()
+    tok = int(orc.argmax(om.forward_token(tok, P + warmup)))
+    per_tok = max(time.perf_counter() - t0, 1e-4)
+    n = int(max(2, min(256, budget_s / per_tok)))
+    t0 = time.perf_counter()
+    for i in range(n):
+        tok = int(orc.argmax(om.forward_token(tok, P + warmup + 1 + i)))
+    return n / (time.perf_counter() - t0), n
+
+
+def prompt_ids(seed, n, vocab, sequence=0):
+    """prompt_tokens of the package (numpy PCG64), restated so the reference
+    arm does not load the CUDA library."""
+    rng = np.random.default_rng(seed + 1000 if sequence == 0 else [seed, sequence])
+    return rng.integers(0, vocab, n, dtype=np.int64).astype(np.uint32)
 
 
 def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
@@ -183,38 +198,46 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
 
 
 def run_reference(args, wl):
+    """The reference CPU path alone: the model file is mapped without the CUDA
+    library (oracle.MappedModel); when the cache is missing a child process
+    builds it first (untimed).  Each step is one greedy decode step of one
+    sequence at the GPU arm's context (the reference has no batching)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    lrs = load_pkg()  # host-side model construction only (no CUDA call)
+    path = model_cache_path(wl)
+    if not os.path.exists(path):
+        code = ("import sys; sys.path.insert(0, %r); import bench; "
+                "bench.build_model(bench.load_pkg(), %r, %d)" % (ROOT, wl, os.cpu_count() or 1))
+        subprocess.run([sys.executable, "-c", code], check=True)
     orc = load_oracle()
+    mf = orc.MappedModel(path)
     threads = os.cpu_count() or 1
-    cfg, sm = build_model(lrs, wl, threads)
-    prompt = lrs.prompt_tokens(wl["seed"], 16, cfg.vocab_size)
-    om2 = orc.OracleModel(sm.desc(), 512, orc.AVX2, threads)
-    om2.prefill(prompt)
-    tok = orc.argmax(om2.forward_token(int(prompt[-1]), len(prompt) - 1))
-    pos = len(prompt)
+    P = args.prompt or wl["prompt"]
+    om = orc.OracleModel(mf.desc(), P + args.warmup + args.steps + 8, orc.AVX2, threads)
+    tok = int(prompt_ids(wl["seed"], 1, mf.vocab_size)[0])
+    pos = P
     for _ in range(args.warmup):
-        tok = orc.argmax(om2.forward_token(tok, pos))
+        tok = int(orc.argmax(om.forward_token(tok, pos)))
         pos += 1
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        tok = orc.argmax(om2.forward_token(tok, pos))
+        tok = int(orc.argmax(om.forward_token(tok, pos)))
         pos += 1
     dt = time.perf_counter() - t0
     value = args.steps / dt
-    sample = (f"1 sequence (the reference has no batching), 16-token prompt, {args.warmup} warm-up "
-              f"+ {args.steps} timed greedy decode steps")
+    sample = (f"1 sequence (the reference has no batching) at context {P}..{P + args.warmup + args.steps}: "
+              f"{args.warmup} warm-up + {args.steps} timed greedy decode steps; the f32 KV cache of "
+              "the prompt positions starts zeroed instead of running the prompt on the CPU "
+              "(a step's cost depends on the context length only)")
     line = {
         "impl": "reference", "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and ids)",
-        "config": dict(workload_config(wl, args.seqs or wl["seqs"], args.prompt or wl["prompt"],
-                                       args.gpus, args.tp and args.gpus > 1, wl.get("layers", 0),
-                                       args.kv_bf16),
-                       kernel="avx2", threads=threads),
+        "config": dict(workload_config(wl, args.seqs or wl["seqs"], P, args.gpus,
+                                       args.tp and args.gpus > 1, wl.get("layers", 0), args.kv_bf16),
+                       kernel="avx2", threads=threads, cpu=cpu_model()),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample + "; C++ restatement of the reference AVX2 backend "
                                             "(src/simd.rs) -- the Rust reference cannot be built "
@@ -222,6 +245,16 @@ def run_reference(args, wl):
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def run_ours(args, wl):
@@ -367,11 +400,12 @@ def run_ours(args, wl):
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         orc = load_oracle()
-        rate, n = cpu_decode_rate(orc, lrs, sm, cfg, wl, ncpu)
-        cpu = {"value": rate, "unit": "tok/s", "cores": ncpu, "kind": "port",
-               "sample": f"1 sequence, 16-token prompt then {n} greedy decode steps of the same "
-                         "model; C++ restatement of the reference AVX2 backend (src/simd.rs, "
-                         "row-parallel pool as src/backend.rs:143-162)"}
+        rate, n = cpu_decode_rate(orc, sm.desc(), cfg.vocab_size, wl, P, ncpu)
+        cpu = {"value": rate, "unit": "tok/s", "cores": ncpu, "kind": "port", "cpu": cpu_model(),
+               "sample": f"1 sequence at context {P}: {n} greedy decode steps of the same model "
+                         "(KV of the prompt positions zeroed, not computed); C++ restatement of "
+                         "the reference AVX2 backend (src/simd.rs, row-parallel pool as "
+                         "src/backend.rs:143-162)"}
 
     if rank == 0:
         nl = launches_per_step(cfg.num_hidden_layers, B)

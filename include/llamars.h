@@ -189,6 +189,9 @@ typedef struct lrs_model_options {
                              on the GPU at creation (maybe_quantize, src/loader.rs:406-447); 0 = as given */
   uint32_t tp_allreduce;  /* tensor-parallel models: LRS_TP_ALLREDUCE_NCCL (default) or
                              LRS_TP_ALLREDUCE_P2P (one kernel over peer memory) */
+  uint32_t persistent_decode; /* 1: batch-1 greedy decode steps run as one persistent
+                                 kernel per step (step1.cu); 0 (default): one CUDA graph of
+                                 per-operation kernels */
 } lrs_model_options;
 
 enum { LRS_TP_ALLREDUCE_NCCL = 0, LRS_TP_ALLREDUCE_P2P = 1 };

@@ -132,7 +132,8 @@ class _ModelDesc(C.Structure):
 class _ModelOptions(C.Structure):
     _fields_ = [("max_seq_len", C.c_uint32), ("max_sequences", C.c_uint32),
                 ("kv_dtype", C.c_uint32), ("use_graph", C.c_uint32),
-                ("device_recipe", C.c_uint32), ("tp_allreduce", C.c_uint32)]
+                ("device_recipe", C.c_uint32), ("tp_allreduce", C.c_uint32),
+                ("persistent_decode", C.c_uint32)]
 
 
 class _SynthSpec(C.Structure):
@@ -677,13 +678,14 @@ class CudaQwen2Model:
                  max_sequences: int = 1, kv_bf16: bool = False, use_graph: bool = True,
                  keepalive=None, tp_rank: int = 0, tp_world: int = 1, tp_id: bytes = b"",
                  device_recipe: LoadQuantization = LoadQuantization.NONE,
-                 tp_p2p: bool = False):
+                 tp_p2p: bool = False, persistent_decode: bool = False):
         """tp_world > 1 makes this process shard tp_rank of a tensor-parallel
         model (every rank passes the full desc and the same tp_id, made once by
         tp_unique_id() and shared out of band).  device_recipe encodes the
         desc's F32/F16/BF16 matrices on the GPU (the load-time recipe)."""
         opts = _ModelOptions(max_seq_len, max_sequences, 1 if kv_bf16 else 0,
-                             1 if use_graph else 0, int(device_recipe), 1 if tp_p2p else 0)
+                             1 if use_graph else 0, int(device_recipe), 1 if tp_p2p else 0,
+                             1 if persistent_decode else 0)
         h = _P()
         if tp_world > 1:
             if len(tp_id) != 128:

@@ -288,18 +288,6 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
   if (!be || !w || !d_in || !d_out) return fail(LRS_ERR_INVALID, "null argument");
   if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
   cudaStream_t st0 = stream ? (cudaStream_t)stream : be->stream;
-  if (batch == 1) {  // the bulk-copy ring GEMV of the batch-1 decode step
-    S1Mat sm{};
-    sm.w = w->t.d;
-    sm.out = d_out;
-    sm.type = (int)w->t.type;
-    sm.rows = w->t.rows;
-    sm.cols = w->t.cols;
-    sm.epi = EPI_STORE;
-    const cudaError_t e = s1_launch_gemv(sm, d_in, be->d_err, be->sms, st0);
-    if (e != cudaSuccess) return fail(LRS_ERR_CUDA, std::string("batch-1 GEMV: ") + cudaGetErrorString(e));
-    return LRS_OK;
-  }
   GemvMat m = mat_of(w->t, d_out, w->t.rows);
   GemvParams p;
   int32_t rc = gemv_plan(&p, &m, 1, EPI_STORE, (int)batch);
@@ -753,7 +741,7 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
 // or x rows wider than shared memory) keep the per-kernel step.
 int32_t setup_step1(lrs_model* m) {
   const lrs_config& c = m->c;
-  if (m->tp_world != 1) return LRS_OK;
+  if (m->tp_world != 1 || !m->opt.persistent_decode) return LRS_OK;
   if ((c.head_dim != 64 && c.head_dim != 128) || c.num_attention_heads / c.num_key_value_heads > 8)
     return LRS_OK;
   int coop = 0;

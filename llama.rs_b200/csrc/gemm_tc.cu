@@ -62,6 +62,7 @@ __host__ __device__ constexpr int tile_bmin(int ni) { return 2 * ni * 16 * 2; }
 constexpr int kTileMin = 128 * 16 * 2;   // 4 KB (A_min or B_min)
 constexpr int kSBO = (kKC / 8) * 128;    // 2048
 constexpr uint32_t kTmemCols = 512;
+constexpr int kTcAhead = 2;  // super-blocks of weight rows prefetched into L2 ahead
 
 // Per-type pipeline shape.  Q4_K: one A tile (sc*q) per half super-block plus
 // the A_min MMA; three A and three x buffers.  Q6_K: two A tiles per half
@@ -366,8 +367,8 @@ __global__ void __launch_bounds__(TcShape<T, NI>::kThreads, 1)
     if (nsb > 0) cur.load(rp + (size_t)s0 * S::kBytes, c);
     for (int sb = 0; sb < nsb && ok; sb++) {
       if (sb + 1 < nsb) nxt.load(rp + (size_t)(s0 + sb + 1) * S::kBytes, c);
-      if (sb + 2 < nsb) {  // two super-blocks ahead into L2
-        const uint8_t* pf = rp + (size_t)(s0 + sb + 2) * S::kBytes + c * 128;
+      if (sb + kTcAhead < nsb) {  // kTcAhead super-blocks ahead into L2
+        const uint8_t* pf = rp + (size_t)(s0 + sb + kTcAhead) * S::kBytes + c * 128;
         if (c * 128 < S::kBytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pf));
       }
 #pragma unroll

@@ -308,6 +308,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 
 // Bulk-prefetches the rows of row group g (R rows, both matrices of a pair)
 // into L2 so that the lanes' loads of the group hit L2 instead of HBM.
+constexpr int kPrefetchPasses = 2;  // row-group passes kept in flight into L2
+
 template <int R, bool PAIR>
 __device__ __forceinline__ void prefetch_group(const GemvParams& p, int g) {
   if (g >= p.total_tiles) return;
@@ -344,7 +346,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
   // The weights do not depend on the previous kernel: pull this CTA's first
   // two passes of row groups into L2 while it finishes.
   const int gpc0 = kWarps / p.wpg;
-  if (tid < 2 * gpc0) prefetch_group<R, PAIR>(p, blockIdx.x * gpc0 + (tid / gpc0) * gridDim.x * gpc0 + tid % gpc0);
+  if (tid < kPrefetchPasses * gpc0)
+    prefetch_group<R, PAIR>(p, blockIdx.x * gpc0 + (tid / gpc0) * gridDim.x * gpc0 + tid % gpc0);
 
   pdl_wait();  // x / residual come from the previous kernel
   float inv_rms = 1.0f;
@@ -417,8 +420,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv5_kernel(const __grid_consta
   for (int gb = blockIdx.x * gpc; gb < p.total_tiles; gb += gridDim.x * gpc) {
     const int g = gb + warp / wpg;
     const bool live = g < p.total_tiles;
-    // keep two passes ahead in L2
-    if (lane == 0 && sub_w == 0) prefetch_group<R, PAIR>(p, g + 2 * gridDim.x * gpc);
+    // keep kPrefetchPasses passes ahead in L2
+    if (lane == 0 && sub_w == 0) prefetch_group<R, PAIR>(p, g + kPrefetchPasses * gridDim.x * gpc);
     const GemvSeg sg = find_seg(p, live ? g : gb);
     const int r0 = ((live ? g : gb) - sg.tile0) * R;
     const int nr = live ? min(R, sg.rows - r0) : 0;

@@ -32,7 +32,6 @@
 #include "common.h"
 #include "gemv.cuh"
 #include "internal.h"
-#include "step1.cuh"
 
 namespace {
 
@@ -97,18 +96,22 @@ extern "C" lrs_status lrs_matvec_noalloc(lrs_backend* be, const lrs_tensor* w, c
   float* dy = reinterpret_cast<float*>(base + kYOffset);
   int* derr = reinterpret_cast<int*>(base + kErrOffset);
 
-  // the kernel of lrs_matvec at batch 1, which needs no scratch
-  lrs::S1Mat m{};
+  lrs::GemvMat m{};
   m.w = w->t.d;
-  m.type = (int)w->t.type;
+  m.type = w->t.type;
   m.rows = w->t.rows;
   m.cols = w->t.cols;
   m.out = dy;
-  m.epi = lrs::EPI_STORE;
+  m.out_ld = w->t.rows;
+  lrs::GemvParams p;
+  if ((rc = lrs::gemv_plan(&p, &m, 1, lrs::EPI_STORE, 1))) return rc;
+  p.x = dx;
+  p.x_ld = w->t.cols;
+  p.error_flag = derr;
   cudaStream_t st = be->stream;
   NOALLOC_CUDA(cudaMemsetAsync(derr, 0, sizeof(int), st));  // the error word must start at zero
   NOALLOC_CUDA(cudaMemcpyAsync(dx, in, n_in * sizeof(float), cudaMemcpyHostToDevice, st));
-  NOALLOC_CUDA(lrs::s1_launch_gemv(m, dx, derr, be->sms, st));
+  NOALLOC_CUDA(lrs::gemv_launch(p, st, be->sms, false));
   NOALLOC_CUDA(cudaMemcpyAsync(out, dy, n_out * sizeof(float), cudaMemcpyDeviceToHost, st));
   int herr = 0;
   NOALLOC_CUDA(cudaMemcpyAsync(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost, st));

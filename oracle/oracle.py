@@ -179,3 +179,79 @@ class OracleModel:
             raise ValueError(_lib.orc_last_error().decode())
         return dict(tokens=toks, margins=margins, logits=logits, prefill_s=ps.value,
                     decode_s=ds.value)
+
+
+# ----------------------------------------------------------------------------
+# Model files written by the package's save_model_file (bench.py's model
+# cache), read without the CUDA library: the reference arm of bench.py maps
+# the model with this and drives the oracle alone.  The structs mirror
+# lrs_model_desc of include/llamars.h.
+class _Config(C.Structure):
+    _fields_ = [("hidden_size", C.c_uint32), ("intermediate_size", C.c_uint32),
+                ("num_attention_heads", C.c_uint32), ("num_key_value_heads", C.c_uint32),
+                ("num_hidden_layers", C.c_uint32), ("vocab_size", C.c_uint32),
+                ("head_dim", C.c_uint32), ("max_position_embeddings", C.c_uint32),
+                ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float)]
+
+
+class _TensorDesc(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("nbytes", C.c_uint64), ("rows", C.c_uint64),
+                ("cols", C.c_uint64), ("ggml_type", C.c_uint32), ("reserved", C.c_uint32)]
+
+
+class _LayerDesc(C.Structure):
+    _fields_ = [("input_layernorm", C.c_void_p), ("post_attention_layernorm", C.c_void_p),
+                ("q_proj", _TensorDesc), ("k_proj", _TensorDesc), ("v_proj", _TensorDesc),
+                ("o_proj", _TensorDesc), ("gate_proj", _TensorDesc), ("up_proj", _TensorDesc),
+                ("down_proj", _TensorDesc), ("q_bias", C.c_void_p), ("k_bias", C.c_void_p),
+                ("v_bias", C.c_void_p)]
+
+
+class _ModelDesc(C.Structure):
+    _fields_ = [("config", _Config), ("embed_tokens", _TensorDesc), ("lm_head", _TensorDesc),
+                ("final_norm", C.c_void_p), ("layers", C.POINTER(_LayerDesc))]
+
+
+class MappedModel:
+    """A model file (magic LRSMODL1, JSON index, 64-byte aligned blobs) mapped
+    read-only; desc() points at an lrs_model_desc valid while this lives."""
+
+    _LAYER_T = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+    _LAYER_V = ("input_layernorm", "post_attention_layernorm", "q_bias", "k_bias", "v_bias")
+
+    def __init__(self, path: str):
+        import json
+        with open(path, "rb") as f:
+            head = f.read(16)
+            if head[:8] != b"LRSMODL1":
+                raise ValueError(f"{path}: not a model file")
+            n = int.from_bytes(head[8:16], "little")
+            meta = json.loads(f.read(n))
+        self._map = np.memmap(path, dtype=np.uint8, mode="r")
+        base = self._map.ctypes.data + (16 + n + 63) // 64 * 64
+        blobs = meta["blobs"]
+
+        def ptr(i):
+            return None if i is None else base + blobs[i][0]
+
+        def tens(t):
+            return _TensorDesc(ptr(t["blob"]), blobs[t["blob"]][1], t["rows"], t["cols"], t["type"], 0)
+
+        c = meta["config"]
+        self._layers = (_LayerDesc * c["num_hidden_layers"])()
+        for i, ent in enumerate(meta["layers"]):
+            L = self._layers[i]
+            for k in self._LAYER_T:
+                setattr(L, k, tens(ent[k]))
+            for k in self._LAYER_V:
+                setattr(L, k, ptr(ent[k]))
+        self._desc = _ModelDesc()
+        self._desc.config = _Config(*[c[k] for k, _ in _Config._fields_])
+        self._desc.embed_tokens = tens(meta["embed_tokens"])
+        self._desc.lm_head = tens(meta["lm_head"])
+        self._desc.final_norm = ptr(meta["final_norm"])
+        self._desc.layers = C.cast(self._layers, C.POINTER(_LayerDesc))
+        self.vocab_size = c["vocab_size"]
+
+    def desc(self):
+        return C.pointer(self._desc)

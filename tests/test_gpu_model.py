@@ -86,6 +86,23 @@ def test_kv_bf16_option_runs(lrs, orc, backend):
     assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
 
 
+@pytest.mark.parametrize("case", ["c0", "c3_2layers"])
+def test_kv_bf16_greedy_128_steps(lrs, orc, backend, case):
+    """The paged bf16 KV cache (the layout the batched bench runs) against the
+    reference's f32 cache: 128 greedy steps must give the same tokens; the
+    oracle's top-1/top-2 margin is reported where they do not."""
+    if case == "c0":
+        cfg, seed, n_prompt = lrs.config_c0(), 0, 128
+    else:
+        cfg, seed, n_prompt = lrs.config_c3(), 2, 64
+        cfg.num_hidden_layers = 2
+    sm, model, prompt, ref, logits, first, toks = _run_pair(
+        lrs, orc, backend, cfg, lrs.LoadQuantization.Q4KM, seed, n_prompt, 128, max_seq=512,
+        kv_bf16=True)
+    assert np.abs(logits - ref["logits"][0]).max() < LOGIT_TOL
+    _assert_tokens(ref, toks)
+
+
 def test_errors_like_reference(lrs, backend):
     cfg = _cfg(lrs, 256, 512, 4, 2, 1, 300, 64, True)
     sm = lrs.SynthModel(cfg, 1, lrs.LoadQuantization.Q4K)
