@@ -14,6 +14,7 @@
 //   Q8_0: ds = d (signed codes)
 //   Q4_K/Q5_K: ds = d*sc, dm = dmin*m per 32 columns
 //   Q6_K: ds = d*sc per 16 columns, z = 32
+//   F16 / BF16 rows: ds = 1, the weights themselves are the f16 values
 // so per group  sum_k w_k x_k = ds * sum_k (q_k - z) x_k - dm * sum_k x_k.
 // The codes minus their zero point are small integers, exact in f16; they are
 // decoded from the GGML block bytes straight into the A fragments (a code
@@ -83,6 +84,11 @@ __device__ __forceinline__ uint4 ldg128(const uint8_t* p) {
   asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
       : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg64(const uint8_t* p) {
+  uint2 v;
+  asm("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint16_t ldg16(const uint8_t* p) {
@@ -258,6 +264,28 @@ struct AFrag {
       const uint16_t sp = ldg16(u + 192 + half * 8 + quarter * 2);
       ds0 = d * (float)(int8_t)(sp & 0xffu);
       ds1 = d * (float)(int8_t)(sp >> 8);
+      ndm = 0.0f;
+    } else if constexpr (T == LRS_GGML_F16 || T == LRS_GGML_BF16) {
+      // dense rows: the f16 weights are the A values (ds = 1); a BF16 weight
+      // is rounded to f16, exact for |w| in the f16 normal range
+      // [2^-14, 65504] (bf16 keeps 8 significant bits, f16 11), within
+      // 2^-25 absolute below it
+      const uint8_t* u = rp + (size_t)gc * 64;
+      const uint2 a = ldg64(u + 8 * t), b = ldg64(u + 32 + 8 * t);
+      uint32_t w[4] = {a.x, a.y, b.x, b.y};
+      if constexpr (T == LRS_GGML_BF16) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const __half2 hv = __floats2half2_rn(__uint_as_float(w[i] << 16),
+                                               __uint_as_float(w[i] & 0xffff0000u));
+          w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+      }
+      h[0] = __byte_perm(w[0], w[1], 0x5410);  // columns (4t, 4t + 2)
+      h[1] = __byte_perm(w[0], w[1], 0x7632);  // columns (4t + 1, 4t + 3)
+      h[2] = __byte_perm(w[2], w[3], 0x5410);
+      h[3] = __byte_perm(w[2], w[3], 0x7632);
+      ds0 = ds1 = 1.0f;
       ndm = 0.0f;
     } else if constexpr (T == LRS_GGML_Q8_0) {
       // d, qs[32] (i8); value_at, src/quant.rs:395-400
@@ -650,14 +678,18 @@ cudaError_t launch_type(int type, int nt, const GemmArgs& a, dim3 grid, cudaStre
     case LRS_GGML_Q4_K: return launch_nt<LRS_GGML_Q4_K, PAIR>(nt, a, grid, st);
     case LRS_GGML_Q5_K: return launch_nt<LRS_GGML_Q5_K, PAIR>(nt, a, grid, st);
     case LRS_GGML_Q6_K: return launch_nt<LRS_GGML_Q6_K, PAIR>(nt, a, grid, st);
+    case LRS_GGML_F16: return launch_nt<LRS_GGML_F16, PAIR>(nt, a, grid, st);
+    case LRS_GGML_BF16: return launch_nt<LRS_GGML_BF16, PAIR>(nt, a, grid, st);
   }
   return cudaErrorInvalidValue;
 }
 
-bool quantized(int type) {
+// Types with an A-fragment decoder: every quantized type, and F16 / BF16 rows.
+bool mma_type(int type) {
   switch (type) {
     case LRS_GGML_Q4_0: case LRS_GGML_Q4_1: case LRS_GGML_Q5_0: case LRS_GGML_Q5_1:
     case LRS_GGML_Q8_0: case LRS_GGML_Q4_K: case LRS_GGML_Q5_K: case LRS_GGML_Q6_K:
+    case LRS_GGML_F16: case LRS_GGML_BF16:
       return true;
   }
   return false;
@@ -680,7 +712,7 @@ int layout_tiles(int batch) {
 bool gemm_supported(const GemvParams& p) {
   if (p.batch < 2 || p.cols % 32) return false;
   for (int i = 0; i < p.nseg; i++)
-    if (!quantized(p.seg[i].type)) return false;
+    if (!mma_type(p.seg[i].type)) return false;
   return true;
 }
 

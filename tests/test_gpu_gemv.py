@@ -34,7 +34,9 @@ def row_norms(orc, t, rows, cols, chunk=4096):
 
 def _check_rows(got, ref, wnorm=None, x=None):
     """The row bar; without norms the floor is |scalar| >= 1 (the shape of
-    src/quant.rs:1029).  Returns the largest relative error."""
+    src/quant.rs:1029).  Returns (largest err / max(|s|, floor): the share of
+    the relative bar used, largest pure relative error over rows with
+    |s| >= floor)."""
     g, r = got.astype(np.float64), ref.astype(np.float64)
     err = np.abs(g - r)
     if wnorm is None:
@@ -45,7 +47,9 @@ def _check_rows(got, ref, wnorm=None, x=None):
     bad = np.nonzero(err > bound)
     assert bad[0].size == 0, (f"{bad[0].size} rows off; worst err {err.max():.3e} "
                               f"at |ref| {np.abs(r[bad[0][0]]):.3e}")
-    return float((err / np.maximum(np.abs(r), 1e-30)).max())
+    big = np.abs(r) >= floor
+    rel = float((err[big] / np.abs(r[big])).max()) if big.any() else 0.0
+    return float((err / np.maximum(np.abs(r), floor)).max()), rel
 
 
 def _kat():
@@ -147,15 +151,17 @@ def test_sweep_shapes_every_row(lrs, orc, backend, qt, shape):
     assert t.quant_type == lrs.QuantType[qt]
     wn = row_norms(orc, t, rows, cols)
     rng = np.random.default_rng(7)
-    worst = 0.0
+    worst = worst_rel = 0.0
     big = rows * cols > 100_000_000
     for batch, items in ((1, [0]), (8, [0, 7] if big else range(8)), (64, [0, 31, 63])):
         x = rng.standard_normal((batch, cols)).astype(np.float32)
         got = backend.matvec_batched(t, x)
         for b in items:
             ref = orc.matvec(orc.SCALAR, t.data, int(t.quant_type), rows, cols, x[b])
-            worst = max(worst, _check_rows(got[b], ref, wn, x[b]))
-    print(f"{qt} {rows}x{cols}: max relative row error {worst:.2e}")
+            used, rel = _check_rows(got[b], ref, wn, x[b])
+            worst, worst_rel = max(worst, used), max(worst_rel, rel)
+    print(f"{qt} {rows}x{cols}: max err/max(|s|, |w||x|/sqrt(n)) {worst:.2e}, "
+          f"max relative error where |s| >= |w||x|/sqrt(n) {worst_rel:.2e}")
     backend.release(t)
 
 
