@@ -417,6 +417,7 @@ struct lrs_model {
   size_t gemm_scratch_bytes = 0;
   unsigned long long* keys = nullptr;
   int *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_step = nullptr;
+  unsigned* d_attn_cnt = nullptr;  // [max_items][kv heads] split counters of the fused attention
   uint32_t* d_last = nullptr;
   uint32_t* d_tokens_out = nullptr;
   size_t tokens_out_cap = 0;  // in elements
@@ -537,13 +538,17 @@ int32_t setup_tp_p2p(lrs_model* m, int h) {
   return LRS_OK;
 }
 
-// Splits of each sequence's context: as many as fit in one wave of resident
-// attention CTAs (batch * kv heads * splits CTAs), so no tail wave.
+// Splits of each sequence's context: about eight waves of resident attention
+// CTAs (batch * kv heads * splits CTAs), so that CTAs of different lengths
+// even out across the SMs and each SM's second CTA streams while the first
+// starts or finishes.
 int nsplit_for(const lrs_model* m, int batch) {
   const int slots = m->be->sms * attention_ctas_per_sm((int)m->c.head_dim,
                                                        m->opt.kv_dtype == LRS_KV_BF16);
-  int want = slots / (batch * (int)m->c.num_key_value_heads);
-  int maxs = std::max(1, (int)((m->opt.max_seq_len + 31) / 32));
+  int want = 8 * slots / (batch * (int)m->c.num_key_value_heads);
+  // at least 128 positions per split of a full context: a split's tiles are
+  // copied back to back, and the merge reads fewer partials
+  int maxs = std::max(1, (int)((m->opt.max_seq_len + 127) / 128));
   return std::max(1, std::min({want, m->max_split, maxs}));
 }
 
@@ -639,10 +644,21 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
       m->prof_attn->push_back(a1);
       cudaEventRecord(a0, st);
     }
-    LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
-                               L.kpool, L.vpool, kv_bf16, st));
-    LRS_CUDA(launch_attention(m->q, io, B, nh, nkv, hd, L.kpool, L.vpool, kv_bf16, nsplit, m->part,
-                              m->att, st));
+    // every item its own sequence (a decode step): RoPE, the KV store and the
+    // split merge run inside the attention kernel; prefill chunks (items of
+    // one sequence read each other's rows) store every row first
+    const bool fused_attn = lm_item == -1 || B == 1;
+    if (!fused_attn)
+      LRS_CUDA(launch_rope_store(m->q, m->k, m->v, m->rope_cos, m->rope_sin, io, B, nh, nkv, hd,
+                                 L.kpool, L.vpool, kv_bf16, st));
+    AttnLaunch al{};
+    al.q = m->q, al.k = m->k, al.v = m->v, al.cos_t = m->rope_cos, al.sin_t = m->rope_sin;
+    al.io = io;
+    al.batch = B, al.nh = nh, al.nkv = nkv, al.hd = hd, al.kv_bf16 = kv_bf16, al.nsplit = nsplit;
+    al.kpool = L.kpool, al.vpool = L.vpool;
+    al.part = m->part, al.att = m->att, al.cnt = m->d_attn_cnt, al.err = m->be->d_err;
+    al.fused = fused_attn;
+    LRS_CUDA(launch_attention(al, st));
     if (a1) cudaEventRecord(a1, st);
     // o_proj + residual (src/model.rs:233-238)
     GemvMat om = mat_of(L.o, res_out(), h);
@@ -1188,8 +1204,10 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->d_pos, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_seq, B * 4)) ||
       (rc = model_alloc(m.get(), (void**)&m->d_step, 4)) ||
-      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)))
+      (rc = model_alloc(m.get(), (void**)&m->d_last, B * 4)) ||
+      (rc = model_alloc(m.get(), (void**)&m->d_attn_cnt, B * c.num_key_value_heads * 4)))
     return cleanup(rc);
+  LRS_CUDA(cudaMemset(m->d_attn_cnt, 0, B * c.num_key_value_heads * 4));
   {
     size_t ow = 0, dw = 0;
     for (const auto& L : m->layers) {

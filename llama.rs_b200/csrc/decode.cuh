@@ -34,12 +34,25 @@ cudaError_t launch_rope_store(float* q, const float* k, const float* v, const fl
                               const float* sin_t, StepIO io, int batch, int nh, int nkv, int hd,
                               void* kpool, void* vpool, int kv_bf16, cudaStream_t st);
 // Split-K GQA decode attention over the paged cache (src/model.rs:206-231 with
-// softmax_inplace :298-313), then the cross-split combine into att[b][nh*hd].
+// softmax_inplace :298-313) into att[b][nh*hd].  Unfused: q already rotated
+// and the position's K/V already stored (launch_rope_store), a combine kernel
+// merges the splits.  Fused (every item a different sequence): the kernel
+// rotates q and k, stores the position's K/V and merges the splits itself
+// (cnt: [B][nkv] zeroed counters, left zeroed).  `err` is set to 1 if a tile
+// copy never completes (bounded wait).
+struct AttnLaunch {
+  const float *q, *k, *v, *cos_t, *sin_t;
+  StepIO io;
+  int batch, nh, nkv, hd, kv_bf16, nsplit;
+  void *kpool, *vpool;
+  float *part, *att;
+  unsigned* cnt;
+  int* err;
+  bool fused;
+};
 // Resident attention CTAs per SM (occupancy of the split kernel).
 int attention_ctas_per_sm(int hd, int kv_bf16);
-cudaError_t launch_attention(const float* q, StepIO io, int batch, int nh, int nkv, int hd,
-                             const void* kpool, const void* vpool, int kv_bf16, int nsplit,
-                             float* part, float* att, cudaStream_t st);
+cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st);
 // Greedy bookkeeping after the LM head: tok[b] = argmax, pos[b] += 1,
 // tokens_out[step * B + b] = argmax while step < n_steps; step += 1.
 // x of a windowed tensor-parallel column shard: dst[b][0..width) holds

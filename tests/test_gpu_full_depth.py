@@ -8,11 +8,20 @@ made tests/golden/model_<case>.json).
 * c2: Qwen2.5-1.5B shape, 28 layers, q4k (tied Q4_K head), 512-token prompt,
   128 greedy steps.
 
-Bars: logits within 2e-2 max-abs at the stored indices (the oracle's top 64
-and 1024 seeded random ones) after the prompt and after the last step, and
-identical greedy tokens (on a mismatch the oracle's top-1/top-2 margin at
-that step is reported).  The fixture records a SHA-256 of the model bytes; the
-test rebuilds the model and checks it first.
+Bars:
+* prefill: logits within 2e-2 max-abs at the stored indices (the oracle's
+  top 64 and 1024 seeded random ones) and the same first token;
+* teacher-forced decode (the oracle's tokens fed, one forward_token per
+  step): all 128 argmaxes equal the oracle's, except at a step whose oracle
+  top-1/top-2 margin is below NEAR_TIE, and the logits after the last step
+  within 2e-2;
+* free-running greedy decode (the benchmark's loop, one CUDA graph per step):
+  the tokens equal the oracle's up to the first step whose margin is below
+  NEAR_TIE (a near-tie flip changes every later token; the teacher-forced
+  pass still checks the steps after it).
+NEAR_TIE = 1e-3 is twenty times below the logit bar: two logits closer than
+the bar allows may swap.  The fixture records a SHA-256 of the model bytes;
+the test rebuilds the model and checks it first.
 """
 import json
 import os
@@ -27,6 +36,7 @@ sys.path.insert(0, os.path.join(HERE, "golden"))
 import model_golden  # noqa: E402
 
 LOGIT_TOL = 2e-2
+NEAR_TIE = 1e-3
 
 
 def _fixture(name):
@@ -55,17 +65,33 @@ def test_full_depth_greedy_matches_oracle(lrs, backend, name, persistent):
     err0 = _logit_err(logits, fx["logits"]["0"])
     assert err0 < LOGIT_TOL, f"prefill logits max-abs error {err0}"
     assert first == fx["logits"]["0"]["argmax"]
-    produced = model.decode_greedy([first], [len(prompt)], n_decode)[:, 0]
-    fed = np.concatenate([[first], produced[:-1]]).astype(np.int64)
     want = np.asarray(fx["tokens"], np.int64)
-    if not np.array_equal(fed, want):
-        i = int(np.nonzero(fed != want)[0][0])
-        raise AssertionError(f"greedy tokens diverge at step {i}: oracle {want[i]} gpu {fed[i]}; "
-                             f"oracle top1-top2 margin there {fx['margins'][i]:.3e}")
-    # logits after the last step: that step again (it rewrites the same KV row)
-    last, am = model.forward_token(int(fed[-1]), len(prompt) + n_decode - 1)
-    assert am == produced[-1]
+    margins = np.asarray(fx["margins"], np.float64)
+    n0 = len(prompt)
+    # teacher-forced: step s feeds want[s]; the oracle's argmax is want[s + 1]
+    flips = []
+    for s in range(n_decode):
+        last, am = model.forward_token(int(want[s]), n0 + s)
+        exp = int(want[s + 1]) if s + 1 < n_decode else fx["logits"][str(n_decode)]["argmax"]
+        if am != exp:
+            flips.append((s, margins[s + 1]))
+            assert margins[s + 1] < NEAR_TIE, (
+                f"teacher-forced step {s}: gpu {am}, oracle {exp}, oracle margin {margins[s + 1]:.3e}")
     err1 = _logit_err(last, fx["logits"][str(n_decode)])
     assert err1 < LOGIT_TOL, f"final logits max-abs error {err1}"
-    print(f"{name}: prefill err {err0:.2e}, final err {err1:.2e}, {n_decode} tokens match")
+    # free-running greedy (the benchmark's decode loop)
+    produced = model.decode_greedy([first], [n0], n_decode)[:, 0]
+    fed = np.concatenate([[first], produced[:-1]]).astype(np.int64)
+    close = np.nonzero(margins[:n_decode] < NEAR_TIE)[0]
+    first_close = int(close[0]) if close.size else n_decode
+    diff = np.nonzero(fed != want)[0]
+    if diff.size:
+        i = int(diff[0])
+        assert i >= first_close, (f"greedy tokens diverge at step {i}: oracle {want[i]} gpu {fed[i]}; "
+                                  f"oracle top1-top2 margin there {margins[i]:.3e}")
+        greedy = f"greedy equal up to the near-tie at step {i} (margin {margins[i]:.2e})"
+    else:
+        greedy = f"{n_decode} greedy tokens match"
+    print(f"{name}: prefill err {err0:.2e}, teacher-forced final err {err1:.2e}, "
+          f"near-tie flips {flips}, {greedy}")
     model.close()
