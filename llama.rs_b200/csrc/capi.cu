@@ -418,6 +418,10 @@ struct lrs_model {
   unsigned long long* keys = nullptr;
   int *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_step = nullptr;
   unsigned* d_attn_cnt = nullptr;  // [max_items][kv heads] split counters of the fused attention
+  // batch-1 steps run the projections of a second GGML type among q/k/v (v
+  // in Q8_0 under q4km) on a side stream, beside the first type's launch
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   uint32_t* d_last = nullptr;
   uint32_t* d_tokens_out = nullptr;
   size_t tokens_out_cap = 0;  // in elements
@@ -623,18 +627,48 @@ int32_t enqueue_step(lrs_model* m, int B, int lm_item, bool want_logits, bool gr
     // input_layernorm + q/k/v projections with bias (src/model.rs:175-186)
     GemvMat qkv[3] = {mat_of(L.q, m->q, qw, L.qb), mat_of(L.k, m->k, kvw, L.kb),
                       mat_of(L.v, m->v, kvw, L.vb)};
-    if ((rc = gemv_plan(&p, qkv, 3, EPI_STORE, B))) return rc;
-    p.error_flag = m->be->d_err;
-    if (B == 1 || gemm_supported(p)) {  // the norm is fused into the x preparation
-      p.x = m->residual;
-      p.norm_w = L.in_norm;
-      p.norm_eps = c.rms_norm_eps;
-    } else {
-      LRS_CUDA(launch_rmsnorm(m->residual, L.in_norm, c.rms_norm_eps, h, B, m->xn, st));
-      p.x = m->xn;
+    // batch 1, two GGML types among q/k/v, not profiling: the second type's
+    // segments on the side stream (its launch is a separate one anyway)
+    GemvMat first[3], second[3];
+    int nf = 0, ns = 0;
+    for (int i = 0; i < 3; i++) {
+      if (qkv[i].type == qkv[0].type) first[nf++] = qkv[i];
+      else second[ns++] = qkv[i];
     }
-    p.x_ld = h;
-    LRS_CUDA(model_gemv(m, p, st, sms));
+    bool fork = B == 1 && ns > 0 && !m->prof && m->side;
+    for (int i = 1; i < ns; i++) fork = fork && second[i].type == second[0].type;
+    auto qkv_input = [&](GemvParams& q) {
+      q.error_flag = m->be->d_err;
+      q.x = m->residual;  // the norm is fused into the x preparation
+      q.norm_w = L.in_norm;
+      q.norm_eps = c.rms_norm_eps;
+      q.x_ld = h;
+    };
+    if (fork) {
+      GemvParams p2;
+      if ((rc = gemv_plan(&p, first, nf, EPI_STORE, B)) ||
+          (rc = gemv_plan(&p2, second, ns, EPI_STORE, B)))
+        return rc;
+      qkv_input(p);
+      qkv_input(p2);
+      LRS_CUDA(cudaEventRecord(m->ev_fork, st));
+      LRS_CUDA(cudaStreamWaitEvent(m->side, m->ev_fork, 0));
+      LRS_CUDA(model_gemv(m, p2, m->side, sms));
+      LRS_CUDA(cudaEventRecord(m->ev_join, m->side));
+      LRS_CUDA(model_gemv(m, p, st, sms));
+      LRS_CUDA(cudaStreamWaitEvent(st, m->ev_join, 0));
+    } else {
+      if ((rc = gemv_plan(&p, qkv, 3, EPI_STORE, B))) return rc;
+      p.error_flag = m->be->d_err;
+      if (B == 1 || gemm_supported(p)) {  // the norm is fused into the x preparation
+        qkv_input(p);
+      } else {
+        LRS_CUDA(launch_rmsnorm(m->residual, L.in_norm, c.rms_norm_eps, h, B, m->xn, st));
+        p.x = m->xn;
+        p.x_ld = h;
+      }
+      LRS_CUDA(model_gemv(m, p, st, sms));
+    }
     // RoPE + KV store (src/model.rs:188-205), attention (:206-231)
     cudaEvent_t a0 = nullptr, a1 = nullptr;
     if (m->prof_attn) {
@@ -1208,6 +1242,9 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
       (rc = model_alloc(m.get(), (void**)&m->d_attn_cnt, B * c.num_key_value_heads * 4)))
     return cleanup(rc);
   LRS_CUDA(cudaMemset(m->d_attn_cnt, 0, B * c.num_key_value_heads * 4));
+  LRS_CUDA(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking));
+  LRS_CUDA(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming));
+  LRS_CUDA(cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming));
   {
     size_t ow = 0, dw = 0;
     for (const auto& L : m->layers) {
@@ -1315,6 +1352,9 @@ void lrs_model_destroy(lrs_model* m) {
       cudaStreamSynchronize(m->be->stream);
   }
   for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+  if (m->side) cudaStreamDestroy(m->side);
+  if (m->ev_fork) cudaEventDestroy(m->ev_fork);
+  if (m->ev_join) cudaEventDestroy(m->ev_join);
   cudaFree(m->embed.d);
   if (!m->tied) cudaFree(m->lm.d);
   for (void* p : m->allocs) cudaFree(p);
