@@ -606,7 +606,10 @@ int occupancy(const void* kernel, int smem, int threads = kGemvThreads) {
   std::lock_guard<std::mutex> g(mu);
   for (auto& c : cache)
     if (c.dev == dev && c.k == kernel && c.smem == smem && c.threads == threads) return c.blocks;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // the dynamic limit is what the static shared memory leaves of 227 KB
+  cudaFuncAttributes fa{};
+  const int stat = cudaFuncGetAttributes(&fa, kernel) == cudaSuccess ? (int)fa.sharedSizeBytes : 0;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - stat);
   int blocks = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem);
   cache.push_back({dev, kernel, smem, blocks, threads});
