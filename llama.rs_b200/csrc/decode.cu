@@ -280,6 +280,40 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
     }
     fence_barrier_init();
   }
+  __syncthreads();
+
+  if (warp == kAttnWarps) {  // producer
+    if (lane == 0) {
+      // decode steps: the tiles hold earlier positions only (the new one is
+      // written over its staged copy), so they stream before the projection
+      // that precedes this kernel has finished; prefill chunks read rows
+      // rope_store_kernel just wrote
+      if constexpr (!FUSED) pdl_wait();
+      const uint64_t pol = evict_first_policy();
+      const uint8_t* kb = reinterpret_cast<const uint8_t*>(a.kpool);
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.vpool);
+      for (int i = 0; i < ntiles; i++) {
+        const int st = i % sp.stages;
+        if (i >= sp.stages && !mbar_wait_bounded(&empty[st], ((i / sp.stages) - 1) & 1)) {
+          atomicExch(a.err, 1);
+          break;
+        }
+        const size_t off = kv_offset(a.io, b, s0 + kTile * i, nkv, kvh, HD) * ESZ;
+        uint8_t* dst = smem + sp.ring + (size_t)st * 2 * sp.tile;
+        mbar_expect_tx(&full[st], 2u * sp.tile);
+        tma_load_1d(dst, kb + off, sp.tile, &full[st], pol);
+        tma_load_1d(dst + sp.tile, vb + off, sp.tile, &full[st], pol);
+      }
+      // stay until the last copies have landed (they may outlive the consumers
+      // on an error exit)
+      for (int i = max(0, ntiles - sp.stages); i < ntiles; i++)
+        if (!mbar_wait_bounded(&full[i % sp.stages], (i / sp.stages) & 1)) atomicExch(a.err, 1);
+    }
+    return;
+  }
+
+
+  pdl_wait();  // q, k, v come from the projection launched before this kernel
   const float* cs = FUSED ? a.cos_t + (size_t)pos_new * HALF : nullptr;
   const float* sn = FUSED ? a.sin_t + (size_t)pos_new * HALF : nullptr;
   // RoPE (apply_rope_inplace, src/model.rs:86-95) of element d of a head row
@@ -289,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
     return d < HALF ? __fsub_rn(__fmul_rn(re, cs[i]), __fmul_rn(im, sn[i]))
                     : __fadd_rn(__fmul_rn(re, sn[i]), __fmul_rn(im, cs[i]));
   };
-  for (int i = tid; i < kMaxGroup * HD; i += kAttnThreads) {
+  for (int i = tid; i < kMaxGroup * HD; i += kAttnCons) {
     const int g = i / HD, d = i % HD;
     float val = 0.0f;
     if (g < G) {
@@ -315,32 +349,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
       reinterpret_cast<float*>(newrow + ROWB)[tid] = vr;
     }
   }
-  __syncthreads();
-
-  if (warp == kAttnWarps) {  // producer
-    if (lane == 0) {
-      const uint64_t pol = evict_first_policy();
-      const uint8_t* kb = reinterpret_cast<const uint8_t*>(a.kpool);
-      const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.vpool);
-      for (int i = 0; i < ntiles; i++) {
-        const int st = i % sp.stages;
-        if (i >= sp.stages && !mbar_wait_bounded(&empty[st], ((i / sp.stages) - 1) & 1)) {
-          atomicExch(a.err, 1);
-          break;
-        }
-        const size_t off = kv_offset(a.io, b, s0 + kTile * i, nkv, kvh, HD) * ESZ;
-        uint8_t* dst = smem + sp.ring + (size_t)st * 2 * sp.tile;
-        mbar_expect_tx(&full[st], 2u * sp.tile);
-        tma_load_1d(dst, kb + off, sp.tile, &full[st], pol);
-        tma_load_1d(dst + sp.tile, vb + off, sp.tile, &full[st], pol);
-      }
-      // stay until the last copies have landed (they may outlive the consumers
-      // on an error exit)
-      for (int i = max(0, ntiles - sp.stages); i < ntiles; i++)
-        if (!mbar_wait_bounded(&full[i % sp.stages], (i / sp.stages) & 1)) atomicExch(a.err, 1);
-    }
-    return;
-  }
+  attn_consumer_sync();
 
   float m = -INFINITY, l = 0.0f;  // running state of head `warp` (softmax warps)
   float o[kMaxGroup];
@@ -451,6 +460,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const __grid_c
     __syncwarp();
     if (lane == 0) attn_arrive(&empty[st]);
   }
+  pdl_launch_dependents();
   // per-head totals, then merge the position ranges and write (max, sum, o)
   if (warp < G && lane == 0) {
     om[warp * 2] = m;  // om is free until the merge below
@@ -671,8 +681,17 @@ cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
   a.kpool = l.kpool, a.vpool = l.vpool;
   a.part = l.part, a.att = l.att, a.cnt = l.cnt, a.err = l.err;
   void* args[] = {&a};
-  e = cudaLaunchKernel(k, dim3(l.nsplit, l.nkv, l.batch), dim3(kAttnThreads), args,
-                       attn_smem(l.hd, l.kv_bf16 ? 2 : 4).total, st);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(l.nsplit, l.nkv, l.batch);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = attn_smem(l.hd, l.kv_bf16 ? 2 : 4).total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelExC(&cfg, k, args);
   if (e != cudaSuccess || l.fused) return e;
   if (l.hd == 128)
     attn_combine_kernel<128><<<dim3(l.nh, l.batch), 128, 0, st>>>(l.part, l.io.pos, l.nh, l.nsplit,
