@@ -122,9 +122,10 @@ class ClockSampler:
 
 
 def launches_per_step(layers, batch):
-    # embed, per layer [rmsnorm] qkv rope_store attn combine o [rmsnorm] gate_up down,
-    # then [rmsnorm] lm_head advance
-    per_layer = 7 + (2 if batch > 1 else 0)
+    # estimate when the graph's node count is unavailable: embed, per layer
+    # q/k, v, attention, o, gate_up, down (+ x preparation and K-split sums at
+    # batch > 1), then lm_head, advance
+    per_layer = 6 + (3 if batch > 1 else 0)
     return 1 + layers * per_layer + (2 if batch == 1 else 3)
 
 
@@ -194,7 +195,11 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
                          f"data-parallel over {world} GPU(s)"),
             "parallelism": f"tp{world}" if tp else f"dp{world}",
             "sequences_per_gpu": total_seqs if tp else total_seqs // max(world, 1), "prompt": P,
-            "kv_cache": "bf16" if kv_bf16 else "f32"}
+            "kv_cache": "bf16" if kv_bf16 else "f32",
+            "arithmetic": ("weights decoded exactly from their GGML blocks; f32 accumulation; "
+                           "x split for the dot products: batch 1 int8 hi/lo per 8 columns "
+                           "(~15 bits, dp4a), batched f16 hi + lo (~22 bits, tensor cores, "
+                           "exact products); attention and norms in f32")}
 
 
 def run_reference(args, wl):
@@ -427,7 +432,7 @@ def run_ours(args, wl):
                          "bytes_per_launch": wbytes / gemv_n, "ms_per_launch": gemv_ms / gemv_n,
                          "launches": gemv_n, "peak_kind": peak_kind,
                          "share_of_step": gemv_ms / prof_step_ms},
-            "attention": {"kernel": "rope_store + attn_split + attn_combine, all layers",
+            "attention": {"kernel": "attn_split_kernel (RoPE, KV store and split merge fused), all layers",
                           "kv_bytes_per_step": kv_bytes, "ms": attn_ms,
                           "achieved_gbs": kv_bytes / (attn_ms / 1e3) / 1e9,
                           "frac": kv_bytes / (attn_ms / 1e3) / 1e9 / hbm,
