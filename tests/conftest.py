@@ -59,3 +59,26 @@ def backend(lrs):
     be = lrs.CudaBackend(0)
     yield be
     be.close()
+
+
+# Greedy tokens may swap only where two logits are closer than any bar can
+# separate: at a step whose oracle top-1/top-2 margin is below NEAR_TIE
+# (twenty times below the 2e-2 logit bar).  After such a swap the sequences
+# differ by construction, so the comparison stops there.
+NEAR_TIE = 1e-3
+
+
+def assert_greedy(ref, toks, near_tie=NEAR_TIE):
+    """ref: oracle benchmark_tokens() result (tokens, margins); toks: the
+    tokens the GPU fed at each step.  Equal up to the first near-tie."""
+    import numpy as np
+    want = np.asarray(ref["tokens"])
+    toks = np.asarray(toks)
+    diff = np.nonzero(want != toks)[0]
+    if not diff.size:
+        return None
+    i = int(diff[0])
+    margin = float(ref["margins"][i])
+    assert margin < near_tie, (f"greedy tokens diverge at step {i}: oracle {want[i]} gpu {toks[i]}; "
+                               f"oracle top1-top2 margin there {margin:.3e}")
+    return i

@@ -34,9 +34,9 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
 import model_golden  # noqa: E402
+from conftest import NEAR_TIE  # noqa: E402
 
 LOGIT_TOL = 2e-2
-NEAR_TIE = 1e-3
 
 
 def _fixture(name):
