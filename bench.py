@@ -121,6 +121,11 @@ class ClockSampler:
                 "samples": len(rows), "reasons": sorted(reasons)}
 
 
+# DRAM bytes read + written per batched-matmul call of a 64-sequence c3 step
+# (5.10 GB over 113 calls), profiles/matmul_traffic_c3_b64.md.
+MATMUL_TRAFFIC_C3_B64 = 45.1e6
+
+
 def launches_per_step(layers, batch):
     # estimate when the graph's node count is unavailable: embed, per layer
     # q/k, v, attention, o, gate_up, down (+ x preparation and K-split sums at
@@ -414,6 +419,14 @@ def run_ours(args, wl):
 
     if rank == 0:
         nl = launches_per_step(cfg.num_hidden_layers, B)
+        # DRAM bytes per matmul call from one ncu capture of this workload's
+        # launch shapes (profiles/matmul_traffic_c3_b64.md); other workloads
+        # have no capture
+        full_c3 = (args.config == "c3" and B == 64 and not wl.get("layers") and not args.kv_bf16
+                   and not args.prompt and not args.ctx)
+        traffic = MATMUL_TRAFFIC_C3_B64 if full_c3 else None
+        traffic_src = ("ncu dram__bytes_read+write per matmul launch, profiles/matmul_traffic_c3_b64.md"
+                       if full_c3 else None)
         line = {
             "metric": "decode_tokens_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
@@ -425,7 +438,8 @@ def run_ours(args, wl):
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
                     "d2h_bytes_per_step": 4 * B + 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
+                         "frac": achieved / hbm, "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "kernel": ("gemm_tc_kernel (tcgen05, Q4_K/Q6_K) + gemm_mma_kernel (Q8_0): batched quantized matmul (x split, matmul, "
                                     "K-split epilogue) of every projection and the LM head"
                                     if B > 1 else "gemv5_kernel: batch-1 quantized GEMV"),
