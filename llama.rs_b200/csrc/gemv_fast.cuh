@@ -5,17 +5,21 @@
 // bandwidth leaves.  Here the same dot is computed in factored form: per group
 // of values sharing a scale,
 //     sum_k w_k x_k = scale * sum_k q_k x_k + offset * sum_k x_k,
-// with sum_k x_k precomputed per 8-column run, and sum_k q_k x_k accumulated
-// from codes turned into floats by one byte-permute each: a code q < 128 in
-// bits 16..22 of 0x3F000000 is the float f = 0.5 + q/256 exactly, so
-//     sum q x = 256 * sum f x - 128 * sum x.
-// Products accumulate with packed fma.rn.f32x2.  Agreement with the reference
-// dot is ~1e-6 relative (the parity bar is 1e-3).
+// with sum_k x_k precomputed per 8-column run.  The default path
+// (gemv5_kernel, gemv.cu) takes sum_k q_k x_k in integers: x is split per
+// 8-column run as x ~= s_r * (xh + xl / 256) with int8 halves (about 15
+// bits), and every 4 codes meet their x bytes in one dp4a (hi and lo sums
+// exact in int32, (hi << 8) + lo), then one float multiply per run
+// (icode / finish_i below).  Agreement with the reference dot is ~1e-5
+// relative (the parity bar is 1e-3).  Dense types multiply float x directly
+// with packed fma.rn.f32x2 (weights / finish).  icode and finish_i are built on
+// code_word (the 4 codes of a word) and finish (the scales applied to per-group
+// sums).
 //
 // A "piece" is the unit one lane handles: 64 values (a group pair) for
 // Q4_K/Q5_K, 32 values otherwise.  load() reads its bytes straight from global
-// memory into registers; code_word(i) yields 4 codes for x columns
-// col(sub, i)..+3; finish() applies the scales.
+// memory (or shared memory) into registers; icode(i) / code_word(i) yield 4
+// codes for x columns col(sub, i)..+3; finish_i() / finish() apply the scales.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
