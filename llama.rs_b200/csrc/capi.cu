@@ -287,7 +287,6 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
                              size_t batch, float* d_out, void* stream) {
   if (!be || !w || !d_in || !d_out) return fail(LRS_ERR_INVALID, "null argument");
   if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
-  cudaStream_t st0 = stream ? (cudaStream_t)stream : be->stream;
   GemvMat m = mat_of(w->t, d_out, w->t.rows);
   GemvParams p;
   int32_t rc = gemv_plan(&p, &m, 1, EPI_STORE, (int)batch);
