@@ -200,11 +200,14 @@ def workload_config(wl, total_seqs, P, world, tp, layers=0, kv_bf16=False):
                          f"data-parallel over {world} GPU(s)"),
             "parallelism": f"tp{world}" if tp else f"dp{world}",
             "sequences_per_gpu": total_seqs if tp else total_seqs // max(world, 1), "prompt": P,
-            "kv_cache": "bf16" if kv_bf16 else "f32",
-            "arithmetic": ("weights decoded exactly from their GGML blocks; f32 accumulation; "
-                           "x split for the dot products: batch 1 int8 hi/lo per 8 columns "
-                           "(~15 bits, dp4a), batched f16 hi + lo (~22 bits, tensor cores, "
-                           "exact products); attention and norms in f32")}
+            "kv_cache": "bf16" if kv_bf16 else "f32"}
+
+
+# The arithmetic of this implementation's dot products (the GPU arm's config).
+GPU_ARITHMETIC = ("weights decoded exactly from their GGML blocks; f32 accumulation; x split "
+                  "for the dot products: batch 1 int8 hi/lo per 8 columns (~15 bits, dp4a), "
+                  "batched f16 hi + lo (~22 bits, tensor cores, exact products); attention and "
+                  "norms in f32")
 
 
 def run_reference(args, wl):
@@ -247,7 +250,8 @@ def run_reference(args, wl):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and ids)",
         "config": dict(workload_config(wl, args.seqs or wl["seqs"], P, args.gpus,
                                        args.tp and args.gpus > 1, wl.get("layers", 0), args.kv_bf16),
-                       kernel="avx2", threads=threads, cpu=cpu_model()),
+                       kernel="avx2", threads=threads, cpu=cpu_model(),
+                       arithmetic="the reference AVX2 dots (src/simd.rs): f32 weights times f32 x"),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample + "; C++ restatement of the reference AVX2 backend "
                                             "(src/simd.rs) -- the Rust reference cannot be built "
@@ -434,6 +438,7 @@ def run_ours(args, wl):
             "data": "synthetic (seeded random weights N(0,0.02), uniform prompt ids)",
             "config": {**workload_config(wl, total_seqs, P, world, tp, wl.get("layers", 0),
                                          args.kv_bf16),
+                       "arithmetic": GPU_ARITHMETIC,
                        "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights streamed per step"},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
                     "d2h_bytes_per_step": 4 * B + 4},
