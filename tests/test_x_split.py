@@ -108,3 +108,36 @@ def test_split_bits():
     e2 = np.abs(split_batched(x) - x) / np.abs(x).max()
     assert e1.max() < 2.0 ** -14.9
     assert e2.max() < 2.0 ** -21
+
+
+def _f16_exact(v):
+    v = np.asarray(v, np.float64)
+    return np.array_equal(v.astype(np.float16).astype(np.float64), v)
+
+
+def test_tensor_core_operands_are_exact_in_f16():
+    """Every A value the tensor-core matmuls build from the GGML codes is an
+    exact f16, so each product with an f16 x half is exact in f32 (11 x 11
+    significant bits) and only the f32 accumulation rounds."""
+    q4 = np.arange(16)
+    sc6 = np.arange(64)
+    # gemm_tc Q4_K: A = sc * q (6-bit scale, 4-bit code); A_min = 32 * m
+    assert _f16_exact(np.outer(sc6, q4)) and _f16_exact(32 * sc6)
+    # gemm_tc Q6_K: (q - 32) * (sc & 15) and (q - 32) * (sc - (sc & 15)), sc int8
+    q6 = np.arange(64) - 32
+    sc8 = np.arange(-128, 128)
+    assert _f16_exact(np.outer(q6, sc8 & 15))
+    assert _f16_exact(np.outer(q6, sc8 - (sc8 & 15)))
+    # gemm_mma: q - z for every type (Q8_0 signed codes; 5-bit codes minus 16)
+    assert _f16_exact(np.arange(-128, 128)) and _f16_exact(np.arange(32) - 16)
+    # the x halves: |x / s| < 2^14 with s a power of two, so hi and lo are
+    # finite f16 and hi * A < 2^14 * 2^12 stays far below the f32 range
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(4096).astype(np.float32) * np.float32(1e3)
+    mx = float(np.abs(x).max())
+    s = np.ldexp(1.0, np.frexp(mx)[1] - 14)
+    hi = (x / np.float32(s)).astype(np.float16)
+    assert np.isfinite(hi).all() and np.abs(hi.astype(np.float64)).max() < 2 ** 14
+    a = np.float64(4096)
+    prod = hi.astype(np.float64) * a
+    assert np.array_equal(prod.astype(np.float32).astype(np.float64), prod)
