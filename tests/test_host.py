@@ -150,3 +150,31 @@ def test_model_file_round_trip(lrs, tmp_path):
                 pb = getattr(mf.desc().contents.layers[i], n)
                 assert np.array_equal(np.ctypeslib.as_array((ctypes.c_float * width).from_address(pa)),
                                       np.ctypeslib.as_array((ctypes.c_float * width).from_address(pb)))
+
+
+def _c_param_counts():
+    """name -> number of parameters of every lrs_* function in include/*.h."""
+    counts = {}
+    for h in ("llamars.h", "llamars_synth.h", "llamars_gguf.h", "llamars_sample.h",
+              "llamars_safetensors.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for name, params in re.findall(r"\b(lrs_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+            p = params.strip()
+            counts[name] = 0 if p in ("", "void") else p.count(",") + 1
+    return counts
+
+
+def test_integration_rust_bindings_match_the_headers():
+    """The Rust `extern "C"` block a maintainer adds to the reference
+     binds functions the headers declare, with the same
+    number of parameters."""
+    md = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    decls = re.findall(r"pub fn (lrs_[a-z0-9_]+)\s*\(([^;]*?)\)\s*(?:->[^;]*)?;", md, flags=re.S)
+    assert len(decls) >= 15
+    c = _c_param_counts()
+    for name, params in decls:
+        params = re.sub(r"/\*.*?\*/", "", params, flags=re.S)
+        n = 0 if not params.strip() else params.count(",") + 1
+        assert name in c, f"{name} is bound in INTEGRATION.md but not declared"
+        assert n == c[name], f"{name}: {n} parameters in INTEGRATION.md, {c[name]} in the header"
