@@ -259,7 +259,7 @@ EXPORTED_SYMBOLS = (
 
 def _check(code: int) -> None:
     if code != 0:
-        raise LrsError(code, (_lib.lrs_last_error() or b"").decode())
+        raise LrsError(code, (_lib.lrs_last_error() or b"").decode(errors="replace"))
 
 
 def _fptr(a: np.ndarray):
@@ -540,8 +540,11 @@ class SynthModel:
             pass
 
     def desc(self):
-        """Pointer to the lrs_model_desc (host views stay valid while this object lives)."""
-        return _lib.lrs_synth_model_desc(self._h)
+        """Pointer to the lrs_model_desc (host views stay valid while this object
+        lives; the pointer keeps it alive)."""
+        p = _lib.lrs_synth_model_desc(self._h)
+        p._owner = self
+        return p
 
     def tensor(self, which: str, layer: Optional[int] = None) -> QuantTensor:
         """A weight as a QuantTensor view: 'embed', 'lm_head' or a layer projection name."""
@@ -662,7 +665,9 @@ class ModelFile:
         self._desc.layers = C.cast(self._layers, C.POINTER(_LayerDesc))
 
     def desc(self):
-        return C.pointer(self._desc)
+        p = C.pointer(self._desc)
+        p._owner = self  # the views stay valid while the pointer lives
+        return p
 
 
 class CudaQwen2Model:
@@ -868,6 +873,7 @@ class GgufFile:
         """The model description (valid while this object lives)."""
         out = C.POINTER(_ModelDesc)()
         _check(_lib.lrs_gguf_qwen2_desc(self._h, int(recipe), C.byref(out)))
+        out._owner = self
         return out
 
 
@@ -1004,6 +1010,7 @@ class SafetensorsFile:
         """The model description (valid while this object lives)."""
         out = C.POINTER(_ModelDesc)()
         _check(_lib.lrs_st_qwen2_desc(self._h, int(recipe), C.byref(out)))
+        out._owner = self
         return out
 
 
@@ -1019,7 +1026,9 @@ class LoadedModel:
         self._desc = d
 
     def desc(self):
-        return self._desc
+        p = C.pointer(self._desc.contents)
+        p._owner = self  # the description stays valid while the pointer lives
+        return p
 
     def close(self):
         if self._h:

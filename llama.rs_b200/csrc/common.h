@@ -2,6 +2,8 @@
 #pragma once
 #include <cstdint>
 #include <cstring>
+#include <exception>
+#include <new>
 #include <string>
 
 #include "../../include/llamars.h"
@@ -11,6 +13,22 @@ namespace lrs {
 // Sets the thread's last-error message and returns `code`.
 int32_t fail(int32_t code, const std::string& msg);
 void clear_error();
+
+// Runs an entry point's body so that no C++ exception crosses the C ABI: a
+// failed host allocation (a corrupt file asking for too much) is
+// LRS_ERR_OOM, any other exception LRS_ERR_INVALID.
+template <class F>
+int32_t guarded(F&& body) {
+  try {
+    return body();
+  } catch (const std::bad_alloc&) {
+    return fail(LRS_ERR_OOM, "out of host memory");
+  } catch (const std::exception& e) {
+    return fail(LRS_ERR_INVALID, e.what());
+  } catch (...) {
+    return fail(LRS_ERR_INVALID, "unexpected host error");
+  }
+}
 
 // QuantType::block_size / type_size (src/quant.rs:46-67).
 inline bool type_geometry(uint32_t t, uint32_t* bv, uint32_t* bb) {

@@ -62,38 +62,6 @@ std::string unsupported_type(uint32_t t) {
          "; supported: F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K";
 }
 
-// Strict UTF-8 check (Rust's str::from_utf8).
-bool valid_utf8(const uint8_t* p, size_t n) {
-  size_t i = 0;
-  while (i < n) {
-    const uint8_t c = p[i];
-    size_t len;
-    uint32_t cp;
-    if (c < 0x80) {
-      i++;
-      continue;
-    } else if ((c & 0xE0) == 0xC0) {
-      len = 2, cp = c & 0x1F;
-    } else if ((c & 0xF0) == 0xE0) {
-      len = 3, cp = c & 0x0F;
-    } else if ((c & 0xF8) == 0xF0) {
-      len = 4, cp = c & 0x07;
-    } else {
-      return false;
-    }
-    if (i + len > n) return false;
-    for (size_t k = 1; k < len; k++) {
-      if ((p[i + k] & 0xC0) != 0x80) return false;
-      cp = (cp << 6) | (p[i + k] & 0x3F);
-    }
-    if ((len == 2 && cp < 0x80) || (len == 3 && cp < 0x800) || (len == 4 && cp < 0x10000) ||
-        cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF))
-      return false;
-    i += len;
-  }
-  return true;
-}
-
 // Reader (src/gguf.rs:238-330): little-endian fields with bounds checks.
 struct Reader {
   const uint8_t* d;
@@ -124,7 +92,7 @@ struct Reader {
     }
     const uint8_t* p;
     if (!take((size_t)len, &p)) return false;
-    if (!valid_utf8(p, (size_t)len)) {
+    if (!lrs::valid_utf8(p, (size_t)len)) {
       err = fail(LRS_ERR_INVALID, "invalid UTF-8 in GGUF string");
       return false;
     }
@@ -311,7 +279,7 @@ std::string shape_str(const lrs_tensor_desc& d, bool one_d) {
 
 extern "C" {
 
-lrs_status lrs_gguf_open(const char* path, lrs_gguf** out) {
+static lrs_status lrs_gguf_open_body(const char* path, lrs_gguf** out) {
   if (!path || !out) return fail(LRS_ERR_INVALID, "null argument");
   auto g = std::make_unique<lrs_gguf>();
   g->fd = open(path, O_RDONLY);
@@ -364,7 +332,7 @@ lrs_status lrs_gguf_tensor(const lrs_gguf* g, const char* name, lrs_tensor_desc*
   return tensor_desc(g, name, out, nullptr);
 }
 
-lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) {
+static lrs_status lrs_gguf_qwen2_desc_body(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) {
   if (!g || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (recipe > LRS_RECIPE_Q4KM) return fail(LRS_ERR_INVALID, "unknown load quantization");
   const char* arch;
@@ -450,10 +418,13 @@ lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_des
   if ((rc = matrix("token_embd.weight", c.vocab_size, hidden, &d.embed_tokens)) ||
       (rc = vector("output_norm.weight", hidden, &d.final_norm)))
     return rc;
-  g->layers.assign(layers, lrs_layer_desc{});
+  // one layer at a time: a corrupt block count fails at its first missing
+  // tensor (the reference's error) instead of allocating for it up front
+  g->layers.clear();
   for (uint64_t i = 0; i < layers; i++) {
     const std::string p = "blk." + std::to_string(i);
-    lrs_layer_desc& L = g->layers[i];
+    g->layers.push_back(lrs_layer_desc{});
+    lrs_layer_desc& L = g->layers.back();
     if ((rc = vector(p + ".attn_norm.weight", hidden, &L.input_layernorm)) ||
         (rc = matrix(p + ".attn_q.weight", hidden, hidden, &L.q_proj)) ||
         (rc = bias(p + ".attn_q.bias", hidden, &L.q_bias)) ||
@@ -477,6 +448,14 @@ lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_des
   d.layers = g->layers.data();
   *out = &d;
   return LRS_OK;
+}
+
+lrs_status lrs_gguf_open(const char* path, lrs_gguf** out) {
+  return lrs::guarded([&] { return lrs_gguf_open_body(path, out); });
+}
+
+lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) {
+  return lrs::guarded([&] { return lrs_gguf_qwen2_desc_body(g, recipe, out); });
 }
 
 }  // extern "C"

@@ -105,4 +105,36 @@ inline int32_t maybe_quantize_desc(uint32_t recipe, const std::string& name, siz
   return LRS_OK;
 }
 
+// Strict UTF-8 check (Rust's str::from_utf8).
+inline bool valid_utf8(const uint8_t* p, size_t n) {
+  size_t i = 0;
+  while (i < n) {
+    const uint8_t c = p[i];
+    size_t len;
+    uint32_t cp;
+    if (c < 0x80) {
+      i++;
+      continue;
+    } else if ((c & 0xE0) == 0xC0) {
+      len = 2, cp = c & 0x1F;
+    } else if ((c & 0xF0) == 0xE0) {
+      len = 3, cp = c & 0x0F;
+    } else if ((c & 0xF8) == 0xF0) {
+      len = 4, cp = c & 0x07;
+    } else {
+      return false;
+    }
+    if (i + len > n) return false;
+    for (size_t k = 1; k < len; k++) {
+      if ((p[i + k] & 0xC0) != 0x80) return false;
+      cp = (cp << 6) | (p[i + k] & 0x3F);
+    }
+    if ((len == 2 && cp < 0x80) || (len == 3 && cp < 0x800) || (len == 4 && cp < 0x10000) ||
+        cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF))
+      return false;
+    i += len;
+  }
+  return true;
+}
+
 }  // namespace lrs

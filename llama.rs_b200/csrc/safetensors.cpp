@@ -135,6 +135,9 @@ int32_t parse_file(lrs_safetensors* st, int fi, std::map<std::string, StTensor>*
   if (n > m.size - 8) return bad("invalid header length");
   const char* h = reinterpret_cast<const char*>(m.map + 8);
   if (n == 0 || h[0] != '{') return bad("invalid header start");
+  // the header is a str (safetensors' from_utf8 before the JSON parse)
+  if (!lrs::valid_utf8(reinterpret_cast<const uint8_t*>(h), (size_t)n))
+    return bad("invalid header: not UTF-8");
   JValue root;
   std::string err;
   if (!lrs::JsonParser(h, n).parse(&root, &err)) return bad("invalid header: " + err);
@@ -279,7 +282,7 @@ int32_t parse_config(const std::string& text, lrs_config* c) {
 
 extern "C" {
 
-lrs_status lrs_st_open(const char* model_dir, lrs_safetensors** out) {
+static lrs_status lrs_st_open_body(const char* model_dir, lrs_safetensors** out) {
   if (!model_dir || !out) return fail(LRS_ERR_INVALID, "null argument");
   *out = nullptr;
   auto st = std::make_unique<lrs_safetensors>();
@@ -370,13 +373,16 @@ lrs_status lrs_st_tensor(const lrs_safetensors* st, const char* name_c, lrs_tens
   return LRS_OK;
 }
 
-lrs_status lrs_st_qwen2_desc(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) {
+static lrs_status lrs_st_qwen2_desc_body(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) {
   if (!st || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (recipe > LRS_RECIPE_Q4KM) return fail(LRS_ERR_INVALID, "unknown load quantization");
   // SafetensorsLoader::load, src/loader.rs:83-100
   const std::string config_path = join(st->dir, "config.json");
   std::string text;
-  if (!read_text(config_path, &text)) return fail(LRS_ERR_INVALID, "failed to read " + config_path);
+  // fs::read_to_string: unreadable or not UTF-8 is a read failure
+  if (!read_text(config_path, &text) ||
+      !lrs::valid_utf8(reinterpret_cast<const uint8_t*>(text.data()), text.size()))
+    return fail(LRS_ERR_INVALID, "failed to read " + config_path);
   {
     JValue root;
     std::string err;
@@ -434,10 +440,13 @@ lrs_status lrs_st_qwen2_desc(lrs_safetensors* st, uint32_t recipe, const lrs_mod
   if ((rc = matrix("model.embed_tokens.weight", c.vocab_size, hidden, &d.embed_tokens)) ||
       (rc = vector("model.norm.weight", hidden, &d.final_norm)))
     return rc;
-  st->layers.assign(c.num_hidden_layers, lrs_layer_desc{});
+  // one layer at a time: a corrupt layer count fails at its first missing
+  // tensor (the reference's error) instead of allocating for it up front
+  st->layers.clear();
   for (uint32_t i = 0; i < c.num_hidden_layers; i++) {
     const std::string p = "model.layers." + std::to_string(i);
-    lrs_layer_desc& L = st->layers[i];
+    st->layers.push_back(lrs_layer_desc{});
+    lrs_layer_desc& L = st->layers.back();
     if ((rc = vector(p + ".input_layernorm.weight", hidden, &L.input_layernorm)) ||
         (rc = vector(p + ".post_attention_layernorm.weight", hidden, &L.post_attention_layernorm)) ||
         (rc = matrix(p + ".self_attn.q_proj.weight", hidden, hidden, &L.q_proj)) ||
@@ -476,8 +485,8 @@ struct lrs_loaded {
 
 extern "C" {
 
-lrs_status lrs_model_load(const char* path_c, uint32_t recipe, lrs_loaded** out,
-                          const lrs_model_desc** desc) {
+static lrs_status lrs_model_load_body(const char* path_c, uint32_t recipe, lrs_loaded** out,
+                                      const lrs_model_desc** desc) {
   if (!path_c || !out || !desc) return fail(LRS_ERR_INVALID, "null argument");
   *out = nullptr;
   const std::string path = path_c;
@@ -517,5 +526,18 @@ lrs_status lrs_model_load(const char* path_c, uint32_t recipe, lrs_loaded** out,
 }
 
 void lrs_loaded_close(lrs_loaded* l) { delete l; }
+
+lrs_status lrs_st_open(const char* model_dir, lrs_safetensors** out) {
+  return lrs::guarded([&] { return lrs_st_open_body(model_dir, out); });
+}
+
+lrs_status lrs_st_qwen2_desc(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) {
+  return lrs::guarded([&] { return lrs_st_qwen2_desc_body(st, recipe, out); });
+}
+
+lrs_status lrs_model_load(const char* path_c, uint32_t recipe, lrs_loaded** out,
+                          const lrs_model_desc** desc) {
+  return lrs::guarded([&] { return lrs_model_load_body(path_c, recipe, out, desc); });
+}
 
 }  // extern "C"
