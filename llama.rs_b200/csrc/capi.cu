@@ -194,7 +194,7 @@ lrs_status lrs_type_geometry(uint32_t t, uint32_t* bv, uint32_t* bb) {
   return LRS_OK;
 }
 
-lrs_status lrs_backend_create(int device, lrs_backend** out) {
+lrs_status lrs_backend_create(int device, lrs_backend** out) try {
   if (!out) return fail(LRS_ERR_INVALID, "null out");
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
@@ -217,6 +217,8 @@ lrs_status lrs_backend_create(int device, lrs_backend** out) {
   cudaMemset(be->d_err, 0, sizeof(int));
   *out = be;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 void lrs_backend_destroy(lrs_backend* be) {
@@ -236,15 +238,17 @@ const char* lrs_backend_name(const lrs_backend*) { return "cuda-sm100a"; }
 size_t lrs_backend_threads(const lrs_backend* be) { return be ? (size_t)be->sms : 0; }
 void* lrs_backend_stream(lrs_backend* be) { return be ? (void*)be->stream : nullptr; }
 
-lrs_status lrs_backend_synchronize(lrs_backend* be) {
+lrs_status lrs_backend_synchronize(lrs_backend* be) try {
   if (!be) return fail(LRS_ERR_INVALID, "null backend");
   LRS_CUDA(cudaSetDevice(be->device));
   LRS_CUDA(cudaStreamSynchronize(be->stream));
   return check_device_error(be);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_tensor_upload(lrs_backend* be, const void* data, size_t nbytes, size_t rows,
-                             size_t cols, uint32_t type, lrs_tensor** out) {
+                             size_t cols, uint32_t type, lrs_tensor** out) try {
   if (!be || !data || !out) return fail(LRS_ERR_INVALID, "null argument");
   LRS_CUDA(cudaSetDevice(be->device));
   auto* t = new lrs_tensor();
@@ -256,6 +260,8 @@ lrs_status lrs_tensor_upload(lrs_backend* be, const void* data, size_t nbytes, s
   }
   *out = t;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 void lrs_tensor_free(lrs_tensor* t) {
@@ -268,7 +274,7 @@ void lrs_tensor_free(lrs_tensor* t) {
 const void* lrs_tensor_device_ptr(const lrs_tensor* t) { return t ? t->t.d : nullptr; }
 
 lrs_status lrs_dequantize_rows(lrs_backend* be, const lrs_tensor* t, size_t row0, size_t nrows,
-                               float* out) {
+                               float* out) try {
   if (!be || !t || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (row0 + nrows > (size_t)t->t.rows) return fail(LRS_ERR_INVALID, "row range out of bounds");
   if (nrows == 0) return LRS_OK;
@@ -281,10 +287,12 @@ lrs_status lrs_dequantize_rows(lrs_backend* be, const lrs_tensor* t, size_t row0
   LRS_CUDA(cudaMemcpyAsync(out, be->d_y, n * 4, cudaMemcpyDeviceToHost, be->stream));
   LRS_CUDA(cudaStreamSynchronize(be->stream));
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* d_in,
-                             size_t batch, float* d_out, void* stream) {
+                             size_t batch, float* d_out, void* stream) try {
   if (!be || !w || !d_in || !d_out) return fail(LRS_ERR_INVALID, "null argument");
   if (batch < 1 || batch > 64) return fail(LRS_ERR_INVALID, "batch must be in 1..=64");
   GemvMat m = mat_of(w->t, d_out, w->t.rows);
@@ -311,10 +319,12 @@ lrs_status lrs_matvec_device(lrs_backend* be, const lrs_tensor* w, const float* 
   cudaStream_t st = stream ? (cudaStream_t)stream : be->stream;
   LRS_CUDA(gemv_launch(p, st, be->sms, false));
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_matvec_batched(lrs_backend* be, const lrs_tensor* w, const float* in, size_t batch,
-                              size_t n_in, float* out, size_t n_out) {
+                              size_t n_in, float* out, size_t n_out) try {
   if (!be || !w || !in || !out) return fail(LRS_ERR_INVALID, "null argument");
   // QuantTensor::validate_matvec, src/quant.rs:303-318
   if (n_in != (size_t)w->t.cols)
@@ -335,11 +345,15 @@ lrs_status lrs_matvec_batched(lrs_backend* be, const lrs_tensor* w, const float*
   LRS_CUDA(cudaMemcpyAsync(out, be->d_y, batch * n_out * 4, cudaMemcpyDeviceToHost, be->stream));
   LRS_CUDA(cudaStreamSynchronize(be->stream));
   return check_device_error(be);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_matvec(lrs_backend* be, const lrs_tensor* w, const float* in, size_t n_in,
-                      float* out, size_t n_out) {
+                      float* out, size_t n_out) try {
   return lrs_matvec_batched(be, w, in, 1, n_in, out, n_out);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 }  // extern "C"
@@ -1292,11 +1306,13 @@ int32_t create_model(lrs_backend* be, const lrs_model_desc* d, const lrs_model_o
 extern "C" {
 
 lrs_status lrs_model_create(lrs_backend* be, const lrs_model_desc* d,
-                            const lrs_model_options* options, lrs_model** out) {
+                            const lrs_model_options* options, lrs_model** out) try {
   return create_model(be, d, options, 0, 1, nullptr, out);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-lrs_status lrs_tp_unique_id(uint8_t* id_out) {
+lrs_status lrs_tp_unique_id(uint8_t* id_out) try {
   if (!id_out) return fail(LRS_ERR_INVALID, "null argument");
   const NcclApi& n = nccl();
   if (!n.ok) return fail(LRS_ERR_UNSUPPORTED, n.err);
@@ -1305,11 +1321,13 @@ lrs_status lrs_tp_unique_id(uint8_t* id_out) {
   LRS_NCCL(n.GetUniqueId(&id));
   memcpy(id_out, &id, sizeof id);
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_create_tp(lrs_backend* be, const lrs_model_desc* d,
                                const lrs_model_options* options, uint32_t rank, uint32_t world,
-                               const uint8_t* id, lrs_model** out) {
+                               const uint8_t* id, lrs_model** out) try {
   if (!be || !d || !id || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (world < 1 || rank >= world) return fail(LRS_ERR_INVALID, "tensor-parallel rank out of range");
   if (world == 1) return create_model(be, d, options, 0, 1, nullptr, out);
@@ -1323,6 +1341,8 @@ lrs_status lrs_model_create_tp(lrs_backend* be, const lrs_model_desc* d,
   int32_t rc = create_model(be, d, options, (int)rank, (int)world, comm, out);
   if (rc) n.CommDestroy(comm);
   return rc;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 uint32_t lrs_model_tp_world(const lrs_model* m) { return m ? (uint32_t)m->tp_world : 0; }
@@ -1364,7 +1384,7 @@ void lrs_model_destroy(lrs_model* m) {
 
 uint64_t lrs_model_weight_bytes(const lrs_model* m) { return m ? m->weight_bytes : 0; }
 
-lrs_status lrs_model_weights_digest(lrs_model* m, uint64_t* out) {
+lrs_status lrs_model_weights_digest(lrs_model* m, uint64_t* out) try {
   if (!m || !out) return fail(LRS_ERR_INVALID, "null argument");
   LRS_CUDA(cudaSetDevice(m->be->device));
   LRS_CUDA(cudaStreamSynchronize(m->be->stream));
@@ -1384,9 +1404,11 @@ lrs_status lrs_model_weights_digest(lrs_model* m, uint64_t* out) {
   if ((rc = eat(m->lm))) return rc;
   *out = h;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-lrs_status lrs_model_reset(lrs_model* m, uint32_t seq) {
+lrs_status lrs_model_reset(lrs_model* m, uint32_t seq) try {
   if (!m) return fail(LRS_ERR_INVALID, "null model");
   if (seq >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
   // KVCache::reset is a no-op in the reference (positions are overwritten
@@ -1394,17 +1416,21 @@ lrs_status lrs_model_reset(lrs_model* m, uint32_t seq) {
   for (int pg : m->seq_pages[seq]) m->free_pages.push_back(pg);
   m->seq_pages[seq].clear();
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_forward_token(lrs_model* m, uint32_t seq, uint32_t token, uint32_t pos,
-                                   int logits_mode, float* logits_out, uint32_t* argmax_out) {
+                                   int logits_mode, float* logits_out, uint32_t* argmax_out) try {
   if (!m) return fail(LRS_ERR_INVALID, "null model");
   return lrs_model_prefill(m, seq, &token, 1, pos, logits_mode == LRS_LOGITS_COMPUTE ? logits_out : nullptr,
                            logits_mode == LRS_LOGITS_COMPUTE ? argmax_out : nullptr) ;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens, size_t n,
-                             uint32_t start_pos, float* logits_out, uint32_t* argmax_out) {
+                             uint32_t start_pos, float* logits_out, uint32_t* argmax_out) try {
   if (!m || !tokens) return fail(LRS_ERR_INVALID, "null argument");
   if (n == 0) return fail(LRS_ERR_INVALID, "prefill requires at least one token");
   if (seq >= m->opt.max_sequences) return fail(LRS_ERR_INVALID, "sequence slot out of range");
@@ -1442,11 +1468,13 @@ lrs_status lrs_model_prefill(lrs_model* m, uint32_t seq, const uint32_t* tokens,
     if ((rc = read_argmax(m, item, argmax_out))) return rc;
   }
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_forward_sample(lrs_model* m, uint32_t seq, uint32_t token, uint32_t pos,
                                     const lrs_sampler* params, const uint32_t* recent,
-                                    size_t n_recent, float u, uint32_t* next_out) {
+                                    size_t n_recent, float u, uint32_t* next_out) try {
   // InferenceEngine::forward_step, src/engine.rs:96-106: forward_token with
   // LogitsMode::Compute, then sample_current_logits on the device logits
   if (!m || !next_out || (n_recent && !recent)) return fail(LRS_ERR_INVALID, "null argument");
@@ -1471,11 +1499,13 @@ lrs_status lrs_model_forward_sample(lrs_model* m, uint32_t seq, uint32_t token, 
   LRS_CUDA(cudaMemcpyAsync(next_out, d_out, 4, cudaMemcpyDeviceToHost, m->be->stream));
   LRS_CUDA(cudaStreamSynchronize(m->be->stream));
   return check_device_error(m->be);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
                                     const uint32_t* first_tokens, const uint32_t* start_pos,
-                                    size_t n_steps) {
+                                    size_t n_steps) try {
   if (!m || !seqs || !first_tokens || !start_pos) return fail(LRS_ERR_INVALID, "null argument");
   if (n_seqs == 0 || n_seqs > (size_t)m->max_items)
     return fail(LRS_ERR_INVALID, "n_seqs out of range");
@@ -1560,11 +1590,13 @@ lrs_status lrs_model_decode_enqueue(lrs_model* m, size_t n_seqs, const uint32_t*
       if ((rc = step1 ? enqueue_step1(m) : enqueue_step(m, B, -1, false, true, cap_steps))) return rc;
   }
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 uint32_t lrs_model_step_kernels(const lrs_model* m) { return m ? m->last_step_kernels : 0; }
 
-lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, uint32_t* out) {
+lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, uint32_t* out) try {
   if (!m || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (n_seqs * n_steps > m->tokens_out_cap) return fail(LRS_ERR_INVALID, "token range out of bounds");
   LRS_CUDA(cudaSetDevice(m->be->device));
@@ -1572,11 +1604,13 @@ lrs_status lrs_model_read_tokens(lrs_model* m, size_t n_seqs, size_t n_steps, ui
                            m->be->stream));
   LRS_CUDA(cudaStreamSynchronize(m->be->stream));
   return check_device_error(m->be);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
                                   const uint32_t* tokens, const uint32_t* pos, float* gemv_ms,
-                                  uint32_t* gemv_launches, float* step_ms, float* attn_ms) {
+                                  uint32_t* gemv_launches, float* step_ms, float* attn_ms) try {
   if (!m || !seqs || !tokens || !pos) return fail(LRS_ERR_INVALID, "null argument");
   if (n_seqs == 0 || n_seqs > (size_t)m->max_items) return fail(LRS_ERR_INVALID, "n_seqs out of range");
   LRS_CUDA(cudaSetDevice(m->be->device));
@@ -1633,15 +1667,19 @@ lrs_status lrs_model_profile_step(lrs_model* m, size_t n_seqs, const uint32_t* s
   if (gemv_launches) *gemv_launches = (uint32_t)(ev.size() / 2);
   if (step_ms) *step_ms = step;
   return check_device_error(m->be);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 lrs_status lrs_model_decode_greedy(lrs_model* m, size_t n_seqs, const uint32_t* seqs,
                                    const uint32_t* first_tokens, const uint32_t* start_pos,
-                                   size_t n_steps, uint32_t* tokens_out) {
+                                   size_t n_steps, uint32_t* tokens_out) try {
   int32_t rc = lrs_model_decode_enqueue(m, n_seqs, seqs, first_tokens, start_pos, n_steps);
   if (rc) return rc;
   if (!tokens_out || n_steps == 0) return lrs_backend_synchronize(m->be);
   return lrs_model_read_tokens(m, n_seqs, n_steps, tokens_out);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 }  // extern "C"

@@ -14,13 +14,13 @@ namespace lrs {
 int32_t fail(int32_t code, const std::string& msg);
 void clear_error();
 
-// Runs an entry point's body so that no C++ exception crosses the C ABI: a
-// failed host allocation (a corrupt file asking for too much) is
+// The status of the exception being handled, for the function-try-blocks of
+// the C entry points: no C++ exception crosses the C ABI.  A failed host
+// allocation (a corrupt file or an argument asking for too much) is
 // LRS_ERR_OOM, any other exception LRS_ERR_INVALID.
-template <class F>
-int32_t guarded(F&& body) {
+inline int32_t status_of_current_exception() {
   try {
-    return body();
+    throw;
   } catch (const std::bad_alloc&) {
     return fail(LRS_ERR_OOM, "out of host memory");
   } catch (const std::exception& e) {

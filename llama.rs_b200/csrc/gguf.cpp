@@ -279,7 +279,7 @@ std::string shape_str(const lrs_tensor_desc& d, bool one_d) {
 
 extern "C" {
 
-static lrs_status lrs_gguf_open_body(const char* path, lrs_gguf** out) {
+lrs_status lrs_gguf_open(const char* path, lrs_gguf** out) try {
   if (!path || !out) return fail(LRS_ERR_INVALID, "null argument");
   auto g = std::make_unique<lrs_gguf>();
   g->fd = open(path, O_RDONLY);
@@ -296,43 +296,53 @@ static lrs_status lrs_gguf_open_body(const char* path, lrs_gguf** out) {
   if (rc) return rc;
   *out = g.release();
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 void lrs_gguf_close(lrs_gguf* g) { delete g; }
 uint32_t lrs_gguf_version(const lrs_gguf* g) { return g ? g->version : 0; }
 size_t lrs_gguf_tensor_count(const lrs_gguf* g) { return g ? g->tensors.size() : 0; }
 
-lrs_status lrs_gguf_metadata_u64(const lrs_gguf* g, const char* key, uint64_t* out) {
+lrs_status lrs_gguf_metadata_u64(const lrs_gguf* g, const char* key, uint64_t* out) try {
   if (!g || !key || !out) return fail(LRS_ERR_INVALID, "null argument");
   auto it = g->meta.find(key);
   if (it == g->meta.end() || !it->second.as_u64(out))
     return fail(LRS_ERR_INVALID, std::string("missing or non-integer GGUF metadata ") + key);
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-lrs_status lrs_gguf_metadata_f32(const lrs_gguf* g, const char* key, float* out) {
+lrs_status lrs_gguf_metadata_f32(const lrs_gguf* g, const char* key, float* out) try {
   if (!g || !key || !out) return fail(LRS_ERR_INVALID, "null argument");
   auto it = g->meta.find(key);
   if (it == g->meta.end() || !it->second.as_f32(out))
     return fail(LRS_ERR_INVALID, std::string("missing or non-numeric GGUF metadata ") + key);
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-lrs_status lrs_gguf_metadata_str(const lrs_gguf* g, const char* key, const char** out) {
+lrs_status lrs_gguf_metadata_str(const lrs_gguf* g, const char* key, const char** out) try {
   if (!g || !key || !out) return fail(LRS_ERR_INVALID, "null argument");
   auto it = g->meta.find(key);
   if (it == g->meta.end() || it->second.kind != Meta::STR)
     return fail(LRS_ERR_INVALID, std::string("missing or non-string GGUF metadata ") + key);
   *out = it->second.s.c_str();
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-lrs_status lrs_gguf_tensor(const lrs_gguf* g, const char* name, lrs_tensor_desc* out) {
+lrs_status lrs_gguf_tensor(const lrs_gguf* g, const char* name, lrs_tensor_desc* out) try {
   if (!g || !name || !out) return fail(LRS_ERR_INVALID, "null argument");
   return tensor_desc(g, name, out, nullptr);
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-static lrs_status lrs_gguf_qwen2_desc_body(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) {
+lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) try {
   if (!g || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (recipe > LRS_RECIPE_Q4KM) return fail(LRS_ERR_INVALID, "unknown load quantization");
   const char* arch;
@@ -448,14 +458,8 @@ static lrs_status lrs_gguf_qwen2_desc_body(lrs_gguf* g, uint32_t recipe, const l
   d.layers = g->layers.data();
   *out = &d;
   return LRS_OK;
-}
-
-lrs_status lrs_gguf_open(const char* path, lrs_gguf** out) {
-  return lrs::guarded([&] { return lrs_gguf_open_body(path, out); });
-}
-
-lrs_status lrs_gguf_qwen2_desc(lrs_gguf* g, uint32_t recipe, const lrs_model_desc** out) {
-  return lrs::guarded([&] { return lrs_gguf_qwen2_desc_body(g, recipe, out); });
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 }  // extern "C"

@@ -75,7 +75,7 @@ int32_t scratch_for(int device, unsigned char** out) {
   } while (0)
 
 extern "C" lrs_status lrs_matvec_noalloc(lrs_backend* be, const lrs_tensor* w, const float* in,
-                                         size_t n_in, float* out, size_t n_out) {
+                                         size_t n_in, float* out, size_t n_out) try {
   if (!be || !w || !in || !out) return lrs::fail(LRS_ERR_INVALID, "null argument");
   if (n_in != (size_t)w->t.cols)
     return lrs::fail(LRS_ERR_INVALID, "matvec input mismatch: got " + std::to_string(n_in) +
@@ -118,4 +118,6 @@ extern "C" lrs_status lrs_matvec_noalloc(lrs_backend* be, const lrs_tensor* w, c
   NOALLOC_CUDA(cudaStreamSynchronize(st));
   if (herr) return lrs::fail(LRS_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up");
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }

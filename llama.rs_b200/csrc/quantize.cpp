@@ -51,7 +51,7 @@ size_t lrs_quantized_size(uint32_t t, size_t rows, size_t cols) {
 }
 
 lrs_status lrs_quantize_matrix(uint32_t t, const float* values, size_t rows, size_t cols,
-                               void* out, size_t out_cap, uint32_t* out_type, size_t* out_len) {
+                               void* out, size_t out_cap, uint32_t* out_type, size_t* out_len) try {
   uint32_t bv, bb;
   if (!type_geometry(t, &bv, &bb)) return fail(LRS_ERR_UNSUPPORTED, "unsupported GGML type");
   uint32_t e = effective_type(t, cols);
@@ -74,6 +74,8 @@ lrs_status lrs_quantize_matrix(uint32_t t, const float* values, size_t rows, siz
   if (out_type) *out_type = e;
   if (out_len) *out_len = need;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 }  // extern "C"

@@ -62,7 +62,7 @@ using namespace lrs;
 extern "C" lrs_status lrs_quantize_matrix_device(lrs_backend* be, uint32_t t, const float* d_values,
                                                  size_t rows, size_t cols, void* d_out,
                                                  size_t out_cap, uint32_t* out_type,
-                                                 size_t* out_len) {
+                                                 size_t* out_len) try {
   if (!be || !d_values || !d_out) return fail(LRS_ERR_INVALID, "null argument");
   uint32_t bv, bb;
   if (!type_geometry(t, &bv, &bb)) return fail(LRS_ERR_UNSUPPORTED, "unsupported GGML type");
@@ -82,4 +82,6 @@ extern "C" lrs_status lrs_quantize_matrix_device(lrs_backend* be, uint32_t t, co
   if (out_type) *out_type = e;
   if (out_len) *out_len = need;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }

@@ -282,7 +282,7 @@ int32_t parse_config(const std::string& text, lrs_config* c) {
 
 extern "C" {
 
-static lrs_status lrs_st_open_body(const char* model_dir, lrs_safetensors** out) {
+lrs_status lrs_st_open(const char* model_dir, lrs_safetensors** out) try {
   if (!model_dir || !out) return fail(LRS_ERR_INVALID, "null argument");
   *out = nullptr;
   auto st = std::make_unique<lrs_safetensors>();
@@ -335,12 +335,14 @@ static lrs_status lrs_st_open_body(const char* model_dir, lrs_safetensors** out)
       if (!st->tensors.count(kv.first)) st->unresolved[kv.first] = kv.second;
   *out = st.release();
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 void lrs_st_close(lrs_safetensors* st) { delete st; }
 size_t lrs_st_tensor_count(const lrs_safetensors* st) { return st ? st->tensors.size() : 0; }
 
-lrs_status lrs_st_tensor(const lrs_safetensors* st, const char* name_c, lrs_tensor_desc* out) {
+lrs_status lrs_st_tensor(const lrs_safetensors* st, const char* name_c, lrs_tensor_desc* out) try {
   if (!st || !name_c || !out) return fail(LRS_ERR_INVALID, "null argument");
   const std::string name = name_c;
   auto it = st->tensors.find(name);
@@ -371,9 +373,11 @@ lrs_status lrs_st_tensor(const lrs_safetensors* st, const char* name_c, lrs_tens
   out->cols = t.shape.empty() ? 1 : t.shape.back();
   out->ggml_type = ty;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
-static lrs_status lrs_st_qwen2_desc_body(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) {
+lrs_status lrs_st_qwen2_desc(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) try {
   if (!st || !out) return fail(LRS_ERR_INVALID, "null argument");
   if (recipe > LRS_RECIPE_Q4KM) return fail(LRS_ERR_INVALID, "unknown load quantization");
   // SafetensorsLoader::load, src/loader.rs:83-100
@@ -470,6 +474,8 @@ static lrs_status lrs_st_qwen2_desc_body(lrs_safetensors* st, uint32_t recipe, c
   d.layers = st->layers.data();
   *out = &d;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 }  // extern "C"
@@ -485,8 +491,8 @@ struct lrs_loaded {
 
 extern "C" {
 
-static lrs_status lrs_model_load_body(const char* path_c, uint32_t recipe, lrs_loaded** out,
-                                      const lrs_model_desc** desc) {
+lrs_status lrs_model_load(const char* path_c, uint32_t recipe, lrs_loaded** out,
+                          const lrs_model_desc** desc) try {
   if (!path_c || !out || !desc) return fail(LRS_ERR_INVALID, "null argument");
   *out = nullptr;
   const std::string path = path_c;
@@ -523,21 +529,10 @@ static lrs_status lrs_model_load_body(const char* path_c, uint32_t recipe, lrs_l
   if (rc) return rc;
   *out = l.release();
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 void lrs_loaded_close(lrs_loaded* l) { delete l; }
-
-lrs_status lrs_st_open(const char* model_dir, lrs_safetensors** out) {
-  return lrs::guarded([&] { return lrs_st_open_body(model_dir, out); });
-}
-
-lrs_status lrs_st_qwen2_desc(lrs_safetensors* st, uint32_t recipe, const lrs_model_desc** out) {
-  return lrs::guarded([&] { return lrs_st_qwen2_desc_body(st, recipe, out); });
-}
-
-lrs_status lrs_model_load(const char* path_c, uint32_t recipe, lrs_loaded** out,
-                          const lrs_model_desc** desc) {
-  return lrs::guarded([&] { return lrs_model_load_body(path_c, recipe, out, desc); });
-}
 
 }  // extern "C"

@@ -305,7 +305,7 @@ int32_t sample_buffers(lrs_backend* be, const uint32_t* recent, size_t n, uint32
 
 using namespace lrs;
 
-extern "C" lrs_status lrs_sampler_check(const lrs_sampler* p, size_t vocab) {
+extern "C" lrs_status lrs_sampler_check(const lrs_sampler* p, size_t vocab) try {
   // validate_sampling, src/engine.rs:327-339
   if (!p) return fail(LRS_ERR_INVALID, "null sampler parameters");
   if (!std::isfinite(p->temperature) || p->temperature < 0.0f)
@@ -323,11 +323,13 @@ extern "C" lrs_status lrs_sampler_check(const lrs_sampler* p, size_t vocab) {
                                          std::to_string(LRS_SAMPLE_MAX_TOP_K) +
                                          " (top_k = 0 and larger values use the host sampler)");
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 extern "C" lrs_status lrs_sample_logits(lrs_backend* be, const float* d_logits, size_t vocab,
                                         const lrs_sampler* p, const uint32_t* recent,
-                                        size_t n_recent, float u, uint32_t* token_out) {
+                                        size_t n_recent, float u, uint32_t* token_out) try {
   if (!be || !d_logits || !token_out || (n_recent && !recent))
     return fail(LRS_ERR_INVALID, "null argument");
   int32_t rc = lrs_sampler_check(p, vocab);
@@ -342,4 +344,6 @@ extern "C" lrs_status lrs_sample_logits(lrs_backend* be, const float* d_logits, 
   if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
   if (e != cudaSuccess) return fail(LRS_ERR_CUDA, cudaGetErrorString(e));
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }

@@ -135,7 +135,7 @@ void lrs_synth_fill(uint64_t seed, const char* name, float stddev, uint64_t offs
   NormalStream(seed, name).fill(stddev, offset, n, out);
 }
 
-lrs_status lrs_synth_model_create(const lrs_synth_spec* spec, lrs_synth_model** out) {
+lrs_status lrs_synth_model_create(const lrs_synth_spec* spec, lrs_synth_model** out) try {
   if (!spec || !out) return fail(LRS_ERR_INVALID, "null argument");
   const lrs_config& c = spec->config;
   if (!c.hidden_size || !c.intermediate_size || !c.num_attention_heads ||
@@ -176,6 +176,8 @@ lrs_status lrs_synth_model_create(const lrs_synth_spec* spec, lrs_synth_model** 
     m->desc.lm_head = make_matrix(m, *spec, "lm_head.weight", c.vocab_size, h, threads);
   *out = m;
   return LRS_OK;
+} catch (...) {
+  return lrs::status_of_current_exception();
 }
 
 const lrs_model_desc* lrs_synth_model_desc(const lrs_synth_model* m) { return m ? &m->desc : nullptr; }
